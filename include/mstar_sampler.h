@@ -1,0 +1,159 @@
+/*
+ * mstar_sampler.h -- C ABI of the B200 batched token sampler.
+ *
+ * Plain pointers and sizes only; every pointer below is a DEVICE pointer on
+ * the current CUDA device unless stated otherwise.  All calls are
+ * asynchronous on `stream` (a cudaStream_t passed as void*), allocate
+ * nothing, never synchronise, and are therefore legal inside CUDA-graph
+ * capture.  Argument validation happens on the host before any launch; a
+ * non-zero return means nothing was launched.
+ *
+ * Reference interfaces these entry points replace (npuichigo/mstar-rs; the
+ * sampler itself lives in the external `mstar.utils.sampling` package):
+ *   mstar_sampler_step      <- CudaGraphableSampler.sample(rids, logits, apply_penalty=True)
+ *                              python/mstar_rs/models/orpheus.py:350, :496;
+ *                              python/mstar_rs/models/qwen3_omni.py:518
+ *                              (and the eager Sampler.sample, orpheus.py:517,
+ *                              qwen3_omni.py:483), plus the in-graph seen-mask
+ *                              update synced back at orpheus.py:426 and the
+ *                              offset_buf advance saved/restored at orpheus.py:353-359
+ *   mstar_sampler_tp_local  <- the vocab-parallel half of the TP sampler whose
+ *   mstar_sampler_tp_merge     tp_group keeps Thinker ranks in agreement
+ *                              (python/mstar_rs/models/qwen3_omni.py:401-404, :408, :431)
+ *   mstar_sampler_smem_bytes / mstar_sampler_cluster_size: launch planning
+ *                              behind SamplerBuffers.allocate
+ *                              (orpheus.py:101-103, qwen3_omni.py:431, :987-989)
+ */
+#ifndef MSTAR_SAMPLER_H_
+#define MSTAR_SAMPLER_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MSTAR_SAMPLER_ABI_VERSION 1
+
+/* logits dtypes */
+#define MSTAR_DTYPE_F32 0
+#define MSTAR_DTYPE_BF16 1
+
+/* flags */
+#define MSTAR_FLAG_UPDATE_HISTORY 0x1u /* append the sampled id to hist_ids/hist_len */
+#define MSTAR_FLAG_UPDATE_SEEN 0x2u    /* set the sampled id's bit in seen_bits */
+#define MSTAR_FLAG_ADVANCE_OFFSET 0x4u /* offset[slot] += 1 after the draw */
+#define MSTAR_FLAG_FORCE_GENERAL 0x8u  /* testing: take the multi-round selection path */
+
+/* per-row status bits written to out_status */
+#define MSTAR_STATUS_EMPTY 0x1u        /* no token had positive weight; id 0 returned */
+#define MSTAR_STATUS_GENERAL 0x2u      /* row took the multi-round selection path */
+#define MSTAR_STATUS_SPECIAL_OVERFLOW 0x4u /* more penalised/biased ids than the table holds */
+#define MSTAR_STATUS_TP_OVERFLOW 0x8u  /* TP: a shard's candidate set exceeded tp_cap */
+#define MSTAR_STATUS_TIMEOUT 0x10u     /* a bounded wait on a bulk copy gave up */
+
+/* return codes */
+#define MSTAR_OK 0
+#define MSTAR_ERR_INVALID 1
+#define MSTAR_ERR_UNSUPPORTED 2
+#define MSTAR_ERR_CUDA 3
+
+typedef struct mstar_sampler_params {
+  /* logits [B, ld], row r holds columns [0, V) of the vocabulary shard that
+   * starts at global id `vocab_offset` (0 without tensor parallelism). */
+  const void *logits;
+  int32_t dtype;
+  int32_t B;
+  int32_t V;
+  int32_t num_slots;         /* rows of every per-slot array below */
+  int64_t ld;                /* row stride in elements */
+  int64_t vocab_offset;
+  const int32_t *slot_idx;   /* [B] or NULL (row r uses slot r); <0 = padding row */
+
+  /* per-slot sampling parameters, [num_slots] each; NULL = default
+   * (temperature 1, top_k 0, top_p 1, min_p 0, rep 1, presence 0, frequency 0) */
+  const float *temperature;
+  const int32_t *top_k;
+  const float *top_p;
+  const float *min_p;
+  const float *rep_pen;
+  const float *pres_pen;
+  const float *freq_pen;
+
+  /* penalty input, at most one of:
+   *   token history  hist_ids [num_slots, H] (global ids, ring of the last H
+   *                  generated tokens) + hist_len [num_slots]
+   *   seen bitmask   seen_bits [num_slots, seen_words] (bit g&31 of word g>>5)
+   * seen_cap bounds the set bits per row the kernel accepts (0 = 2048). */
+  int32_t *hist_ids;
+  int32_t *hist_len;
+  int32_t H;
+  int32_t seen_cap;
+  uint32_t *seen_bits;
+  int64_t seen_words;
+
+  /* logit bias [num_slots, NB]; id < 0 marks an unused entry */
+  const int32_t *bias_ids;
+  const float *bias_vals;
+  int32_t NB;
+  int32_t pad0;
+
+  /* allowed-token bitmask [num_slots, allowed_words] or NULL (all allowed) */
+  const uint32_t *allowed_bits;
+  int64_t allowed_words;
+
+  /* randomness: uniforms [B] in [0,1) if non-NULL, else Philox4x32-10 keyed
+   * by seed[slot] at counter offset[slot] */
+  const float *uniforms;
+  const uint64_t *seed;
+  uint64_t *offset;
+
+  /* outputs */
+  int64_t *out_ids;          /* [B] global token ids (or NULL) */
+  int32_t *out_ids32;        /* [B] (or NULL) */
+  int32_t *out_status;       /* [B] (or NULL) */
+  /* debug / verification outputs, [B, V] each, or NULL */
+  float *out_x;              /* processed logits */
+  uint8_t *out_kept;         /* kept-set membership */
+  float *out_probs;          /* normalised probabilities over the kept set */
+
+  uint32_t flags;
+  int32_t cluster_size;      /* CTAs per row; 0 = automatic */
+} mstar_sampler_params_t;
+
+/* Library ABI version (MSTAR_SAMPLER_ABI_VERSION). */
+int mstar_sampler_abi_version(void);
+
+/* Human-readable text for the last host-side error in this thread. */
+const char *mstar_sampler_last_error(void);
+
+/* Dynamic shared memory per CTA and CTAs per row the step would use for
+ * these parameters (no launch). Returns MSTAR_OK or an error code. */
+int mstar_sampler_plan(const mstar_sampler_params_t *p, int32_t *cluster_size,
+                       int64_t *smem_bytes);
+
+/* One sampling step for B rows: logits -> token ids, with per-slot state
+ * (RNG offset, history / seen bits) advanced on the device. */
+int mstar_sampler_step(const mstar_sampler_params_t *p, void *stream);
+
+/* Tensor-parallel sampling over a vocabulary shard.
+ * tp_local: writes this shard's candidate record for every row into
+ *   send [B, rec_words] (uint32 words; rec_words = mstar_sampler_tp_record_words(tp_cap)).
+ * tp_merge: reads the all-gathered records recv [tp_world, B, rec_words] and
+ *   produces the same ids and state updates on every rank.  p->V / vocab_offset
+ *   describe this rank's shard; V_global is the full vocabulary. */
+int32_t mstar_sampler_tp_record_words(int32_t tp_cap);
+int mstar_sampler_tp_local(const mstar_sampler_params_t *p, int32_t tp_cap, uint32_t *send,
+                           void *stream);
+int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world,
+                           int64_t V_global, const uint32_t *recv, void *stream);
+
+/* The sampler's Philox4x32-10 uniform for (seed, offset), computed on the
+ * host; lets callers reproduce a draw without a device. */
+float mstar_sampler_philox_uniform(uint64_t seed, uint64_t offset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MSTAR_SAMPLER_H_ */

@@ -1,0 +1,1679 @@
+// B200 batched token sampler: logits [B, V] -> token ids [B].
+//
+// One thread-block cluster of S CTAs samples one row.  Each CTA owns a
+// contiguous slice of the row, pulls it into shared memory with 1-D bulk
+// copies (cp.async.bulk + mbarrier, one barrier per 16 KB chunk) and keeps it
+// resident for the whole step, so HBM is read exactly once:
+//
+//   setup     penalised / biased ids of the slice go into a small hash table
+//             (the "specials"); their final values are computed from global
+//             memory while the bulk copies are in flight.
+//   pass A    per chunk as it lands: disallowed ids -> -inf, specials -> NaN
+//             (they are handled from the special list), running max of the
+//             raw values (bf16x2 max / fmax).
+//   cluster   row max m = max over CTAs (DSMEM); every CTA runs the same
+//             32-ary search for x_A, the smallest value whose weight is
+//             positive and passes min_p, and for the raw threshold r_A with
+//             f(r_A) >= x_A (f = the temperature transform, monotone).
+//   pass C    vectors whose max is below r_A are skipped after one compare;
+//             survivors (x, id) are pushed into the leader CTA's tail buffer
+//             through DSMEM atomics.
+//   tail      the leader bucket-sorts the candidates by (x desc, id asc),
+//             computes the fixed-point weights and their exact u64 prefix
+//             sums, and resolves top_k / top_p / the inverse-CDF draw.
+//   general   rows whose candidate set exceeds the tail capacity run a
+//             leader-driven loop of histogram (count + mass) and compaction
+//             rounds over the still-resident slices until every boundary is
+//             pinned to a bin small enough to sort.
+//
+// Reference call sites this kernel serves: CudaGraphableSampler.sample in
+// python/mstar_rs/models/orpheus.py:350 and qwen3_omni.py:518 (batched,
+// in-graph), Sampler.sample in orpheus.py:517 / qwen3_omni.py:483 (eager).
+#include <cooperative_groups.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/mstar_sampler.h"
+#include "spec.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace mstar {
+
+constexpr int NT = 512;            // threads per CTA
+constexpr int NWARP = NT / 32;
+constexpr int TAIL_CAP = 2048;     // candidates the fast tail sorts
+constexpr int GCAP = 1024;         // candidates per locate round of the general path
+constexpr int NBIN = 1024;         // histogram bins per round
+constexpr int NBK = 1024;          // buckets of the tail sort
+constexpr int CHUNK_BYTES = 16384; // bulk-copy granule (one mbarrier each)
+constexpr int MAX_CHUNKS = 16;     // slice data <= 256 KB
+constexpr int MAX_ROUNDS = 96;     // bound on general-path rounds
+constexpr int WORK_BYTES_MIN = 40 * 1024;
+constexpr int FAST_SCRATCH = 48 * 1024;
+constexpr unsigned kWaitLimit = 1u << 24;
+
+struct __align__(8) Cand {
+  float x;
+  uint32_t gid;
+};
+
+// Launch plan computed on the host (see plan_launch).
+struct Plan {
+  int32_t S;
+  int32_t es;
+  int64_t slice;       // elements per CTA slice
+  int32_t data_bytes;  // slice data (>= FAST_SCRATCH: reused by the fast tail)
+  int32_t map_bytes;   // each of the two bitmaps
+  int32_t ht_cap;      // hash table slots (power of two)
+  int32_t spec_cap;    // special list entries
+  int32_t off_work, off_spec, off_tail;
+  int32_t smem_bytes;
+  int32_t mode;        // 0 = step, 1 = TP local
+  int32_t tp_cap, rec_words;
+};
+
+enum : int { OP_DONE = 0, OP_HIST = 1, OP_COMPACT = 2 };
+enum : int { TGT_L1 = 0, TGT_REF = 1 };
+
+struct Cmd {
+  int op, target;
+  uint64_t lo, hi;
+  int shift, nbins;
+};
+
+enum : int {
+  ST_START = 0,
+  ST_AFTER_L1,
+  ST_AFTER_PREFIX,
+  ST_LOC_BIN,
+  ST_LOC_AFTER_REF,
+  ST_LOC_AFTER_COMPACT,
+  ST_FINISH
+};
+enum : int { Q_COUNT = 0, Q_LASTLT = 1, Q_POINT = 2 };
+
+struct Planner {
+  int state;
+  int stage;      // 0 = A boundary, 1 = top-p boundary, 2 = draw
+  int qkind;
+  int level;      // 0 = L1 arrays, 1 = REF arrays
+  uint64_t lo, hi;
+  int shift, nbins;
+  uint64_t base_c, base_m;
+  uint64_t l1lo, l1hi;
+  int l1shift, l1nbins;
+  uint64_t tcount, tpoint;
+  double thr;
+  uint64_t cbase_c, cbase_m;  // stats before the compacted bin
+  uint64_t N, Wv, WA, WK, ckA, ckK;
+  uint32_t token;
+  int done;
+  int found_bin;
+};
+
+struct Result {
+  float m, xA;
+  uint64_t WK, ckK;
+  uint32_t token;
+  uint32_t status;
+  int greedy, empty;
+};
+
+struct CtaSh {
+  uint64_t mbar[MAX_CHUNKS];
+  uint32_t red_u32[NWARP];
+  float red_f[NWARP];
+  uint64_t red_u64[NWARP];
+  uint64_t red_u64b[NWARP];
+  float cta_max;        // read by every CTA of the cluster
+  uint32_t tail_count;  // leader: pushes into its tail buffer
+  uint32_t min_gid;     // leader: lowest id at the max (greedy / top-1)
+  uint32_t status;      // leader: status bits (remote atomicOr)
+  uint32_t n_spec;
+  uint32_t ht_fail;
+  float m, xA, rA;
+  int decision;
+  int tp_ovf;
+  int bcast_i;
+  uint64_t bcast_u64;
+  Cmd cmd;
+  Planner pl;
+  Result res;
+};
+
+// ---------------------------------------------------------------- helpers
+
+__device__ __forceinline__ uint64_t u64min(uint64_t a, uint64_t b) { return a < b ? a : b; }
+__device__ __forceinline__ uint64_t u64max(uint64_t a, uint64_t b) { return a > b ? a : b; }
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Bounded wait on phase `parity`; false if the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  for (unsigned i = 0; i < kWaitLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+  static constexpr int VEC = 4;
+  static __device__ __forceinline__ float get(const uint4 &v, int j) {
+    const uint32_t w = j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+    return __uint_as_float(w);
+  }
+  static __device__ __forceinline__ float vmax(const uint4 &v) {
+    return fmaxf(fmaxf(__uint_as_float(v.x), __uint_as_float(v.y)),
+                 fmaxf(__uint_as_float(v.z), __uint_as_float(v.w)));
+  }
+  static __device__ __forceinline__ float load(const void *row, int64_t i) {
+    return static_cast<const float *>(row)[i];
+  }
+  static __device__ __forceinline__ uint32_t neg_inf_bits() { return 0xFF800000u; }
+  static __device__ __forceinline__ void patch(uint4 &v, uint32_t mbits, uint32_t sbits) {
+    uint32_t *w = reinterpret_cast<uint32_t *>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if ((mbits >> j) & 1u) w[j] = 0xFF800000u;
+      else if ((sbits >> j) & 1u) w[j] = 0x7FC00000u;
+    }
+  }
+  static __device__ __forceinline__ uint32_t bits_of(const uint32_t *map, int k) {
+    return (map[k >> 3] >> ((k & 7) * 4)) & 0xFu;
+  }
+};
+
+template <>
+struct Elem<__nv_bfloat16> {
+  static constexpr int VEC = 8;
+  static __device__ __forceinline__ float get(const uint4 &v, int j) {
+    const uint32_t w = (j >> 1) == 0 ? v.x : (j >> 1) == 1 ? v.y : (j >> 1) == 2 ? v.z : v.w;
+    return __uint_as_float((j & 1) ? (w & 0xFFFF0000u) : (w << 16));
+  }
+  static __device__ __forceinline__ float vmax(const uint4 &v) {
+    __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162 *>(&v.x);
+    __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162 *>(&v.y);
+    __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162 *>(&v.z);
+    __nv_bfloat162 d = *reinterpret_cast<const __nv_bfloat162 *>(&v.w);
+    a = __hmax2(__hmax2(a, b), __hmax2(c, d));
+    return fmaxf(__low2float(a), __high2float(a));
+  }
+  static __device__ __forceinline__ float load(const void *row, int64_t i) {
+    const uint16_t h = static_cast<const uint16_t *>(row)[i];
+    return __uint_as_float((uint32_t)h << 16);
+  }
+  static __device__ __forceinline__ void patch(uint4 &v, uint32_t mbits, uint32_t sbits) {
+    uint16_t *h = reinterpret_cast<uint16_t *>(&v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if ((mbits >> j) & 1u) h[j] = 0xFF80u;
+      else if ((sbits >> j) & 1u) h[j] = 0x7FC0u;
+    }
+  }
+  static __device__ __forceinline__ uint32_t bits_of(const uint32_t *map, int k) {
+    return (map[k >> 2] >> ((k & 3) * 8)) & 0xFFu;
+  }
+};
+
+// ------------------------------------------------------- block reductions
+
+__device__ __forceinline__ uint32_t block_max_u32(uint32_t v, CtaSh &sh) {
+  for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(~0u, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh.red_u32[threadIdx.x >> 5] = v;
+  __syncthreads();
+  uint32_t r = sh.red_u32[0];
+  for (int i = 1; i < NWARP; ++i) r = max(r, sh.red_u32[i]);
+  return r;
+}
+
+__device__ __forceinline__ float block_max_f32(float v, CtaSh &sh) {
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(~0u, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh.red_f[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = sh.red_f[0];
+  for (int i = 1; i < NWARP; ++i) r = fmaxf(r, sh.red_f[i]);
+  return r;
+}
+
+__device__ __forceinline__ void block_minmax_u64(uint64_t &mn, uint64_t &mx, CtaSh &sh) {
+  for (int o = 16; o; o >>= 1) {
+    mn = u64min(mn, (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)mn, o));
+    mx = u64max(mx, (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)mx, o));
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    sh.red_u64[threadIdx.x >> 5] = mn;
+    sh.red_u64b[threadIdx.x >> 5] = mx;
+  }
+  __syncthreads();
+  mn = sh.red_u64[0];
+  mx = sh.red_u64b[0];
+  for (int i = 1; i < NWARP; ++i) {
+    mn = u64min(mn, sh.red_u64[i]);
+    mx = u64max(mx, sh.red_u64b[i]);
+  }
+}
+
+// Exclusive block scan (one value per thread); returns the prefix and the total.
+__device__ __forceinline__ uint64_t block_exscan_u64(uint64_t v, uint64_t &total, CtaSh &sh) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  uint64_t inc = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t t = __shfl_up_sync(~0u, (unsigned long long)inc, o);
+    if (lane >= o) inc += t;
+  }
+  __syncthreads();
+  if (lane == 31) sh.red_u64[wid] = inc;
+  __syncthreads();
+  uint64_t off = 0, tot = 0;
+  for (int i = 0; i < NWARP; ++i) {
+    const uint64_t s = sh.red_u64[i];
+    if (i < wid) off += s;
+    tot += s;
+  }
+  total = tot;
+  return off + inc - v;
+}
+
+// ---------------------------------------------------------- row context
+
+struct Row {
+  const mstar_sampler_params_t *p;
+  int row, slot;
+  int64_t V, gbase;         // vocab_offset
+  const void *rowp;         // logits row
+  float T, invT, Mp, P;
+  int K;                    // 0 = off
+  bool greedy, topk, minp, topp;
+};
+
+__device__ __forceinline__ void row_init(Row &r, const mstar_sampler_params_t &p, int row, int slot) {
+  r.p = &p;
+  r.row = row;
+  r.slot = slot;
+  r.V = p.V;
+  r.gbase = p.vocab_offset;
+  const int es = p.dtype == MSTAR_DTYPE_BF16 ? 2 : 4;
+  r.rowp = static_cast<const uint8_t *>(p.logits) + (int64_t)row * p.ld * es;
+  r.T = p.temperature ? p.temperature[slot] : 1.0f;
+  r.greedy = !(r.T >= 1e-5f);
+  r.invT = r.greedy ? 1.0f : __fdiv_rn(1.0f, r.T);
+  const int K = p.top_k ? p.top_k[slot] : 0;
+  r.topk = K > 0 && (int64_t)K < r.V;
+  r.K = r.topk ? K : 0;
+  float Mp = p.min_p ? p.min_p[slot] : 0.0f;
+  r.minp = Mp > 0.0f;
+  r.Mp = fminf(Mp, 1.0f);
+  r.P = p.top_p ? p.top_p[slot] : 1.0f;
+  r.topp = r.P < 1.0f;
+}
+
+// value-A predicate of x given the row max m (positive weight and min_p).
+__device__ __forceinline__ bool pred_A(const Row &r, float x, float m) {
+  const float e = spec_e(x, m);
+  if (spec_w_from_e(e) == 0) return false;
+  return !r.minp || e >= r.Mp;
+}
+
+// Smallest key in (lo, hi] with pred true, given pred(lo) false, pred(hi)
+// true and pred monotone.  Called by one full warp.
+template <class F>
+__device__ __forceinline__ uint32_t warp_search(uint32_t lo, uint32_t hi, F pred) {
+  const int lane = threadIdx.x & 31;
+  for (int it = 0; it < 64 && hi - lo > 1; ++it) {
+    const uint64_t span = (uint64_t)(hi - lo);
+    uint32_t probe = lo + (uint32_t)((span * (uint64_t)(lane + 1)) >> 5);
+    if (probe <= lo) probe = lo + 1;
+    const bool ok = pred(probe);
+    const unsigned mask = __ballot_sync(~0u, ok);
+    const int f = __ffs(mask) - 1;  // lane 31 probes hi, so mask != 0
+    const uint32_t nhi = __shfl_sync(~0u, probe, f);
+    const uint32_t nlo = __shfl_sync(~0u, probe, f > 0 ? f - 1 : 0);
+    if (f > 0) lo = nlo;
+    hi = nhi;
+  }
+  return hi;
+}
+
+__device__ __forceinline__ uint32_t okey16(uint32_t h) {
+  if (h == 0x8000u) h = 0u;
+  return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
+}
+__device__ __forceinline__ float okey16_inv(uint32_t k) {
+  const uint32_t h = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
+  return __uint_as_float(h << 16);
+}
+
+// Thresholds: x_A (exact value-A boundary) and the raw threshold r_A.
+template <typename T>
+__device__ void compute_thresholds(const Row &r, float m, CtaSh &sh) {
+  if (threadIdx.x < 32) {
+    float xA;
+    if (r.greedy || r.K == 1) {
+      xA = m;
+    } else {
+      const uint32_t kh = okey(m);
+      const uint32_t kl = okey(-INFINITY);
+      const uint32_t k = warp_search(kl, kh, [&](uint32_t key) { return pred_A(r, okey_inv(key), m); });
+      xA = okey_inv(k);
+    }
+    // raw threshold: smallest raw value whose transform reaches xA
+    float rA;
+    auto f = [&](float raw) { return r.greedy ? raw : __fmul_rn(raw, r.invT); };
+    if (sizeof(T) == 2) {
+      const uint32_t lo = okey16(0xFF80u), hi = okey16(0x7F80u);
+      const uint32_t k = warp_search(lo, hi, [&](uint32_t key) { return f(okey16_inv(key)) >= xA; });
+      rA = okey16_inv(k);
+      if (!(f(rA) >= xA)) rA = INFINITY;
+    } else {
+      const uint32_t lo = okey(-INFINITY), hi = okey(INFINITY);
+      const uint32_t k = warp_search(lo, hi, [&](uint32_t key) { return f(okey_inv(key)) >= xA; });
+      rA = okey_inv(k);
+      if (!(f(rA) >= xA)) rA = INFINITY;
+    }
+    if (threadIdx.x == 0) {
+      sh.xA = xA;
+      sh.rA = rA;
+    }
+  }
+  __syncthreads();
+}
+
+// Iterate every element of value-A held by this CTA: resident vectors with
+// raw >= rA, and specials with x >= xA.  fn(x, gid).
+template <typename T, typename F>
+__device__ __forceinline__ void for_each_value(const uint4 *data, int nvec, int64_t pos0_gid, const Cand *spec,
+                                               int nspec, float rA, float xA, bool greedy, float invT, F &&fn) {
+  constexpr int VEC = Elem<T>::VEC;
+  for (int k = threadIdx.x; k < nvec; k += NT) {
+    const uint4 v = data[k];
+    if (Elem<T>::vmax(v) >= rA) {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float raw = Elem<T>::get(v, j);
+        if (raw >= rA) {
+          const float x = greedy ? raw : __fmul_rn(raw, invT);
+          fn(x, (uint32_t)(pos0_gid + (int64_t)k * VEC + j));
+        }
+      }
+    }
+  }
+  for (int i = threadIdx.x; i < nspec; i += NT) {
+    const Cand c = spec[i];
+    if (c.x >= xA) fn(c.x, c.gid);
+  }
+}
+
+__device__ __forceinline__ uint64_t ckey(uint32_t km, float x, uint32_t gid) {
+  return ((uint64_t)(km - okey(x)) << 32) | gid;
+}
+
+// ------------------------------------------------------------- tail sort
+
+struct SortScratch {
+  Cand *mid;
+  uint32_t *tmp;
+  uint64_t *S;
+  uint32_t *bcnt, *boff;
+};
+
+// Sort in[0..n) by (x desc, gid asc) in place; computes S[j] = inclusive
+// prefix of the weights.  Block-wide (all NT threads of one CTA).
+__device__ void tail_sort_scan(Cand *in, int n, float m, const SortScratch &s, CtaSh &sh) {
+  const uint32_t km = okey(m);
+  uint64_t kmin = ~0ull, kmax = 0;
+  for (int i = threadIdx.x; i < n; i += NT) {
+    const uint64_t k = ckey(km, in[i].x, in[i].gid);
+    kmin = u64min(kmin, k);
+    kmax = u64max(kmax, k);
+  }
+  block_minmax_u64(kmin, kmax, sh);
+  const uint64_t span = n > 0 ? kmax - kmin : 0;
+  const int bits = span ? 64 - __clzll((long long)span) : 0;
+  const int shift = bits > 10 ? bits - 10 : 0;
+  for (int b = threadIdx.x; b < NBK; b += NT) s.bcnt[b] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += NT) {
+    const uint32_t b = (uint32_t)((ckey(km, in[i].x, in[i].gid) - kmin) >> shift);
+    const uint32_t pos = atomicAdd(&s.bcnt[b], 1u);
+    s.tmp[i] = (b << 16) | pos;
+  }
+  __syncthreads();
+  {  // exclusive scan of bucket counts, NBK / NT per thread
+    constexpr int PER = NBK / NT;
+    uint32_t loc[PER];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      loc[q] = s.bcnt[threadIdx.x * PER + q];
+      sum += loc[q];
+    }
+    uint64_t tot;
+    uint32_t off = (uint32_t)block_exscan_u64(sum, tot, sh);
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      s.boff[threadIdx.x * PER + q] = off;
+      off += loc[q];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += NT) {
+    const uint32_t t = s.tmp[i];
+    s.mid[s.boff[t >> 16] + (t & 0xFFFFu)] = in[i];
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < n; q += NT) {
+    const Cand c = s.mid[q];
+    const uint64_t key = ckey(km, c.x, c.gid);
+    const uint32_t b = (uint32_t)((key - kmin) >> shift);
+    const uint32_t st = s.boff[b], cn = s.bcnt[b];
+    uint32_t rank = 0;
+    for (uint32_t j = st; j < st + cn; ++j) {
+      const Cand o = s.mid[j];
+      rank += ckey(km, o.x, o.gid) < key;
+    }
+    in[st + rank] = c;
+  }
+  __syncthreads();
+  // weights and inclusive prefix sums: contiguous segments per thread
+  const int seg = (n + NT - 1) / NT;
+  const int a = min(n, (int)threadIdx.x * seg), bnd = min(n, a + seg);
+  uint64_t loc = 0;
+  for (int j = a; j < bnd; ++j) {
+    const uint64_t w = spec_w_from_e(spec_e(in[j].x, m));
+    loc += w;
+    s.S[j] = w;
+  }
+  uint64_t tot;
+  uint64_t run = block_exscan_u64(loc, tot, sh);
+  for (int j = a; j < bnd; ++j) {
+    run += s.S[j];
+    s.S[j] = run;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ uint64_t S_excl(const uint64_t *S, int j) { return j ? S[j - 1] : 0; }
+
+// Fast tail over a sorted prefix of value-A holding all of A: resolves
+// top_k, top_p and the draw.  Sets res.token / WK / ckK.  Block-wide.
+__device__ void fast_resolve(const Row &r, Cand *in, int n, float m, float u, const uint64_t *S, CtaSh &sh) {
+  const uint32_t km = okey(m);
+  const int nA = r.topk ? min(n, r.K) : n;
+  const uint64_t WA = S[nA - 1];
+  int nK = nA;
+  if (r.topp) {
+    const double thr = __dmul_rn((double)r.P, (double)WA);
+    int c = 0;
+    for (int j = threadIdx.x; j < nA; j += NT) c += ((double)S_excl(S, j) < thr) ? 1 : 0;
+    // the predicate holds on a prefix, so its count is the kept-set size
+    uint64_t tot;
+    block_exscan_u64((uint64_t)c, tot, sh);
+    nK = max(1, (int)tot);
+  }
+  const uint64_t WK = S[nK - 1];
+  const uint64_t rr = draw_point(u, WK);
+  for (int j = threadIdx.x; j < nK; j += NT) {
+    if (S_excl(S, j) <= rr && rr < S[j]) sh.res.token = in[j].gid;
+  }
+  if (threadIdx.x == 0) {
+    sh.res.WK = WK;
+    sh.res.ckK = ckey(km, in[nK - 1].x, in[nK - 1].gid);
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------- kernel sections
+
+struct Layout {
+  uint8_t *data;
+  uint32_t *map_mask, *map_spec;
+  int2 *ht;
+  Cand *spec;
+  Cand *tail;
+  uint8_t *work;
+  // work area views
+  uint32_t *l1c;
+  uint64_t *l1m;
+  uint32_t *refc;
+  uint64_t *refm;
+  SortScratch gsort;
+  SortScratch fsort;
+};
+
+__device__ __forceinline__ Layout make_layout(uint8_t *smem, const Plan &pl) {
+  Layout L;
+  L.data = smem;
+  L.work = smem + pl.off_work;
+  L.map_mask = reinterpret_cast<uint32_t *>(L.work);
+  L.map_spec = reinterpret_cast<uint32_t *>(L.work + pl.map_bytes);
+  L.ht = reinterpret_cast<int2 *>(L.work + 2 * pl.map_bytes);
+  L.spec = reinterpret_cast<Cand *>(smem + pl.off_spec);
+  L.tail = reinterpret_cast<Cand *>(smem + pl.off_tail);
+  L.l1c = reinterpret_cast<uint32_t *>(L.work);
+  L.l1m = reinterpret_cast<uint64_t *>(L.work + 4096);
+  L.refc = reinterpret_cast<uint32_t *>(L.work + 12288);
+  L.refm = reinterpret_cast<uint64_t *>(L.work + 16384);
+  L.gsort.mid = reinterpret_cast<Cand *>(L.work + 12288);
+  L.gsort.tmp = reinterpret_cast<uint32_t *>(L.work + 20480);
+  L.gsort.S = reinterpret_cast<uint64_t *>(L.work + 24576);
+  L.gsort.bcnt = reinterpret_cast<uint32_t *>(L.work + 32768);
+  L.gsort.boff = reinterpret_cast<uint32_t *>(L.work + 36864);
+  L.fsort.mid = reinterpret_cast<Cand *>(smem);
+  L.fsort.tmp = reinterpret_cast<uint32_t *>(smem + 16384);
+  L.fsort.S = reinterpret_cast<uint64_t *>(smem + 24576);
+  L.fsort.bcnt = reinterpret_cast<uint32_t *>(smem + 40960);
+  L.fsort.boff = reinterpret_cast<uint32_t *>(smem + 45056);
+  return L;
+}
+
+__device__ __forceinline__ uint32_t ht_hash(uint32_t k, int cap) {
+  return (k * 2654435761u) & (uint32_t)(cap - 1);
+}
+
+// Insert element index e (row-relative) with count increment c.
+__device__ __forceinline__ bool ht_insert(int2 *ht, int cap, int e, int c) {
+  uint32_t h = ht_hash((uint32_t)e, cap);
+  for (int probe = 0; probe < cap; ++probe) {
+    const int prev = atomicCAS(&ht[h].x, -1, e);
+    if (prev == -1 || prev == e) {
+      if (c) atomicAdd(&ht[h].y, c);
+      return true;
+    }
+    h = (h + 1) & (uint32_t)(cap - 1);
+  }
+  return false;
+}
+
+__device__ __forceinline__ uint32_t allowed32(const uint32_t *aw, int64_t nwords, int64_t g) {
+  const int64_t w = g >> 5;
+  const int sh = (int)(g & 31);
+  uint32_t lo = w < nwords ? aw[w] : 0u;
+  uint32_t hi = (sh && w + 1 < nwords) ? aw[w + 1] : 0u;
+  return sh ? ((lo >> sh) | (hi << (32 - sh))) : lo;
+}
+
+// State updates + scalar outputs for one row (called by one thread).
+__device__ __forceinline__ void write_row_outputs(const mstar_sampler_params_t &p, int row, int slot, uint32_t token,
+                                                  uint32_t status, bool drew) {
+  if (p.out_ids) p.out_ids[row] = (int64_t)token;
+  if (p.out_ids32) p.out_ids32[row] = (int32_t)token;
+  if (p.out_status) p.out_status[row] = (int32_t)status;
+  if ((p.flags & MSTAR_FLAG_ADVANCE_OFFSET) && p.offset && !p.uniforms) p.offset[slot] += 1;
+  if ((p.flags & MSTAR_FLAG_UPDATE_HISTORY) && p.hist_ids && p.hist_len && p.H > 0) {
+    const int32_t len = p.hist_len[slot];
+    p.hist_ids[(int64_t)slot * p.H + (len % p.H)] = (int32_t)token;
+    p.hist_len[slot] = len + 1;
+  }
+  if ((p.flags & MSTAR_FLAG_UPDATE_SEEN) && p.seen_bits) {
+    atomicOr(&p.seen_bits[(int64_t)slot * p.seen_words + (token >> 5)], 1u << (token & 31));
+  }
+  (void)drew;
+}
+
+// ------------------------------------------------------------ the kernel
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(NT, 1)
+    sampler_kernel(const mstar_sampler_params_t p, const Plan pl, uint32_t *tp_send) {
+  constexpr int VEC = Elem<T>::VEC;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int S = pl.S;
+  const int row = blockIdx.y;
+  const int tid = threadIdx.x;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ CtaSh sh;
+
+  const int slot = p.slot_idx ? p.slot_idx[row] : row;
+  if (slot < 0) {  // padding row: uniform across the cluster
+    if (rank == 0 && tid == 0) {
+      if (MODE == 0) {
+        if (p.out_ids) p.out_ids[row] = p.vocab_offset;
+        if (p.out_ids32) p.out_ids32[row] = (int32_t)p.vocab_offset;
+        if (p.out_status) p.out_status[row] = 0;
+      } else {
+        uint32_t *rec = tp_send + (int64_t)row * pl.rec_words;
+        rec[0] = __float_as_uint(-INFINITY);
+        rec[1] = 0;
+        rec[2] = 0;
+        rec[3] = 0;
+      }
+    }
+    if (MODE == 0 && (p.out_x || p.out_kept || p.out_probs)) {
+      const int64_t c0 = min((int64_t)rank * pl.slice, (int64_t)p.V), c1 = min((int64_t)p.V, c0 + pl.slice);
+      for (int64_t i = c0 + tid; i < c1; i += NT) {
+        const int64_t o = (int64_t)row * p.V + i;
+        if (p.out_x) p.out_x[o] = -INFINITY;
+        if (p.out_kept) p.out_kept[o] = 0;
+        if (p.out_probs) p.out_probs[o] = 0.0f;
+      }
+    }
+    return;
+  }
+
+  Row r;
+  row_init(r, p, row, slot);
+  const Layout L = make_layout(smem, pl);
+
+  // ---- slice geometry (a slice past the end of a short row is empty)
+  const int64_t c0 = min((int64_t)rank * pl.slice, (int64_t)p.V);
+  const int64_t c1 = min((int64_t)p.V, c0 + pl.slice);
+  const uint8_t *rowp = static_cast<const uint8_t *>(r.rowp);
+  const uintptr_t a_c0 = reinterpret_cast<uintptr_t>(rowp + c0 * pl.es);
+  const uintptr_t a_c1 = reinterpret_cast<uintptr_t>(rowp + c1 * pl.es);
+  const uintptr_t a_al = a_c0 & ~(uintptr_t)15;
+  const int64_t c0al = c0 - (int64_t)((a_c0 - a_al) / pl.es);
+  const uintptr_t b0 = (a_c0 + 15) & ~(uintptr_t)15;
+  const uintptr_t b1 = a_c1 & ~(uintptr_t)15;
+  const int64_t nbulk = (b1 > b0) ? (int64_t)(b1 - b0) : 0;
+  const int hv = (int)((b0 - a_al) / 16);                 // head fringe vectors (0 or 1)
+  const int nbv = (int)(nbulk / 16);                      // bulk vectors
+  const int nvec = (int)((a_c1 - a_al + 15) / 16);        // all vectors of the slice
+  const int nchunk = (int)((nbulk + CHUNK_BYTES - 1) / CHUNK_BYTES);
+  const int64_t pos0_gid = r.gbase + c0al;                // gid of data position 0
+  uint4 *data4 = reinterpret_cast<uint4 *>(L.data);
+
+  // ---- setup: barriers, bulk copies, bitmaps, specials
+  if (tid == 0) {
+    for (int j = 0; j < nchunk; ++j) mbar_init(&sh.mbar[j], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    sh.cta_max = -INFINITY;
+    sh.tail_count = 0;
+    sh.min_gid = 0xFFFFFFFFu;
+    sh.status = 0;
+    sh.n_spec = 0;
+    sh.ht_fail = 0;
+    sh.tp_ovf = 0;
+  }
+  const int map_words = pl.map_bytes / 4;
+  for (int i = tid; i < map_words; i += NT) {
+    L.map_spec[i] = 0u;
+  }
+  for (int i = tid; i < pl.ht_cap; i += NT) L.ht[i] = make_int2(-1, 0);
+  __syncthreads();
+  if (tid == 0) {
+    for (int j = 0; j < nchunk; ++j) {
+      const uint32_t bytes = (uint32_t)min((int64_t)CHUNK_BYTES, nbulk - (int64_t)j * CHUNK_BYTES);
+      mbar_expect_tx(&sh.mbar[j], bytes);
+      bulk_g2s(L.data + (b0 - a_al) + (int64_t)j * CHUNK_BYTES,
+               reinterpret_cast<const void *>(b0 + (uintptr_t)j * CHUNK_BYTES), bytes, &sh.mbar[j]);
+    }
+  }
+  // fringe vectors: plain loads (positions outside the slice get -inf)
+  for (int k = tid; k < nvec; k += NT) {
+    if (k >= hv && k < hv + nbv) continue;
+    uint4 v;
+    uint8_t *vb = reinterpret_cast<uint8_t *>(&v);
+    for (int j = 0; j < VEC; ++j) {
+      const int64_t e = c0al + (int64_t)k * VEC + j;
+      if (e >= c0 && e < c1) {
+        if (sizeof(T) == 2) {
+          const uint16_t h = static_cast<const uint16_t *>(r.rowp)[e];
+          memcpy(vb + 2 * j, &h, 2);
+        } else {
+          const uint32_t w = static_cast<const uint32_t *>(r.rowp)[e];
+          memcpy(vb + 4 * j, &w, 4);
+        }
+      } else {
+        if (sizeof(T) == 2) {
+          const uint16_t h = 0xFF80u;
+          memcpy(vb + 2 * j, &h, 2);
+        } else {
+          const uint32_t w = 0xFF800000u;
+          memcpy(vb + 4 * j, &w, 4);
+        }
+      }
+    }
+    data4[k] = v;
+  }
+  // mask bitmap: outside-slice positions and disallowed ids
+  {
+    const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)slot * p.allowed_words : nullptr;
+    for (int wi = tid; wi < map_words; wi += NT) {
+      const int64_t e0 = c0al + (int64_t)wi * 32;
+      const int64_t lo_in = min((int64_t)32, max((int64_t)0, c0 - e0));
+      const int64_t hi_in = min((int64_t)32, max((int64_t)0, c1 - e0));
+      uint32_t inmask = 0u;
+      if (hi_in > lo_in) {
+        const uint32_t hm = hi_in == 32 ? ~0u : ((1u << hi_in) - 1u);
+        const uint32_t lm = lo_in == 32 ? ~0u : ((1u << lo_in) - 1u);
+        inmask = hm & ~lm;
+      }
+      uint32_t dis = 0u;
+      if (aw && inmask) {
+        const uint32_t bits = allowed32(aw, p.allowed_words, r.gbase + e0 + lo_in) << lo_in;
+        dis = inmask & ~bits;
+      }
+      L.map_mask[wi] = ~inmask | dis;
+    }
+  }
+  // specials: history / seen bits / bias ids that fall in [c0, c1)
+  if (p.hist_ids && p.hist_len) {
+    const int32_t len = p.hist_len[slot];
+    const int n = min(len, p.H);
+    const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
+    for (int j = tid; j < n; j += NT) {
+      const int64_t e = (int64_t)h[j] - r.gbase;
+      if (e >= c0 && e < c1) {
+        if (!ht_insert(L.ht, pl.ht_cap, (int)e, 1)) sh.ht_fail = 1;
+        atomicOr(&L.map_spec[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
+      }
+    }
+  } else if (p.seen_bits) {
+    const uint32_t *sw = p.seen_bits + (int64_t)slot * p.seen_words;
+    const int64_t g0 = r.gbase + c0, g1 = r.gbase + c1;
+    for (int64_t w = (g0 >> 5) + tid; w <= ((g1 - 1) >> 5); w += NT) {
+      uint32_t bits = sw[w];
+      while (bits) {
+        const int b = __ffs(bits) - 1;
+        bits &= bits - 1;
+        const int64_t g = (w << 5) + b;
+        if (g < g0 || g >= g1) continue;
+        const int64_t e = g - r.gbase;
+        if (!ht_insert(L.ht, pl.ht_cap, (int)e, 1)) sh.ht_fail = 1;
+        atomicOr(&L.map_spec[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
+      }
+    }
+  }
+  if (p.bias_ids && p.bias_vals) {
+    const int32_t *bi = p.bias_ids + (int64_t)slot * p.NB;
+    for (int j = tid; j < p.NB; j += NT) {
+      const int32_t g = bi[j];
+      if (g < 0) continue;
+      const int64_t e = (int64_t)g - r.gbase;
+      if (e >= c0 && e < c1) {
+        if (!ht_insert(L.ht, pl.ht_cap, (int)e, 0)) sh.ht_fail = 1;
+        atomicOr(&L.map_spec[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
+      }
+    }
+  }
+  __syncthreads();
+  // finalize specials from global memory (overlaps the bulk copies)
+  float spec_max = -INFINITY;
+  {
+    const float R = p.rep_pen ? p.rep_pen[slot] : 1.0f;
+    const float F = p.freq_pen ? p.freq_pen[slot] : 0.0f;
+    const float Pp = p.pres_pen ? p.pres_pen[slot] : 0.0f;
+    const int32_t *bi = p.bias_ids ? p.bias_ids + (int64_t)slot * p.NB : nullptr;
+    const float *bv = p.bias_vals ? p.bias_vals + (int64_t)slot * p.NB : nullptr;
+    for (int i = tid; i < pl.ht_cap; i += NT) {
+      const int2 ent = L.ht[i];
+      if (ent.x < 0) continue;
+      const int64_t e = ent.x;
+      float v = Elem<T>::load(r.rowp, e);
+      if (bi && bv) {
+        const int32_t gid = (int32_t)(e + r.gbase);
+        for (int j = 0; j < p.NB; ++j)
+          if (bi[j] == gid) v = __fadd_rn(v, bv[j]);
+      }
+      if (ent.y > 0) {
+        v = (v > 0.0f) ? __fdiv_rn(v, R) : __fmul_rn(v, R);
+        v = __fsub_rn(v, __fmul_rn(F, (float)ent.y));
+        v = __fsub_rn(v, Pp);
+      }
+      const int64_t pos = e - c0al;
+      const bool masked = (L.map_mask[pos >> 5] >> (pos & 31)) & 1u;
+      float x;
+      if (v != v) x = v;
+      else if (masked) x = -INFINITY;
+      else x = r.greedy ? v : __fmul_rn(v, r.invT);
+      const uint32_t idx = atomicAdd(&sh.n_spec, 1u);
+      if ((int)idx < pl.spec_cap) L.spec[idx] = Cand{x, (uint32_t)(e + r.gbase)};
+      else sh.ht_fail = 1;
+      spec_max = fmaxf(spec_max, x);
+    }
+  }
+  __syncthreads();
+  const int nspec = min((int)sh.n_spec, pl.spec_cap);
+
+  // ---- pass A: patch + raw max, chunk by chunk as the bulk copies land
+  float rawmax = -INFINITY;
+  bool timed_out = false;
+  {
+    auto process = [&](int k) {
+      uint4 v = data4[k];
+      const uint32_t mb = Elem<T>::bits_of(L.map_mask, k), sb = Elem<T>::bits_of(L.map_spec, k);
+      if (mb | sb) {
+        Elem<T>::patch(v, mb, sb);
+        data4[k] = v;
+      }
+      rawmax = fmaxf(rawmax, Elem<T>::vmax(v));
+    };
+    for (int k = tid; k < nvec; k += NT)
+      if (k < hv || k >= hv + nbv) process(k);
+    constexpr int CV = CHUNK_BYTES / 16;
+    for (int j = 0; j < nchunk; ++j) {
+      if (!mbar_wait(&sh.mbar[j], 0)) timed_out = true;
+      const int kb = hv + j * CV, ke = hv + min(nbv, (j + 1) * CV);
+      for (int k = kb + tid; k < ke; k += NT) process(k);
+    }
+  }
+  if (timed_out) atomicOr(&sh.status, MSTAR_STATUS_TIMEOUT);
+  if (sh.ht_fail && tid == 0) atomicOr(&sh.status, MSTAR_STATUS_SPECIAL_OVERFLOW);
+  {
+    const float xm = r.greedy ? rawmax : __fmul_rn(rawmax, r.invT);
+    const float cm = block_max_f32(fmaxf(xm, spec_max), sh);
+    if (tid == 0) sh.cta_max = cm;
+  }
+  cluster.sync();  // #1: maxima published; leader counters initialised
+
+  // ---- row max and thresholds
+  float m = -INFINITY;
+  for (int q = 0; q < S; ++q) m = fmaxf(m, *cluster.map_shared_rank(&sh.cta_max, q));
+  CtaSh *lead = cluster.map_shared_rank(&sh, 0);
+  Cand *lead_tail = cluster.map_shared_rank(L.tail, 0);
+  if (sh.status && tid == 0) atomicOr(&lead->status, sh.status);
+  const bool empty = !(m > -INFINITY);
+  const bool one = r.greedy || r.K == 1;
+  float u = 0.0f;
+  if (!empty) {
+    compute_thresholds<T>(r, m, sh);
+    const float xA = sh.xA, rA = sh.rA;
+    const uint32_t km = okey(m);
+    (void)km;
+    // ---- pass C: compaction of value-A (or lowest id at the max)
+    if (one) {
+      uint32_t best = 0xFFFFFFFFu;
+      for_each_value<T>(data4, nvec, pos0_gid, L.spec, nspec, rA, xA, r.greedy, r.invT,
+                        [&](float x, uint32_t gid) { best = min(best, gid); });
+      for (int o = 16; o; o >>= 1) best = min(best, __shfl_xor_sync(~0u, best, o));
+      if ((tid & 31) == 0 && best != 0xFFFFFFFFu) atomicMin(&lead->min_gid, best);
+    } else {
+      for_each_value<T>(data4, nvec, pos0_gid, L.spec, nspec, rA, xA, r.greedy, r.invT,
+                        [&](float x, uint32_t gid) {
+                          const uint32_t idx = atomicAdd(&lead->tail_count, 1u);
+                          if (idx < (uint32_t)TAIL_CAP) lead_tail[idx] = Cand{x, gid};
+                        });
+    }
+  }
+  cluster.sync();  // #2: candidates complete
+
+  const uint32_t ncand = lead->tail_count;
+  const bool force_general = (p.flags & MSTAR_FLAG_FORCE_GENERAL) != 0;
+  const bool fast = empty || one || (ncand <= (uint32_t)TAIL_CAP && !force_general);
+  if (rank == 0) {
+    if (tid == 0) {
+      sh.res.m = m;
+      sh.res.xA = empty ? INFINITY : sh.xA;
+      sh.res.greedy = r.greedy;
+      sh.res.empty = empty;
+      sh.res.token = 0;
+      sh.res.WK = 0;
+      sh.res.ckK = 0;
+    }
+    __syncthreads();
+    if (!empty) {
+      if (p.uniforms) u = p.uniforms[row];
+      else u = philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
+    }
+  }
+  int nemit = 0;  // TP: sorted candidates to emit from L.tail
+  if (fast) {
+    if (rank == 0 && !empty) {
+      if (one) {
+        if (tid == 0) {
+          sh.res.token = sh.min_gid;
+          sh.res.WK = 4294967296ull;
+          sh.res.ckK = ((uint64_t)0 << 32) | sh.min_gid;
+        }
+        __syncthreads();
+        nemit = -1;
+      } else {
+        tail_sort_scan(L.tail, (int)ncand, m, L.fsort, sh);
+        if (MODE == 0) {
+          fast_resolve(r, L.tail, (int)ncand, m, u, L.fsort.S, sh);
+        } else {
+          nemit = r.topk ? min((int)ncand, r.K) : (int)ncand;
+        }
+      }
+    }
+  } else {
+    // ---- general path: leader-driven rounds over the resident slices
+    Planner &P = sh.pl;
+    if (rank == 0 && tid == 0) {
+      memset(&P, 0, sizeof(P));
+      P.state = ST_START;
+      atomicOr(&sh.status, MSTAR_STATUS_GENERAL);
+    }
+    const uint32_t km = okey(m);
+    const float xA = sh.xA, rA = sh.rA;
+    for (int round = 0; round < MAX_ROUNDS; ++round) {
+      if (rank == 0) {
+        // ================= leader planning (block-wide) =================
+        for (int guard = 0; guard < 16; ++guard) {
+          __syncthreads();
+          const int state = P.state;
+          __syncthreads();
+          if (state == ST_START) {
+            if (tid == 0) {
+              const uint32_t DA = km - okey(xA);
+              P.l1lo = 0;
+              P.l1hi = ((uint64_t)DA << 32) | 0xFFFFFFFFull;
+              const int bits = 64 - __clzll((long long)(P.l1hi - P.l1lo));
+              P.l1shift = bits > 10 ? bits - 10 : 0;
+              P.l1nbins = (int)((P.l1hi - P.l1lo) >> P.l1shift) + 1;
+              sh.cmd = Cmd{OP_HIST, TGT_L1, P.l1lo, P.l1hi, P.l1shift, P.l1nbins};
+              P.state = ST_AFTER_L1;
+            }
+            for (int b = tid; b < NBIN; b += NT) {
+              L.l1c[b] = 0;
+              L.l1m[b] = 0;
+            }
+            break;
+          }
+          if (state == ST_AFTER_L1 || state == ST_LOC_AFTER_REF) {
+            // inclusive prefix of the level's bins
+            uint32_t *C = state == ST_AFTER_L1 ? L.l1c : L.refc;
+            uint64_t *M = state == ST_AFTER_L1 ? L.l1m : L.refm;
+            constexpr int PER = NBIN / NT;
+            uint64_t lc[PER], lm[PER], sc = 0, sm = 0;
+#pragma unroll
+            for (int q = 0; q < PER; ++q) {
+              lc[q] = C[tid * PER + q];
+              lm[q] = M[tid * PER + q];
+              sc += lc[q];
+              sm += lm[q];
+            }
+            uint64_t tc, tm;
+            uint64_t oc = block_exscan_u64(sc, tc, sh);
+            __syncthreads();
+            uint64_t om = block_exscan_u64(sm, tm, sh);
+#pragma unroll
+            for (int q = 0; q < PER; ++q) {
+              oc += lc[q];
+              om += lm[q];
+              C[tid * PER + q] = (uint32_t)oc;
+              M[tid * PER + q] = om;
+            }
+            __syncthreads();
+            if (state == ST_AFTER_L1) {
+              if (tid == 0) {
+                P.N = tc;
+                P.Wv = tm;
+                P.level = 0;
+                P.lo = P.l1lo;
+                P.hi = P.l1hi;
+                P.shift = P.l1shift;
+                P.nbins = P.l1nbins;
+                P.base_c = 0;
+                P.base_m = 0;
+                const bool needA = r.topk && P.N > (uint64_t)r.K;
+                // smallest prefix [l1lo, end of bin b_end] containing A
+                int b_end = P.nbins - 1;
+                if (needA) {
+                  for (int b = 0; b < P.nbins; ++b)
+                    if ((uint64_t)L.l1c[b] > (uint64_t)(r.K - 1)) {
+                      b_end = b;
+                      break;
+                    }
+                }
+                const uint64_t pre = L.l1c[b_end];
+                if (pre <= (uint64_t)TAIL_CAP) {
+                  const uint64_t bhi = u64min(P.l1hi, P.l1lo + (((uint64_t)b_end + 1) << P.l1shift) - 1);
+                  sh.cmd = Cmd{OP_COMPACT, 0, P.l1lo, bhi, 0, 0};
+                  P.state = ST_AFTER_PREFIX;
+                } else if (needA) {
+                  P.stage = 0;
+                  P.qkind = Q_COUNT;
+                  P.tcount = (uint64_t)(r.K - 1);
+                  P.state = ST_LOC_BIN;
+                } else if (MODE == 1) {
+                  P.state = ST_FINISH;
+                  sh.tp_ovf = 1;
+                } else {
+                  P.WA = P.Wv;
+                  P.ckA = P.l1hi;
+                  P.stage = 1;
+                  if (r.topp) {
+                    P.thr = __dmul_rn((double)r.P, (double)P.WA);
+                    if (!(0.0 < P.thr)) {
+                      P.qkind = Q_COUNT;
+                      P.tcount = 0;
+                    } else {
+                      P.qkind = Q_LASTLT;
+                    }
+                  } else {
+                    P.WK = P.WA;
+                    P.ckK = P.ckA;
+                    P.stage = 2;
+                    P.qkind = Q_POINT;
+                    P.tpoint = draw_point(u, P.WK);
+                  }
+                  P.state = ST_LOC_BIN;
+                }
+              }
+              __syncthreads();
+              if (P.state == ST_AFTER_PREFIX) {
+                if (tid == 0) sh.tail_count = 0;
+                break;
+              }
+              continue;
+            }
+            // ST_LOC_AFTER_REF: switch to the refined level
+            if (tid == 0) {
+              P.level = 1;
+              P.state = ST_LOC_BIN;
+            }
+            continue;
+          }
+          if (state == ST_LOC_BIN) {
+            const uint32_t *C = P.level == 0 ? L.l1c : L.refc;
+            const uint64_t *M = P.level == 0 ? L.l1m : L.refm;
+            if (tid == 0) sh.bcast_i = -1;
+            __syncthreads();
+            for (int b = tid; b < P.nbins; b += NT) {
+              const uint64_t pc0 = P.base_c + (b ? C[b - 1] : 0), pc1 = P.base_c + C[b];
+              const uint64_t pm0 = P.base_m + (b ? M[b - 1] : 0), pm1 = P.base_m + M[b];
+              bool hit = false;
+              if (P.qkind == Q_COUNT) hit = pc0 <= P.tcount && P.tcount < pc1;
+              else if (P.qkind == Q_POINT) hit = pm0 <= P.tpoint && P.tpoint < pm1;
+              if (hit) sh.bcast_i = b;
+              if (P.qkind == Q_LASTLT && pc1 > pc0 && (double)pm0 < P.thr) atomicMax(&sh.bcast_i, b);
+            }
+            __syncthreads();
+            if (tid == 0) {
+              const int b = sh.bcast_i;
+              if (b < 0) {  // cannot happen for consistent inputs; finish defensively
+                P.state = ST_FINISH;
+                atomicOr(&sh.status, MSTAR_STATUS_EMPTY);
+              } else {
+                const uint64_t blo = P.lo + ((uint64_t)b << P.shift);
+                const uint64_t bhi = u64min(P.hi, blo + (1ull << P.shift) - 1);
+                const uint64_t cnt = (uint64_t)C[b] - (b ? C[b - 1] : 0);
+                P.cbase_c = P.base_c + (b ? C[b - 1] : 0);
+                P.cbase_m = P.base_m + (b ? M[b - 1] : 0);
+                if (cnt <= (uint64_t)GCAP || P.shift == 0) {
+                  sh.cmd = Cmd{OP_COMPACT, 0, blo, bhi, 0, 0};
+                  sh.tail_count = 0;
+                  P.state = ST_LOC_AFTER_COMPACT;
+                } else {
+                  P.base_c = P.cbase_c;
+                  P.base_m = P.cbase_m;
+                  P.lo = blo;
+                  P.hi = bhi;
+                  const int bits = 64 - __clzll((long long)(bhi - blo));
+                  P.shift = bits > 10 ? bits - 10 : 0;
+                  P.nbins = (int)((bhi - blo) >> P.shift) + 1;
+                  sh.cmd = Cmd{OP_HIST, TGT_REF, blo, bhi, P.shift, P.nbins};
+                  P.state = ST_LOC_AFTER_REF;
+                }
+              }
+            }
+            __syncthreads();
+            if (P.state == ST_LOC_AFTER_REF) {
+              for (int b = tid; b < NBIN; b += NT) {
+                L.refc[b] = 0;
+                L.refm[b] = 0;
+              }
+            }
+            if (P.state == ST_FINISH) continue;
+            break;
+          }
+          if (state == ST_AFTER_PREFIX) {
+            const int n = (int)min(sh.tail_count, (uint32_t)TAIL_CAP);
+            tail_sort_scan(L.tail, n, m, L.fsort, sh);
+            if (MODE == 0) {
+              fast_resolve(r, L.tail, n, m, u, L.fsort.S, sh);
+            } else {
+              nemit = r.topk ? min(n, r.K) : n;
+            }
+            if (tid == 0) P.state = ST_FINISH;
+            __syncthreads();
+            continue;
+          }
+          if (state == ST_LOC_AFTER_COMPACT) {
+            const int n = (int)min(sh.tail_count, (uint32_t)GCAP);
+            tail_sort_scan(L.tail, n, m, L.gsort, sh);
+            const uint64_t *Sx = L.gsort.S;
+            if (tid == 0) sh.bcast_i = -1;
+            __syncthreads();
+            for (int j = tid; j < n; j += NT) {
+              const uint64_t se = P.cbase_m + S_excl(Sx, j), si = P.cbase_m + Sx[j];
+              bool hit = false;
+              if (P.qkind == Q_COUNT) hit = (P.cbase_c + j) == P.tcount;
+              else if (P.qkind == Q_POINT) hit = se <= P.tpoint && P.tpoint < si;
+              if (hit) sh.bcast_i = j;
+              if (P.qkind == Q_LASTLT && (double)se < P.thr) atomicMax(&sh.bcast_i, j);
+            }
+            __syncthreads();
+            if (tid == 0) {
+              const int j = sh.bcast_i;
+              if (j < 0) {
+                P.state = ST_FINISH;
+                atomicOr(&sh.status, MSTAR_STATUS_EMPTY);
+              } else {
+                const uint64_t ck = ckey(km, L.tail[j].x, L.tail[j].gid);
+                const uint64_t se = P.cbase_m + S_excl(Sx, j), si = P.cbase_m + Sx[j];
+                // back to L1 for the next query
+                P.level = 0;
+                P.lo = P.l1lo;
+                P.hi = P.l1hi;
+                P.shift = P.l1shift;
+                P.nbins = P.l1nbins;
+                P.base_c = 0;
+                P.base_m = 0;
+                if (P.stage == 0) {  // A boundary (top_k)
+                  P.WA = si;
+                  P.ckA = ck;
+                  if (MODE == 1 || r.K <= TAIL_CAP) {
+                    sh.cmd = Cmd{OP_COMPACT, 0, P.l1lo, ck, 0, 0};
+                    P.state = ST_AFTER_PREFIX;
+                  } else {
+                    P.stage = 1;
+                    if (r.topp) {
+                      P.thr = __dmul_rn((double)r.P, (double)P.WA);
+                      if (!(0.0 < P.thr)) {
+                        P.qkind = Q_COUNT;
+                        P.tcount = 0;
+                      } else {
+                        P.qkind = Q_LASTLT;
+                      }
+                    } else {
+                      P.WK = P.WA;
+                      P.ckK = P.ckA;
+                      P.stage = 2;
+                      P.qkind = Q_POINT;
+                      P.tpoint = draw_point(u, P.WK);
+                    }
+                    P.state = ST_LOC_BIN;
+                  }
+                } else if (P.stage == 1) {  // top-p boundary: last kept element
+                  P.WK = si;
+                  P.ckK = ck;
+                  P.stage = 2;
+                  P.qkind = Q_POINT;
+                  P.tpoint = draw_point(u, P.WK);
+                  P.state = ST_LOC_BIN;
+                } else {  // draw
+                  sh.res.token = L.tail[j].gid;
+                  sh.res.WK = P.WK;
+                  sh.res.ckK = P.ckK;
+                  P.state = ST_FINISH;
+                }
+              }
+            }
+            __syncthreads();
+            if (P.state == ST_AFTER_PREFIX) {
+              if (tid == 0) sh.tail_count = 0;
+              break;
+            }
+            continue;
+          }
+          if (state == ST_FINISH) {
+            if (tid == 0) sh.cmd = Cmd{OP_DONE, 0, 0, 0, 0, 0};
+            break;
+          }
+        }
+        __syncthreads();
+      }
+      cluster.sync();  // command published
+      const Cmd cmd = lead->cmd;
+      if (cmd.op == OP_DONE) break;
+      if (cmd.op == OP_HIST) {
+        uint32_t *hc = rank == 0 ? (cmd.target == TGT_L1 ? L.l1c : L.refc) : L.l1c;
+        uint64_t *hm = rank == 0 ? (cmd.target == TGT_L1 ? L.l1m : L.refm) : L.l1m;
+        if (rank != 0) {
+          for (int b = tid; b < NBIN; b += NT) {
+            hc[b] = 0;
+            hm[b] = 0;
+          }
+          __syncthreads();
+        }
+        for_each_value<T>(data4, nvec, pos0_gid, L.spec, nspec, rA, xA, r.greedy, r.invT,
+                          [&](float x, uint32_t gid) {
+                            const uint64_t ck = ckey(km, x, gid);
+                            if (ck < cmd.lo || ck > cmd.hi) return;
+                            const int b = (int)((ck - cmd.lo) >> cmd.shift);
+                            atomicAdd(&hc[b], 1u);
+                            atomicAdd((unsigned long long *)&hm[b],
+                                      (unsigned long long)spec_w_from_e(spec_e(x, m)));
+                          });
+        if (rank != 0) {
+          __syncthreads();
+          uint32_t *rc = cluster.map_shared_rank(cmd.target == TGT_L1 ? L.l1c : L.refc, 0);
+          uint64_t *rm = cluster.map_shared_rank(cmd.target == TGT_L1 ? L.l1m : L.refm, 0);
+          for (int b = tid; b < cmd.nbins; b += NT) {
+            if (hc[b]) {
+              atomicAdd(&rc[b], hc[b]);
+              atomicAdd((unsigned long long *)&rm[b], (unsigned long long)hm[b]);
+            }
+          }
+        }
+      } else {  // OP_COMPACT
+        for_each_value<T>(data4, nvec, pos0_gid, L.spec, nspec, rA, xA, r.greedy, r.invT,
+                          [&](float x, uint32_t gid) {
+                            const uint64_t ck = ckey(km, x, gid);
+                            if (ck < cmd.lo || ck > cmd.hi) return;
+                            const uint32_t idx = atomicAdd(&lead->tail_count, 1u);
+                            if (idx < (uint32_t)TAIL_CAP) lead_tail[idx] = Cand{x, gid};
+                          });
+      }
+      cluster.sync();  // round results complete
+    }
+  }
+
+  // ---- leader: outputs and state updates
+  if (rank == 0) {
+    __syncthreads();
+    if (MODE == 0) {
+      if (tid == 0) {
+        uint32_t status = sh.status;
+        uint32_t token = sh.res.token;
+        if (empty) {
+          status |= MSTAR_STATUS_EMPTY;
+          token = (uint32_t)r.gbase;
+        }
+        sh.res.status = status;
+        write_row_outputs(p, row, slot, token, status, !empty);
+      }
+    } else {
+      uint32_t *rec = tp_send + (int64_t)row * pl.rec_words;
+      const bool ovf = sh.tp_ovf || (nemit > pl.tp_cap);
+      if (tid == 0) {
+        rec[0] = __float_as_uint(empty ? -INFINITY : m);
+        uint32_t st = sh.status | (ovf ? MSTAR_STATUS_TP_OVERFLOW : 0u) | (empty ? MSTAR_STATUS_EMPTY : 0u);
+        if (nemit < 0) {
+          rec[1] = 1;
+          rec[4] = __float_as_uint(m);
+          rec[5] = sh.min_gid;
+        } else {
+          rec[1] = ovf ? 0u : (uint32_t)nemit;
+        }
+        rec[2] = st;
+        rec[3] = 0;
+      }
+      if (!ovf && nemit > 0) {
+        for (int j = tid; j < nemit; j += NT) {
+          rec[4 + 2 * j] = __float_as_uint(L.tail[j].x);
+          rec[5 + 2 * j] = L.tail[j].gid;
+        }
+      }
+    }
+  }
+
+  // ---- debug dense outputs (recomputed from global memory)
+  if (MODE == 0 && (p.out_x || p.out_kept || p.out_probs)) {
+    cluster.sync();
+    const Result res = lead->res;
+    const uint32_t kmm = okey(res.m);
+    const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)slot * p.allowed_words : nullptr;
+    auto emit = [&](int64_t e, float x) {
+      const int64_t o = (int64_t)row * p.V + e;
+      const uint32_t gid = (uint32_t)(e + r.gbase);
+      bool kept = false;
+      float prob = 0.0f;
+      if (!res.empty) {
+        if (res.greedy) {
+          kept = gid == res.token;
+          prob = kept ? 1.0f : 0.0f;
+        } else if (x >= res.xA && ckey(kmm, x, gid) <= res.ckK) {
+          kept = true;
+          prob = (float)__ddiv_rn((double)spec_w_from_e(spec_e(x, res.m)), (double)res.WK);
+        }
+      }
+      if (p.out_x) p.out_x[o] = x;
+      if (p.out_kept) p.out_kept[o] = kept ? 1 : 0;
+      if (p.out_probs) p.out_probs[o] = prob;
+    };
+    for (int64_t e = c0 + tid; e < c1; e += NT) {
+      float v = Elem<T>::load(r.rowp, e);
+      const int64_t g = e + r.gbase;
+      const bool allowed = !aw || ((aw[g >> 5] >> (g & 31)) & 1u);
+      float x;
+      if (!allowed) x = (v != v) ? v : -INFINITY;
+      else if (v != v) x = v;
+      else x = r.greedy ? v : __fmul_rn(v, r.invT);
+      emit(e, x);
+    }
+    __syncthreads();
+    for (int i = tid; i < nspec; i += NT) emit((int64_t)L.spec[i].gid - r.gbase, L.spec[i].x);
+  }
+  cluster.sync();  // keep shared memory alive until every remote access is done
+}
+
+// ------------------------------------------------------------ TP merge
+
+// One CTA per row: merge tp_world candidate records and sample.
+__global__ void __launch_bounds__(NT, 1)
+    tp_merge_kernel(const mstar_sampler_params_t p, int tp_cap, int tp_world, int rec_words, int64_t V_global,
+                    const uint32_t *recv) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ CtaSh sh;
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int slot = p.slot_idx ? p.slot_idx[row] : row;
+  if (slot < 0) {
+    if (tid == 0) {
+      if (p.out_ids) p.out_ids[row] = 0;
+      if (p.out_ids32) p.out_ids32[row] = 0;
+      if (p.out_status) p.out_status[row] = 0;
+    }
+    return;
+  }
+  Row r;
+  mstar_sampler_params_t pg = p;
+  pg.V = (int32_t)V_global;
+  pg.vocab_offset = 0;
+  row_init(r, pg, row, slot);
+  Cand *tail = reinterpret_cast<Cand *>(smem + FAST_SCRATCH);
+  SortScratch fs;
+  fs.mid = reinterpret_cast<Cand *>(smem);
+  fs.tmp = reinterpret_cast<uint32_t *>(smem + 16384);
+  fs.S = reinterpret_cast<uint64_t *>(smem + 24576);
+  fs.bcnt = reinterpret_cast<uint32_t *>(smem + 40960);
+  fs.boff = reinterpret_cast<uint32_t *>(smem + 45056);
+  float m = -INFINITY;
+  uint32_t status = 0;
+  for (int q = 0; q < tp_world; ++q) {
+    const uint32_t *rec = recv + ((int64_t)q * p.B + row) * rec_words;
+    m = fmaxf(m, __uint_as_float(rec[0]));
+    status |= rec[2];
+  }
+  status &= ~(uint32_t)MSTAR_STATUS_EMPTY;
+  if (tid == 0) {
+    sh.tail_count = 0;
+    sh.min_gid = 0xFFFFFFFFu;
+    sh.res.token = 0;
+  }
+  __syncthreads();
+  const bool empty = !(m > -INFINITY);
+  const bool one = r.greedy || r.K == 1;
+  if (!empty) {
+    if (!one) compute_thresholds<float>(r, m, sh);
+    const float xA = one ? m : sh.xA;
+    for (int q = 0; q < tp_world; ++q) {
+      const uint32_t *rec = recv + ((int64_t)q * p.B + row) * rec_words;
+      const int n = (int)min(rec[1], (uint32_t)tp_cap);
+      for (int j = tid; j < n; j += NT) {
+        const float x = __uint_as_float(rec[4 + 2 * j]);
+        const uint32_t gid = rec[5 + 2 * j];
+        if (!(x >= xA)) continue;
+        if (one) {
+          atomicMin(&sh.min_gid, gid);
+        } else {
+          const uint32_t idx = atomicAdd(&sh.tail_count, 1u);
+          if (idx < (uint32_t)TAIL_CAP) tail[idx] = Cand{x, gid};
+        }
+      }
+    }
+    __syncthreads();
+    if (one) {
+      if (tid == 0) sh.res.token = sh.min_gid;
+    } else {
+      const int n = (int)min(sh.tail_count, (uint32_t)TAIL_CAP);
+      float u = p.uniforms ? p.uniforms[row]
+                           : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
+      tail_sort_scan(tail, n, m, fs, sh);
+      fast_resolve(r, tail, n, m, u, fs.S, sh);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t token = sh.res.token;
+    if (empty) {
+      status |= MSTAR_STATUS_EMPTY;
+      token = 0;
+    }
+    write_row_outputs(p, row, slot, token, status, !empty);
+  }
+}
+
+// ================================================================== host
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const std::string &msg) {
+  g_last_error = msg;
+  return code;
+}
+
+static int next_pow2(int v) {
+  int c = 1;
+  while (c < v) c <<= 1;
+  return c;
+}
+
+static int validate(const mstar_sampler_params_t *p) {
+  if (!p) return fail(MSTAR_ERR_INVALID, "params is NULL");
+  if (!p->logits) return fail(MSTAR_ERR_INVALID, "logits is NULL");
+  if (p->dtype != MSTAR_DTYPE_F32 && p->dtype != MSTAR_DTYPE_BF16)
+    return fail(MSTAR_ERR_INVALID, "dtype must be MSTAR_DTYPE_F32 or MSTAR_DTYPE_BF16");
+  if (p->B < 1 || p->B > 65535) return fail(MSTAR_ERR_INVALID, "B must be in [1, 65535]");
+  if (p->V < 1 || p->V > (1 << 22)) return fail(MSTAR_ERR_INVALID, "V must be in [1, 4194304]");
+  if (p->ld < p->V) return fail(MSTAR_ERR_INVALID, "ld must be >= V");
+  if (p->vocab_offset < 0 || p->vocab_offset + p->V > 0x7FFFFFFFLL)
+    return fail(MSTAR_ERR_INVALID, "vocab_offset out of range");
+  if (p->num_slots < 1) return fail(MSTAR_ERR_INVALID, "num_slots must be >= 1");
+  if (!p->slot_idx && p->num_slots < p->B)
+    return fail(MSTAR_ERR_INVALID, "without slot_idx, num_slots must be >= B");
+  if (p->hist_ids && p->seen_bits) return fail(MSTAR_ERR_INVALID, "give hist_ids or seen_bits, not both");
+  if (p->hist_ids && (!p->hist_len || p->H < 1)) return fail(MSTAR_ERR_INVALID, "hist_ids needs hist_len and H >= 1");
+  if (p->seen_bits && p->seen_words * 32 < p->vocab_offset + p->V)
+    return fail(MSTAR_ERR_INVALID, "seen_words too small for the vocabulary");
+  if (p->allowed_bits && p->allowed_words * 32 < p->vocab_offset + p->V)
+    return fail(MSTAR_ERR_INVALID, "allowed_words too small for the vocabulary");
+  if ((p->bias_ids == nullptr) != (p->bias_vals == nullptr))
+    return fail(MSTAR_ERR_INVALID, "bias_ids and bias_vals go together");
+  if (p->bias_ids && p->NB < 1) return fail(MSTAR_ERR_INVALID, "NB must be >= 1 with bias_ids");
+  if (!p->uniforms && (!p->seed || !p->offset))
+    return fail(MSTAR_ERR_INVALID, "need uniforms, or seed and offset");
+  if (!p->out_ids && !p->out_ids32) return fail(MSTAR_ERR_INVALID, "need out_ids or out_ids32");
+  if ((p->flags & MSTAR_FLAG_UPDATE_HISTORY) && !p->hist_ids)
+    return fail(MSTAR_ERR_INVALID, "UPDATE_HISTORY needs hist_ids");
+  if ((p->flags & MSTAR_FLAG_UPDATE_SEEN) && !p->seen_bits)
+    return fail(MSTAR_ERR_INVALID, "UPDATE_SEEN needs seen_bits");
+  return MSTAR_OK;
+}
+
+static int max_smem_optin() {
+  static int v = -1;
+  if (v < 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 232448;
+  }
+  return v;
+}
+
+static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Plan &pl) {
+  const int es = p->dtype == MSTAR_DTYPE_BF16 ? 2 : 4;
+  const int64_t row_bytes = (int64_t)p->V * es;
+  const int spec_max = (p->hist_ids ? p->H : (p->seen_bits ? (p->seen_cap > 0 ? p->seen_cap : 2048) : 0)) +
+                       (p->bias_ids ? p->NB : 0);
+  const int spec_cap = std::max(16, spec_max);
+  const int ht_cap = next_pow2(std::max(32, 2 * spec_cap));
+  const int static_bytes = (int)sizeof(CtaSh);
+  const int budget = max_smem_optin() - static_bytes - 1024;
+  int S = p->cluster_size;
+  auto need = [&](int s, Plan &q) {
+    int64_t slice = (p->V + s - 1) / s;
+    slice = (slice + 63) / 64 * 64;
+    q.S = s;
+    q.es = es;
+    q.slice = slice;
+    const int64_t span_bytes = slice * es + 32;
+    q.data_bytes = (int)std::max<int64_t>(FAST_SCRATCH, (span_bytes + 127) / 128 * 128);
+    const int64_t nvec = (span_bytes + 15) / 16;
+    const int64_t positions = nvec * (16 / es);
+    q.map_bytes = (int)(((positions + 31) / 32) * 4);
+    q.map_bytes = (q.map_bytes + 127) / 128 * 128;
+    q.ht_cap = ht_cap;
+    q.spec_cap = spec_cap;
+    const int work = std::max(WORK_BYTES_MIN, 2 * q.map_bytes + ht_cap * 8);
+    q.off_work = q.data_bytes;
+    q.off_spec = q.off_work + (work + 127) / 128 * 128;
+    q.off_tail = q.off_spec + (spec_cap * 8 + 127) / 128 * 128;
+    q.smem_bytes = q.off_tail + TAIL_CAP * 8;
+    q.mode = mode;
+    q.tp_cap = tp_cap;
+    q.rec_words = 4 + 2 * tp_cap;
+    return q.smem_bytes <= budget && slice * es <= (int64_t)MAX_CHUNKS * CHUNK_BYTES;
+  };
+  if (S > 0) {
+    if (S > 16) return fail(MSTAR_ERR_INVALID, "cluster_size must be <= 16");
+    if (!need(S, pl)) return fail(MSTAR_ERR_UNSUPPORTED, "row does not fit the requested cluster size");
+    return MSTAR_OK;
+  }
+  // smallest cluster whose slices fit; prefer <= 8 (portable)
+  for (int s = 1; s <= 16; ++s) {
+    if (need(s, pl)) return MSTAR_OK;
+  }
+  (void)row_bytes;
+  return fail(MSTAR_ERR_UNSUPPORTED, "row too large for a 16-CTA cluster");
+}
+
+template <typename T, int MODE>
+static int launch_T(const mstar_sampler_params_t *p, const Plan &pl, uint32_t *send, cudaStream_t st) {
+  auto kern = sampler_kernel<T, MODE>;
+  static int configured_smem[2] = {0, 0};
+  (void)configured_smem;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem_bytes);
+  if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  if (pl.S > 8) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess)
+      return fail(MSTAR_ERR_CUDA, std::string("non-portable cluster: ") + cudaGetErrorString(e));
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.S, p->B, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = pl.smem_bytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = pl.S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, *p, pl, send);
+  if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return MSTAR_OK;
+}
+
+static int launch(const mstar_sampler_params_t *p, int mode, int tp_cap, uint32_t *send, cudaStream_t st) {
+  Plan pl;
+  int rc = plan_launch(p, mode, tp_cap, pl);
+  if (rc) return rc;
+  if (p->dtype == MSTAR_DTYPE_BF16)
+    return mode == 0 ? launch_T<__nv_bfloat16, 0>(p, pl, send, st) : launch_T<__nv_bfloat16, 1>(p, pl, send, st);
+  return mode == 0 ? launch_T<float, 0>(p, pl, send, st) : launch_T<float, 1>(p, pl, send, st);
+}
+
+}  // namespace mstar
+
+using namespace mstar;
+
+extern "C" {
+
+int mstar_sampler_abi_version(void) { return MSTAR_SAMPLER_ABI_VERSION; }
+
+const char *mstar_sampler_last_error(void) { return g_last_error.c_str(); }
+
+int mstar_sampler_plan(const mstar_sampler_params_t *p, int32_t *cluster_size, int64_t *smem_bytes) {
+  int rc = validate(p);
+  if (rc) return rc;
+  Plan pl;
+  rc = plan_launch(p, 0, 0, pl);
+  if (rc) return rc;
+  if (cluster_size) *cluster_size = pl.S;
+  if (smem_bytes) *smem_bytes = pl.smem_bytes;
+  return MSTAR_OK;
+}
+
+int mstar_sampler_step(const mstar_sampler_params_t *p, void *stream) {
+  int rc = validate(p);
+  if (rc) return rc;
+  return launch(p, 0, 0, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int32_t mstar_sampler_tp_record_words(int32_t tp_cap) { return 4 + 2 * tp_cap; }
+
+int mstar_sampler_tp_local(const mstar_sampler_params_t *p, int32_t tp_cap, uint32_t *send, void *stream) {
+  mstar_sampler_params_t q = *p;
+  if (!q.out_ids && !q.out_ids32) q.out_ids32 = reinterpret_cast<int32_t *>(send);  // not written in TP mode
+  int rc = validate(&q);
+  if (rc) return rc;
+  if (!send) return fail(MSTAR_ERR_INVALID, "send is NULL");
+  if (tp_cap < 1 || tp_cap > TAIL_CAP) return fail(MSTAR_ERR_INVALID, "tp_cap must be in [1, 2048]");
+  if (q.out_x || q.out_kept || q.out_probs) return fail(MSTAR_ERR_UNSUPPORTED, "dense debug outputs are single-shard only");
+  q.flags &= ~(MSTAR_FLAG_UPDATE_HISTORY | MSTAR_FLAG_UPDATE_SEEN | MSTAR_FLAG_ADVANCE_OFFSET);
+  return launch(&q, 1, tp_cap, send, static_cast<cudaStream_t>(stream));
+}
+
+int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world, int64_t V_global,
+                           const uint32_t *recv, void *stream) {
+  int rc = validate(p);
+  if (rc) return rc;
+  if (!recv) return fail(MSTAR_ERR_INVALID, "recv is NULL");
+  if (tp_world < 1 || tp_world * tp_cap > TAIL_CAP)
+    return fail(MSTAR_ERR_INVALID, "tp_world * tp_cap must be in [1, 2048]");
+  if (V_global < p->V) return fail(MSTAR_ERR_INVALID, "V_global < V");
+  const int smem = FAST_SCRATCH + TAIL_CAP * 8;
+  cudaError_t e = cudaFuncSetAttribute(tp_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  tp_merge_kernel<<<p->B, NT, smem, static_cast<cudaStream_t>(stream)>>>(*p, tp_cap, tp_world, 4 + 2 * tp_cap,
+                                                                         V_global, recv);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return MSTAR_OK;
+}
+
+float mstar_sampler_philox_uniform(uint64_t seed, uint64_t offset) {
+  uint32_t c0 = (uint32_t)offset, c1 = (uint32_t)(offset >> 32), c2 = 0u, c3 = 0u;
+  uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+  for (int i = 0; i < 10; ++i) {
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c0, p1 = (uint64_t)0xCD9E8D57u * c2;
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ k0, n2 = (uint32_t)(p0 >> 32) ^ c3 ^ k1;
+    c1 = (uint32_t)p1;
+    c3 = (uint32_t)p0;
+    c0 = n0;
+    c2 = n2;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return (float)(c0 >> 8) * 0x1.0p-24f;
+}
+
+}  // extern "C"

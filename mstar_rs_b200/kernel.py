@@ -1,0 +1,159 @@
+"""Torch-tensor front end of the sampler kernel.
+
+`sampler_step` fills a `Params` struct from device tensors and launches one
+sampling step on the current CUDA stream.  It allocates nothing, never
+synchronises and never reads device memory on the host, so it can be called
+inside `torch.cuda.graph` capture.  Shapes, dtypes, devices and contiguity are
+validated here (before any launch) and again by the C ABI.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native as N
+
+_DT = {torch.float32: N.DTYPE_F32, torch.bfloat16: N.DTYPE_BF16}
+_U64 = (torch.int64, torch.uint64)  # seed / offset: 64-bit words, read as unsigned
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _need(t, name, dtype, dev, shape0=None, ndim=1):
+    if t is None:
+        return
+    ok = dtype if isinstance(dtype, tuple) else (dtype,)
+    if t.dtype not in ok:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.device != dev:
+        raise ValueError(f"{name} must live on {dev}, got {t.device}")
+    if t.dim() != ndim:
+        raise ValueError(f"{name} must be {ndim}-D, got shape {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if shape0 is not None and t.shape[0] < shape0:
+        raise ValueError(f"{name} has {t.shape[0]} rows, need >= {shape0}")
+
+
+def build_params(logits: torch.Tensor, *, slot_idx=None, num_slots=None, temperature=None, top_k=None,
+                 top_p=None, min_p=None, rep_pen=None, pres_pen=None, freq_pen=None, hist_ids=None,
+                 hist_len=None, seen_bits=None, seen_cap=0, bias_ids=None, bias_vals=None,
+                 allowed_bits=None, uniforms=None, seed=None, offset=None, out_ids=None, out_ids32=None,
+                 out_status=None, out_x=None, out_kept=None, out_probs=None, flags=0, cluster_size=0,
+                 vocab_offset=0) -> N.Params:
+    if logits.dim() != 2:
+        raise ValueError("logits must be [B, V]")
+    if logits.dtype not in _DT:
+        raise TypeError(f"logits must be float32 or bfloat16, got {logits.dtype}")
+    if not logits.is_cuda:
+        raise ValueError("logits must be a CUDA tensor (there is no CPU path)")
+    if logits.stride(1) != 1:
+        raise ValueError("logits rows must be contiguous")
+    dev = logits.device
+    B, V = logits.shape
+    ns = num_slots
+    if ns is None:
+        for t in (temperature, top_k, top_p, min_p, rep_pen, pres_pen, freq_pen, seed, offset, hist_len):
+            if t is not None:
+                ns = t.shape[0]
+                break
+        else:
+            ns = B
+    _need(slot_idx, "slot_idx", torch.int32, dev, B)
+    for name, t, dt in (("temperature", temperature, torch.float32), ("top_k", top_k, torch.int32),
+                        ("top_p", top_p, torch.float32), ("min_p", min_p, torch.float32),
+                        ("rep_pen", rep_pen, torch.float32), ("pres_pen", pres_pen, torch.float32),
+                        ("freq_pen", freq_pen, torch.float32), ("hist_len", hist_len, torch.int32),
+                        ("seed", seed, _U64), ("offset", offset, _U64)):
+        _need(t, name, dt, dev, ns)
+    _need(hist_ids, "hist_ids", torch.int32, dev, ns, 2)
+    _need(seen_bits, "seen_bits", torch.int32, dev, ns, 2)
+    _need(bias_ids, "bias_ids", torch.int32, dev, ns, 2)
+    _need(bias_vals, "bias_vals", torch.float32, dev, ns, 2)
+    _need(allowed_bits, "allowed_bits", torch.int32, dev, ns, 2)
+    _need(uniforms, "uniforms", torch.float32, dev, B)
+    _need(out_ids, "out_ids", torch.int64, dev, B)
+    _need(out_ids32, "out_ids32", torch.int32, dev, B)
+    _need(out_status, "out_status", torch.int32, dev, B)
+    for name, t, dt in (("out_x", out_x, torch.float32), ("out_kept", out_kept, torch.uint8),
+                        ("out_probs", out_probs, torch.float32)):
+        if t is not None:
+            _need(t, name, dt, dev, B, 2)
+            if t.shape[1] != V:
+                raise ValueError(f"{name} must be [B, V]")
+    p = N.Params()
+    p.logits = logits.data_ptr()
+    p.dtype = _DT[logits.dtype]
+    p.B, p.V, p.num_slots = B, V, ns
+    p.ld = logits.stride(0)
+    p.vocab_offset = vocab_offset
+    p.slot_idx = _ptr(slot_idx)
+    p.temperature, p.top_k, p.top_p, p.min_p = _ptr(temperature), _ptr(top_k), _ptr(top_p), _ptr(min_p)
+    p.rep_pen, p.pres_pen, p.freq_pen = _ptr(rep_pen), _ptr(pres_pen), _ptr(freq_pen)
+    p.hist_ids, p.hist_len = _ptr(hist_ids), _ptr(hist_len)
+    p.H = 0 if hist_ids is None else hist_ids.shape[1]
+    p.seen_cap = seen_cap
+    p.seen_bits = _ptr(seen_bits)
+    p.seen_words = 0 if seen_bits is None else seen_bits.shape[1]
+    p.bias_ids, p.bias_vals = _ptr(bias_ids), _ptr(bias_vals)
+    p.NB = 0 if bias_ids is None else bias_ids.shape[1]
+    p.allowed_bits = _ptr(allowed_bits)
+    p.allowed_words = 0 if allowed_bits is None else allowed_bits.shape[1]
+    p.uniforms, p.seed, p.offset = _ptr(uniforms), _ptr(seed), _ptr(offset)
+    p.out_ids, p.out_ids32, p.out_status = _ptr(out_ids), _ptr(out_ids32), _ptr(out_status)
+    p.out_x, p.out_kept, p.out_probs = _ptr(out_x), _ptr(out_kept), _ptr(out_probs)
+    p.flags = flags
+    p.cluster_size = cluster_size
+    return p
+
+
+def launch_step(p: N.Params, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        N.check(N.lib().mstar_sampler_step(ctypes.byref(p), ctypes.c_void_p(stream)), "mstar_sampler_step")
+
+
+def sampler_step(logits: torch.Tensor, **kw) -> N.Params:
+    """Launch one sampling step; returns the Params used (keep it to relaunch)."""
+    p = build_params(logits, **kw)
+    launch_step(p, logits.device)
+    return p
+
+
+def plan(logits: torch.Tensor, **kw):
+    p = build_params(logits, **kw)
+    cs, sm = N.I32(), N.I64()
+    N.check(N.lib().mstar_sampler_plan(ctypes.byref(p), ctypes.byref(cs), ctypes.byref(sm)), "mstar_sampler_plan")
+    return cs.value, sm.value
+
+
+def tp_record_words(tp_cap: int) -> int:
+    return int(N.lib().mstar_sampler_tp_record_words(tp_cap))
+
+
+def tp_local(logits: torch.Tensor, tp_cap: int, send: torch.Tensor, **kw) -> None:
+    p = build_params(logits, **kw)
+    if send.dtype != torch.int32 or not send.is_contiguous() or send.device != logits.device:
+        raise ValueError("send must be a contiguous int32 tensor on the logits device")
+    if send.numel() < logits.shape[0] * tp_record_words(tp_cap):
+        raise ValueError("send buffer too small")
+    with torch.cuda.device(logits.device):
+        stream = torch.cuda.current_stream(logits.device).cuda_stream
+        N.check(N.lib().mstar_sampler_tp_local(ctypes.byref(p), tp_cap, ctypes.c_void_p(send.data_ptr()),
+                                               ctypes.c_void_p(stream)), "mstar_sampler_tp_local")
+
+
+def tp_merge(logits: torch.Tensor, tp_cap: int, tp_world: int, V_global: int, recv: torch.Tensor, **kw) -> None:
+    p = build_params(logits, **kw)
+    if recv.dtype != torch.int32 or not recv.is_contiguous() or recv.device != logits.device:
+        raise ValueError("recv must be a contiguous int32 tensor on the logits device")
+    if recv.numel() < tp_world * logits.shape[0] * tp_record_words(tp_cap):
+        raise ValueError("recv buffer too small")
+    with torch.cuda.device(logits.device):
+        stream = torch.cuda.current_stream(logits.device).cuda_stream
+        N.check(N.lib().mstar_sampler_tp_merge(ctypes.byref(p), tp_cap, tp_world, V_global,
+                                               ctypes.c_void_p(recv.data_ptr()), ctypes.c_void_p(stream)),
+                "mstar_sampler_tp_merge")

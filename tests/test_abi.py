@@ -1,0 +1,95 @@
+"""CPU: the C-ABI library builds, loads without a GPU, exports every symbol
+include/mstar_sampler.h declares, matches the ctypes struct layout, and
+rejects invalid arguments on the host before any launch."""
+import ctypes
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "mstar_sampler.h")
+
+
+@pytest.fixture(scope="module")
+def L():
+    from mstar_rs_b200 import _native, build
+
+    build.build()
+    return _native.lib()
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(mstar_\w+)\s*\(", text)))
+
+
+def test_exports_every_declared_symbol(L):
+    names = declared_functions()
+    assert len(names) >= 8
+    for n in names:
+        assert hasattr(L, n), f"library does not export {n}"
+    from mstar_rs_b200 import _native
+
+    assert set(_native.EXPORTS) == set(names)
+
+
+def test_abi_version(L):
+    assert L.mstar_sampler_abi_version() == 1
+
+
+def test_struct_layout_matches_header():
+    from mstar_rs_b200._native import Params
+
+    fields = [f[0] for f in Params._fields_]
+    src = ["#include <stdio.h>", "#include <stddef.h>", '#include "mstar_sampler.h"', "int main(void){",
+           'printf("%zu\\n", sizeof(mstar_sampler_params_t));']
+    for f in fields:
+        src.append(f'printf("%zu\\n", offsetof(mstar_sampler_params_t, {f}));')
+    src.append("return 0;}")
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        open(c, "w").write("\n".join(src))
+        exe = os.path.join(d, "t")
+        subprocess.check_call(["gcc", "-I", os.path.join(ROOT, "include"), "-o", exe, c])
+        out = [int(v) for v in subprocess.check_output([exe]).split()]
+    assert out[0] == ctypes.sizeof(Params)
+    for f, off in zip(fields, out[1:]):
+        assert getattr(Params, f).offset == off, f
+
+
+def test_host_philox_matches_oracle(L, oracle_lib):
+    from mstar_rs_b200 import _native
+
+    ol = oracle_lib.lib()
+    for seed, off in [(0, 0), (1, 2), (2**63 + 5, 2**40 + 3), (123456789, 987654321)]:
+        assert _native.philox_uniform(seed, off) == ol.orc_philox_uniform(seed, off)
+
+
+def test_invalid_arguments_rejected_on_host(L):
+    from mstar_rs_b200 import _native
+
+    p = _native.Params()
+    assert L.mstar_sampler_step(ctypes.byref(p), None) == _native.ERR_INVALID
+    assert b"logits" in L.mstar_sampler_last_error()
+    p.logits = 0x1000
+    p.dtype = 7
+    assert L.mstar_sampler_step(ctypes.byref(p), None) == _native.ERR_INVALID
+    p.dtype, p.B, p.V, p.ld, p.num_slots = 0, 4, 100, 50, 4
+    assert L.mstar_sampler_step(ctypes.byref(p), None) == _native.ERR_INVALID
+    assert b"ld" in L.mstar_sampler_last_error()
+    p.ld = 100
+    assert L.mstar_sampler_step(ctypes.byref(p), None) == _native.ERR_INVALID  # no uniforms / seed
+    assert L.mstar_sampler_tp_record_words(50) == 104
+
+
+def test_python_front_end_rejects_cpu_tensors():
+    import torch
+
+    from mstar_rs_b200 import kernel
+
+    with pytest.raises(ValueError, match="CUDA"):
+        kernel.build_params(torch.zeros(2, 10))
