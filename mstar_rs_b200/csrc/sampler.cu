@@ -2,25 +2,29 @@
 //
 // One thread-block cluster of S CTAs samples one row.  Each CTA owns a
 // contiguous slice of the row, pulls it into shared memory with 1-D bulk
-// copies (cp.async.bulk + mbarrier, one barrier per 16 KB chunk) and keeps it
-// resident for the whole step, so HBM is read exactly once:
+// copies (cp.async.bulk + mbarrier, one barrier per 32 KB chunk, all issued
+// by one thread before anything else) and keeps it resident for the whole
+// step, so HBM is read exactly once:
 //
-//   setup     penalised / biased ids of the slice go into a small hash table
-//             (the "specials"); their final values are computed from global
-//             memory while the bulk copies are in flight.
-//   pass A    per chunk as it lands: disallowed ids -> -inf, specials -> NaN
-//             (they are handled from the special list), running max of the
-//             raw values (bf16x2 max / fmax).
-//   cluster   row max m = max over CTAs (DSMEM); every CTA runs the same
-//             32-ary search for x_A, the smallest value whose weight is
-//             positive and passes min_p, and for the raw threshold r_A with
-//             f(r_A) >= x_A (f = the temperature transform, monotone).
-//   pass C    vectors whose max is below r_A are skipped after one compare;
-//             survivors (x, id) are pushed into the leader CTA's tail buffer
-//             through DSMEM atomics.
-//   tail      the leader bucket-sorts the candidates by (x desc, id asc),
-//             computes the fixed-point weights and their exact u64 prefix
-//             sums, and resolves top_k / top_p / the inverse-CDF draw.
+//   setup     while the copies fly: the slice's penalised / biased ids go
+//             into a small hash table and a bitmap, disallowed ids into a
+//             second bitmap.
+//   pass A    per chunk as it lands: disallowed ids -> -inf, penalised /
+//             biased ids ("specials") -> NaN after their raw value is saved
+//             in the hash table, running max of the raw values.  The
+//             specials' final values are then computed from the table.
+//   cluster   row max m = max over the CTAs (DSMEM).  A conservative value
+//             threshold theta <= x_A (x_A = smallest value with positive
+//             weight passing min_p) is picked from m and checked with the
+//             spec's exponential.
+//   pass C    vectors whose transformed max is below theta are skipped after
+//             one compare; the few survivors pass the exact predicate and go
+//             into a CTA-local candidate list.
+//   tail      the leader pulls every list over DSMEM, counts candidates and
+//             weight mass into 2048 buckets of the order key, scans the
+//             buckets, ranks each candidate inside its bucket, and resolves
+//             top_k / top_p / the inverse-CDF draw from exact u64 prefix sums
+//             of the fixed-point weights.
 //   general   rows whose candidate set exceeds the tail capacity run a
 //             leader-driven loop of histogram (count + mass) and compaction
 //             rounds over the still-resident slices until every boundary is
@@ -46,17 +50,22 @@ namespace cg = cooperative_groups;
 
 namespace mstar {
 
-constexpr int NT = 512;            // threads per CTA
+constexpr int NT = 512;             // threads per CTA
 constexpr int NWARP = NT / 32;
-constexpr int TAIL_CAP = 2048;     // candidates the fast tail sorts
-constexpr int GCAP = 1024;         // candidates per locate round of the general path
-constexpr int NBIN = 1024;         // histogram bins per round
-constexpr int NBK = 1024;          // buckets of the tail sort
-constexpr int CHUNK_BYTES = 16384; // bulk-copy granule (one mbarrier each)
-constexpr int MAX_CHUNKS = 16;     // slice data <= 256 KB
-constexpr int MAX_ROUNDS = 96;     // bound on general-path rounds
-constexpr int WORK_BYTES_MIN = 40 * 1024;
-constexpr int FAST_SCRATCH = 48 * 1024;
+constexpr int TAIL_CAP = 2048;      // candidates the fast tail resolves
+constexpr int LCAP = 2048;          // CTA-local candidate list
+constexpr int GCAP = 1024;          // candidates per locate round of the general path
+constexpr int NBIN = 1024;          // histogram bins per general-path round
+constexpr int NBK = 2048;           // buckets of the fast tail
+constexpr int GBK = 1024;           // buckets of the general-path sort
+constexpr int CHUNK_BYTES = 32768;  // bulk-copy granule (one mbarrier each)
+constexpr int MAX_CHUNKS = 8;       // slice data <= 256 KB
+constexpr int MAX_ROUNDS = 96;      // bound on general-path rounds
+constexpr int BIAS_SMEM = 256;      // bias entries staged in shared memory
+constexpr int QCAP = 2048;          // vectors queued by the candidate scan before draining
+constexpr int GQCAP = 1024;         // vectors queued per general-path round
+constexpr int WORK_BYTES_MIN = 52 * 1024;
+constexpr int LEAN_SCRATCH = 72 * 1024;  // fast-tail scratch (the leader's data region)
 constexpr unsigned kWaitLimit = 1u << 24;
 
 struct __align__(8) Cand {
@@ -69,11 +78,11 @@ struct Plan {
   int32_t S;
   int32_t es;
   int64_t slice;       // elements per CTA slice
-  int32_t data_bytes;  // slice data (>= FAST_SCRATCH: reused by the fast tail)
+  int32_t data_bytes;  // slice data (>= LEAN_SCRATCH: reused by the fast tail)
   int32_t map_bytes;   // each of the two bitmaps
   int32_t ht_cap;      // hash table slots (power of two)
   int32_t spec_cap;    // special list entries
-  int32_t off_work, off_spec, off_tail;
+  int32_t off_work, off_spec, off_lcand, off_bias;
   int32_t smem_bytes;
   int32_t mode;        // 0 = step, 1 = TP local
   int32_t tp_cap, rec_words;
@@ -101,9 +110,9 @@ enum : int { Q_COUNT = 0, Q_LASTLT = 1, Q_POINT = 2 };
 
 struct Planner {
   int state;
-  int stage;      // 0 = A boundary, 1 = top-p boundary, 2 = draw
+  int stage;  // 0 = A boundary, 1 = top-p boundary, 2 = draw
   int qkind;
-  int level;      // 0 = L1 arrays, 1 = REF arrays
+  int level;  // 0 = L1 arrays, 1 = REF arrays
   uint64_t lo, hi;
   int shift, nbins;
   uint64_t base_c, base_m;
@@ -113,13 +122,10 @@ struct Planner {
   double thr;
   uint64_t cbase_c, cbase_m;  // stats before the compacted bin
   uint64_t N, Wv, WA, WK, ckA, ckK;
-  uint32_t token;
-  int done;
-  int found_bin;
 };
 
 struct Result {
-  float m, xA;
+  float m, theta;
   uint64_t WK, ckK;
   uint32_t token;
   uint32_t status;
@@ -132,14 +138,14 @@ struct CtaSh {
   float red_f[NWARP];
   uint64_t red_u64[NWARP];
   uint64_t red_u64b[NWARP];
-  float cta_max;        // read by every CTA of the cluster
-  uint32_t tail_count;  // leader: pushes into its tail buffer
-  uint32_t min_gid;     // leader: lowest id at the max (greedy / top-1)
-  uint32_t status;      // leader: status bits (remote atomicOr)
+  float cta_max;     // read by every CTA of the cluster
+  uint32_t nloc;     // CTA-local candidate count (read by the leader)
+  uint32_t min_gid;  // lowest id at the max in this CTA (greedy / top-1)
+  uint32_t status;   // status bits of this CTA
   uint32_t n_spec;
   uint32_t ht_fail;
-  float m, xA, rA;
-  int decision;
+  uint32_t qcount;
+  float theta;
   int tp_ovf;
   int bcast_i;
   uint64_t bcast_u64;
@@ -173,7 +179,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   for (unsigned i = 0; i < kWaitLimit; ++i) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000000;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
         : "r"(a), "r"(parity)
@@ -201,6 +207,12 @@ struct Elem<float> {
     const uint32_t w = j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
     return __uint_as_float(w);
   }
+  static __device__ __forceinline__ void set_bits(uint4 &v, int j, uint32_t bits) {
+    if (j == 0) v.x = bits;
+    else if (j == 1) v.y = bits;
+    else if (j == 2) v.z = bits;
+    else v.w = bits;
+  }
   static __device__ __forceinline__ float vmax(const uint4 &v) {
     return fmaxf(fmaxf(__uint_as_float(v.x), __uint_as_float(v.y)),
                  fmaxf(__uint_as_float(v.z), __uint_as_float(v.w)));
@@ -208,17 +220,24 @@ struct Elem<float> {
   static __device__ __forceinline__ float load(const void *row, int64_t i) {
     return static_cast<const float *>(row)[i];
   }
-  static __device__ __forceinline__ uint32_t neg_inf_bits() { return 0xFF800000u; }
-  static __device__ __forceinline__ void patch(uint4 &v, uint32_t mbits, uint32_t sbits) {
-    uint32_t *w = reinterpret_cast<uint32_t *>(&v);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if ((mbits >> j) & 1u) w[j] = 0xFF800000u;
-      else if ((sbits >> j) & 1u) w[j] = 0x7FC00000u;
-    }
+  static __device__ __forceinline__ uint32_t load_bits(const void *row, int64_t i) {
+    return static_cast<const uint32_t *>(row)[i];
   }
-  static __device__ __forceinline__ uint32_t bits_of(const uint32_t *map, int k) {
-    return (map[k >> 3] >> ((k & 7) * 4)) & 0xFu;
+  static __device__ __forceinline__ uint32_t neg_inf() { return 0xFF800000u; }
+  static __device__ __forceinline__ uint32_t nan_bits() { return 0x7FC00000u; }
+  static __device__ __forceinline__ uint32_t bits_of(const uint8_t *map, int k) {
+    return (map[k >> 1] >> ((k & 1) * 4)) & 0xFu;
+  }
+  // lanes whose bit is set become -inf
+  static __device__ __forceinline__ uint4 mask_out(uint4 v, uint32_t b) {
+    v.x = (b & 1u) ? 0xFF800000u : v.x;
+    v.y = (b & 2u) ? 0xFF800000u : v.y;
+    v.z = (b & 4u) ? 0xFF800000u : v.z;
+    v.w = (b & 8u) ? 0xFF800000u : v.w;
+    return v;
+  }
+  static __device__ __forceinline__ float smem_elem(const uint8_t *data, int64_t pos) {
+    return reinterpret_cast<const float *>(data)[pos];
   }
 };
 
@@ -228,6 +247,15 @@ struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ float get(const uint4 &v, int j) {
     const uint32_t w = (j >> 1) == 0 ? v.x : (j >> 1) == 1 ? v.y : (j >> 1) == 2 ? v.z : v.w;
     return __uint_as_float((j & 1) ? (w & 0xFFFF0000u) : (w << 16));
+  }
+  static __device__ __forceinline__ void set_bits(uint4 &v, int j, uint32_t bits) {
+    const uint32_t hi = (j & 1) ? 0x0000FFFFu : 0xFFFF0000u;  // half to keep
+    const uint32_t put = (j & 1) ? (bits << 16) : (bits & 0xFFFFu);
+    const int w = j >> 1;
+    if (w == 0) v.x = (v.x & hi) | put;
+    else if (w == 1) v.y = (v.y & hi) | put;
+    else if (w == 2) v.z = (v.z & hi) | put;
+    else v.w = (v.w & hi) | put;
   }
   static __device__ __forceinline__ float vmax(const uint4 &v) {
     __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162 *>(&v.x);
@@ -241,30 +269,30 @@ struct Elem<__nv_bfloat16> {
     const uint16_t h = static_cast<const uint16_t *>(row)[i];
     return __uint_as_float((uint32_t)h << 16);
   }
-  static __device__ __forceinline__ void patch(uint4 &v, uint32_t mbits, uint32_t sbits) {
-    uint16_t *h = reinterpret_cast<uint16_t *>(&v);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if ((mbits >> j) & 1u) h[j] = 0xFF80u;
-      else if ((sbits >> j) & 1u) h[j] = 0x7FC0u;
-    }
+  static __device__ __forceinline__ uint32_t load_bits(const void *row, int64_t i) {
+    return static_cast<const uint16_t *>(row)[i];
   }
-  static __device__ __forceinline__ uint32_t bits_of(const uint32_t *map, int k) {
-    return (map[k >> 2] >> ((k & 3) * 8)) & 0xFFu;
+  static __device__ __forceinline__ uint32_t neg_inf() { return 0xFF80u; }
+  static __device__ __forceinline__ uint32_t nan_bits() { return 0x7FC0u; }
+  static __device__ __forceinline__ uint32_t bits_of(const uint8_t *map, int k) { return map[k]; }
+  static __device__ __forceinline__ uint32_t mask2(uint32_t w, uint32_t b2) {
+    const uint32_t m = ((b2 & 1u) ? 0x0000FFFFu : 0u) | ((b2 & 2u) ? 0xFFFF0000u : 0u);
+    return (w & ~m) | (0xFF80FF80u & m);
+  }
+  // lanes whose bit is set become -inf
+  static __device__ __forceinline__ uint4 mask_out(uint4 v, uint32_t b) {
+    v.x = mask2(v.x, b);
+    v.y = mask2(v.y, b >> 2);
+    v.z = mask2(v.z, b >> 4);
+    v.w = mask2(v.w, b >> 6);
+    return v;
+  }
+  static __device__ __forceinline__ float smem_elem(const uint8_t *data, int64_t pos) {
+    return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(data)[pos] << 16);
   }
 };
 
 // ------------------------------------------------------- block reductions
-
-__device__ __forceinline__ uint32_t block_max_u32(uint32_t v, CtaSh &sh) {
-  for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(~0u, v, o));
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) sh.red_u32[threadIdx.x >> 5] = v;
-  __syncthreads();
-  uint32_t r = sh.red_u32[0];
-  for (int i = 1; i < NWARP; ++i) r = max(r, sh.red_u32[i]);
-  return r;
-}
 
 __device__ __forceinline__ float block_max_f32(float v, CtaSh &sh) {
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(~0u, v, o));
@@ -273,6 +301,16 @@ __device__ __forceinline__ float block_max_f32(float v, CtaSh &sh) {
   __syncthreads();
   float r = sh.red_f[0];
   for (int i = 1; i < NWARP; ++i) r = fmaxf(r, sh.red_f[i]);
+  return r;
+}
+
+__device__ __forceinline__ uint32_t block_min_u32(uint32_t v, CtaSh &sh) {
+  for (int o = 16; o; o >>= 1) v = min(v, __shfl_xor_sync(~0u, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sh.red_u32[threadIdx.x >> 5] = v;
+  __syncthreads();
+  uint32_t r = sh.red_u32[0];
+  for (int i = 1; i < NWARP; ++i) r = min(r, sh.red_u32[i]);
   return r;
 }
 
@@ -316,23 +354,53 @@ __device__ __forceinline__ uint64_t block_exscan_u64(uint64_t v, uint64_t &total
   return off + inc - v;
 }
 
+// Two exclusive block scans at once (count and mass).
+__device__ __forceinline__ void block_exscan2_u64(uint64_t a, uint64_t b, uint64_t &pa, uint64_t &pb, uint64_t &ta,
+                                                  uint64_t &tb, CtaSh &sh) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  uint64_t ia = a, ib = b;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t sa = __shfl_up_sync(~0u, (unsigned long long)ia, o);
+    const uint64_t sb = __shfl_up_sync(~0u, (unsigned long long)ib, o);
+    if (lane >= o) {
+      ia += sa;
+      ib += sb;
+    }
+  }
+  __syncthreads();
+  if (lane == 31) {
+    sh.red_u64[wid] = ia;
+    sh.red_u64b[wid] = ib;
+  }
+  __syncthreads();
+  uint64_t oa = 0, ob = 0, sa_ = 0, sb_ = 0;
+  for (int i = 0; i < NWARP; ++i) {
+    const uint64_t x = sh.red_u64[i], y = sh.red_u64b[i];
+    if (i < wid) {
+      oa += x;
+      ob += y;
+    }
+    sa_ += x;
+    sb_ += y;
+  }
+  pa = oa + ia - a;
+  pb = ob + ib - b;
+  ta = sa_;
+  tb = sb_;
+}
+
 // ---------------------------------------------------------- row context
 
 struct Row {
-  const mstar_sampler_params_t *p;
-  int row, slot;
-  int64_t V, gbase;         // vocab_offset
-  const void *rowp;         // logits row
+  const void *rowp;
+  int64_t V, gbase;  // gbase = vocab_offset
   float T, invT, Mp, P;
-  int K;                    // 0 = off
+  int K;             // 0 = off
   bool greedy, topk, minp, topp;
 };
 
-__device__ __forceinline__ void row_init(Row &r, const mstar_sampler_params_t &p, int row, int slot) {
-  r.p = &p;
-  r.row = row;
-  r.slot = slot;
-  r.V = p.V;
+__device__ __forceinline__ void row_init(Row &r, const mstar_sampler_params_t &p, int row, int slot, int64_t V) {
+  r.V = V;
   r.gbase = p.vocab_offset;
   const int es = p.dtype == MSTAR_DTYPE_BF16 ? 2 : 4;
   r.rowp = static_cast<const uint8_t *>(p.logits) + (int64_t)row * p.ld * es;
@@ -342,7 +410,7 @@ __device__ __forceinline__ void row_init(Row &r, const mstar_sampler_params_t &p
   const int K = p.top_k ? p.top_k[slot] : 0;
   r.topk = K > 0 && (int64_t)K < r.V;
   r.K = r.topk ? K : 0;
-  float Mp = p.min_p ? p.min_p[slot] : 0.0f;
+  const float Mp = p.min_p ? p.min_p[slot] : 0.0f;
   r.minp = Mp > 0.0f;
   r.Mp = fminf(Mp, 1.0f);
   r.P = p.top_p ? p.top_p[slot] : 1.0f;
@@ -356,110 +424,301 @@ __device__ __forceinline__ bool pred_A(const Row &r, float x, float m) {
   return !r.minp || e >= r.Mp;
 }
 
-// Smallest key in (lo, hi] with pred true, given pred(lo) false, pred(hi)
-// true and pred monotone.  Called by one full warp.
-template <class F>
-__device__ __forceinline__ uint32_t warp_search(uint32_t lo, uint32_t hi, F pred) {
+__device__ __forceinline__ float prev_float(float t) {
+  if (t != t || t == -INFINITY) return t;
+  if (t == 0.0f) return -1.4e-45f;
+  const int b = __float_as_int(t);
+  return __int_as_float(t > 0.0f ? b - 1 : b + 1);
+}
+
+// Conservative value threshold: every x below it fails the value-A
+// predicate.  Guesses of the boundary, each checked with the spec's own
+// exponential at prev_float(theta) (the predicate is monotone in x); lanes
+// 0-2 try the positive-weight bound, lanes 3-5 the min_p bound.  Called by
+// one full warp; every lane returns the same value.
+__device__ float choose_theta(const Row &r, float m) {
+  if (r.greedy || r.K == 1) return m;
   const int lane = threadIdx.x & 31;
-  for (int it = 0; it < 64 && hi - lo > 1; ++it) {
-    const uint64_t span = (uint64_t)(hi - lo);
-    uint32_t probe = lo + (uint32_t)((span * (uint64_t)(lane + 1)) >> 5);
-    if (probe <= lo) probe = lo + 1;
-    const bool ok = pred(probe);
-    const unsigned mask = __ballot_sync(~0u, ok);
-    const int f = __ffs(mask) - 1;  // lane 31 probes hi, so mask != 0
-    const uint32_t nhi = __shfl_sync(~0u, probe, f);
-    const uint32_t nlo = __shfl_sync(~0u, probe, f > 0 ? f - 1 : 0);
-    if (f > 0) lo = nlo;
-    hi = nhi;
+  float t = -INFINITY;
+  bool ok = false;
+  if (lane < 3) {
+    const float off = lane == 0 ? -23.25f : lane == 1 ? -25.0f : -32.0f;
+    t = __fadd_rn(m, off);
+    ok = spec_w_from_e(spec_e(prev_float(t), m)) == 0;
+  } else if (lane < 6 && r.minp) {
+    const float off = lane == 3 ? -0.002f : lane == 4 ? -0.1f : -1.0f;
+    t = __fadd_rn(m, __fadd_rn(logf(r.Mp), off));
+    ok = !(spec_e(prev_float(t), m) >= r.Mp);
   }
-  return hi;
-}
-
-__device__ __forceinline__ uint32_t okey16(uint32_t h) {
-  if (h == 0x8000u) h = 0u;
-  return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
-}
-__device__ __forceinline__ float okey16_inv(uint32_t k) {
-  const uint32_t h = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
-  return __uint_as_float(h << 16);
-}
-
-// Thresholds: x_A (exact value-A boundary) and the raw threshold r_A.
-template <typename T>
-__device__ void compute_thresholds(const Row &r, float m, CtaSh &sh) {
-  if (threadIdx.x < 32) {
-    float xA;
-    if (r.greedy || r.K == 1) {
-      xA = m;
-    } else {
-      const uint32_t kh = okey(m);
-      const uint32_t kl = okey(-INFINITY);
-      const uint32_t k = warp_search(kl, kh, [&](uint32_t key) { return pred_A(r, okey_inv(key), m); });
-      xA = okey_inv(k);
-    }
-    // raw threshold: smallest raw value whose transform reaches xA
-    float rA;
-    auto f = [&](float raw) { return r.greedy ? raw : __fmul_rn(raw, r.invT); };
-    if (sizeof(T) == 2) {
-      const uint32_t lo = okey16(0xFF80u), hi = okey16(0x7F80u);
-      const uint32_t k = warp_search(lo, hi, [&](uint32_t key) { return f(okey16_inv(key)) >= xA; });
-      rA = okey16_inv(k);
-      if (!(f(rA) >= xA)) rA = INFINITY;
-    } else {
-      const uint32_t lo = okey(-INFINITY), hi = okey(INFINITY);
-      const uint32_t k = warp_search(lo, hi, [&](uint32_t key) { return f(okey_inv(key)) >= xA; });
-      rA = okey_inv(k);
-      if (!(f(rA) >= xA)) rA = INFINITY;
-    }
-    if (threadIdx.x == 0) {
-      sh.xA = xA;
-      sh.rA = rA;
-    }
-  }
-  __syncthreads();
-}
-
-// Iterate every element of value-A held by this CTA: resident vectors with
-// raw >= rA, and specials with x >= xA.  fn(x, gid).
-template <typename T, typename F>
-__device__ __forceinline__ void for_each_value(const uint4 *data, int nvec, int64_t pos0_gid, const Cand *spec,
-                                               int nspec, float rA, float xA, bool greedy, float invT, F &&fn) {
-  constexpr int VEC = Elem<T>::VEC;
-  for (int k = threadIdx.x; k < nvec; k += NT) {
-    const uint4 v = data[k];
-    if (Elem<T>::vmax(v) >= rA) {
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        const float raw = Elem<T>::get(v, j);
-        if (raw >= rA) {
-          const float x = greedy ? raw : __fmul_rn(raw, invT);
-          fn(x, (uint32_t)(pos0_gid + (int64_t)k * VEC + j));
-        }
-      }
-    }
-  }
-  for (int i = threadIdx.x; i < nspec; i += NT) {
-    const Cand c = spec[i];
-    if (c.x >= xA) fn(c.x, c.gid);
-  }
+  const unsigned bal = __ballot_sync(~0u, ok);
+  const unsigned bw = bal & 7u, bm = (bal >> 3) & 7u;
+  const float tw = bw ? __shfl_sync(~0u, t, __ffs(bw) - 1) : -INFINITY;
+  const float tm = bm ? __shfl_sync(~0u, t, __ffs(bm) + 2) : -INFINITY;
+  return fmaxf(tw, tm);
 }
 
 __device__ __forceinline__ uint64_t ckey(uint32_t km, float x, uint32_t gid) {
   return ((uint64_t)(km - okey(x)) << 32) | gid;
 }
 
-// ------------------------------------------------------------- tail sort
+// Resident slice view used by the scans: data vectors plus the two bitmaps
+// (disallowed / outside positions, penalised-or-biased positions); lanes
+// flagged in either bitmap read as -inf.
+struct Slice {
+  const uint4 *data;
+  const uint8_t *mmask, *mspec;
+  int nvec;
+  bool has_spec;
+  int64_t pos0_gid;
+};
+
+template <typename T>
+__device__ __forceinline__ uint4 load_masked(const Slice &sl, int k) {
+  uint4 v = sl.data[k];
+  uint32_t b = Elem<T>::bits_of(sl.mmask, k);
+  if (sl.has_spec) b |= Elem<T>::bits_of(sl.mspec, k);
+  return b ? Elem<T>::mask_out(v, b) : v;
+}
+
+// Iterate the value-A elements this CTA holds (resident vectors and the
+// special list), applying the exact predicate; fn(x, gid).  Phase 1 streams
+// every vector and queues (warp-aggregated) the few whose transformed max
+// reaches theta; phase 2 drains the queue one vector per thread.  If the
+// queue overflows, phase 2 rescans everything directly.  Block-wide.
+template <typename T, typename F>
+__device__ __forceinline__ void for_each_value(const Slice &sl, const Cand *spec, int nspec, const Row &r, float m,
+                                               float theta, int *queue, int qcap, uint32_t *qcount, F &&fn) {
+  constexpr int VEC = Elem<T>::VEC;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) *qcount = 0;
+  __syncthreads();
+  const int rounds = (sl.nvec + NT * 4 - 1) / (NT * 4);
+  for (int rd = 0; rd < rounds; ++rd) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = rd * NT * 4 + u * NT + threadIdx.x;
+      if (k < sl.nvec) v[u] = load_masked<T>(sl, k);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = rd * NT * 4 + u * NT + threadIdx.x;
+      bool pass = false;
+      if (k < sl.nvec) {
+        const float vm = Elem<T>::vmax(v[u]);
+        pass = (r.greedy ? vm : __fmul_rn(vm, r.invT)) >= theta;
+      }
+      const unsigned bal = __ballot_sync(~0u, pass);
+      if (bal) {
+        const int leader = __ffs(bal) - 1;
+        uint32_t base = 0;
+        if (lane == leader) base = atomicAdd(qcount, (uint32_t)__popc(bal));
+        base = __shfl_sync(~0u, base, leader);
+        if (pass) {
+          const uint32_t idx = base + (uint32_t)__popc(bal & ((1u << lane) - 1u));
+          if (idx < (uint32_t)qcap) queue[idx] = k;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t nq = *qcount;
+  auto scan = [&](int k) {
+    const uint4 v = load_masked<T>(sl, k);
+    const uint32_t gid0 = (uint32_t)(sl.pos0_gid + (int64_t)k * VEC);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float raw = Elem<T>::get(v, j);
+      const float x = r.greedy ? raw : __fmul_rn(raw, r.invT);
+      if (x >= theta && pred_A(r, x, m)) fn(x, gid0 + (uint32_t)j);
+    }
+  };
+  if (nq <= (uint32_t)qcap) {
+    for (int i = threadIdx.x; i < (int)nq; i += NT) scan(queue[i]);
+  } else {
+    for (int k = threadIdx.x; k < sl.nvec; k += NT) {
+      const float vm = Elem<T>::vmax(load_masked<T>(sl, k));
+      if ((r.greedy ? vm : __fmul_rn(vm, r.invT)) >= theta) scan(k);
+    }
+  }
+  for (int i = threadIdx.x; i < nspec; i += NT) {
+    const Cand c = spec[i];
+    if (c.x >= theta && pred_A(r, c.x, m)) fn(c.x, c.gid);
+  }
+}
+
+// ------------------------------------------------------------- fast tail
+
+struct LeanScratch {
+  Cand *cand;       // [TAIL_CAP]
+  uint32_t *bcnt;   // [NBK]
+  uint64_t *bmass;  // [NBK]
+  uint64_t *skey;   // [TAIL_CAP]
+  uint64_t *sw;     // [TAIL_CAP]
+};
+
+__device__ __forceinline__ LeanScratch lean_scratch(uint8_t *base) {
+  LeanScratch s;
+  s.cand = reinterpret_cast<Cand *>(base);
+  s.bcnt = reinterpret_cast<uint32_t *>(base + TAIL_CAP * 8);
+  s.bmass = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 8 + NBK * 4);
+  s.skey = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 8 + NBK * 12);
+  s.sw = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 16 + NBK * 12);
+  return s;
+}
+
+// Resolve top_k / top_p / the draw over n value-A candidates s.cand[0..n)
+// (any order; all x >= theta; all of A among them).  Bucket counting on the
+// order key, exclusive scans of bucket counts and masses, rank inside the
+// bucket, then each query is answered by the one candidate that straddles
+// it.  Block-wide.  With rec != nullptr (TP shard) the first `nemit`
+// candidates in order are written to rec instead.
+__device__ void lean_tail(const Row &r, int n, float m, float theta, float u, const LeanScratch &s, CtaSh &sh,
+                          uint32_t *rec, int nemit) {
+  constexpr int PER = TAIL_CAP / NT;
+  constexpr int BPT = NBK / NT;
+  const uint32_t km = okey(m);
+  const uint32_t Dth = km - okey(theta);
+  const int bits = Dth ? 32 - __clz((int)Dth) : 0;
+  const int dsh = bits > 11 ? bits - 11 : 0;
+  for (int b = threadIdx.x; b < NBK; b += NT) {
+    s.bcnt[b] = 0;
+    s.bmass[b] = 0;
+  }
+  __syncthreads();
+  uint64_t key[PER], w[PER];
+  uint32_t bk[PER], pos[PER];
+  float xv[PER];
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int i = threadIdx.x + q * NT;
+    if (i < n) {
+      const Cand c = s.cand[i];
+      const uint32_t d = km - okey(c.x);
+      key[q] = ((uint64_t)d << 32) | c.gid;
+      w[q] = spec_w_from_e(spec_e(c.x, m));
+      xv[q] = c.x;
+      bk[q] = min(d >> dsh, (uint32_t)(NBK - 1));
+      pos[q] = atomicAdd(&s.bcnt[bk[q]], 1u);
+      atomicAdd((unsigned long long *)&s.bmass[bk[q]], (unsigned long long)w[q]);
+    }
+  }
+  __syncthreads();
+  uint64_t tot_c, tot_m;
+  {
+    uint32_t lc[BPT];
+    uint64_t lm[BPT], sc = 0, sm = 0;
+#pragma unroll
+    for (int q = 0; q < BPT; ++q) {
+      lc[q] = s.bcnt[threadIdx.x * BPT + q];
+      lm[q] = s.bmass[threadIdx.x * BPT + q];
+      sc += lc[q];
+      sm += lm[q];
+    }
+    uint64_t pc, pm;
+    block_exscan2_u64(sc, sm, pc, pm, tot_c, tot_m, sh);
+#pragma unroll
+    for (int q = 0; q < BPT; ++q) {  // inclusive prefixes
+      pc += lc[q];
+      pm += lm[q];
+      s.bcnt[threadIdx.x * BPT + q] = (uint32_t)pc;
+      s.bmass[threadIdx.x * BPT + q] = pm;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int i = threadIdx.x + q * NT;
+    if (i < n) {
+      const uint32_t lo = bk[q] ? s.bcnt[bk[q] - 1] : 0u;
+      s.skey[lo + pos[q]] = key[q];
+      s.sw[lo + pos[q]] = w[q];
+    }
+  }
+  __syncthreads();
+  uint32_t rank[PER];
+  uint64_t Sx[PER];
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int i = threadIdx.x + q * NT;
+    rank[q] = 0xFFFFFFFFu;
+    Sx[q] = 0;
+    if (i < n) {
+      const uint32_t lo = bk[q] ? s.bcnt[bk[q] - 1] : 0u, hi = s.bcnt[bk[q]];
+      uint32_t rin = 0;
+      uint64_t min_ = 0;
+      for (uint32_t j = lo; j < hi; ++j) {
+        if (s.skey[j] < key[q]) {
+          ++rin;
+          min_ += s.sw[j];
+        }
+      }
+      rank[q] = lo + rin;
+      Sx[q] = (bk[q] ? s.bmass[bk[q] - 1] : 0ull) + min_;
+    }
+  }
+  const int nA = r.topk ? min(n, r.K) : n;
+  if (rec) {  // TP shard: emit the first nemit candidates in order
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int i = threadIdx.x + q * NT;
+      if (i < n && (int)rank[q] < nemit) {
+        rec[4 + 2 * rank[q]] = __float_as_uint(xv[q]);
+        rec[5 + 2 * rank[q]] = (uint32_t)(key[q] & 0xFFFFFFFFu);
+      }
+    }
+    __syncthreads();
+    return;
+  }
+  uint64_t WA = tot_m;
+  if (nA < n) {
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int i = threadIdx.x + q * NT;
+      if (i < n && (int)rank[q] == nA - 1) sh.bcast_u64 = Sx[q] + w[q];
+    }
+    __syncthreads();
+    WA = sh.bcast_u64;
+  }
+  const double thr = __dmul_rn((double)r.P, (double)WA);
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int i = threadIdx.x + q * NT;
+    if (i < n && (int)rank[q] < nA) {
+      const bool kept = rank[q] == 0 || !r.topp || (double)Sx[q] < thr;
+      const bool last = kept && ((int)rank[q] == nA - 1 || (r.topp && !((double)(Sx[q] + w[q]) < thr)));
+      if (last) {
+        sh.res.WK = Sx[q] + w[q];
+        sh.res.ckK = key[q];
+        sh.bcast_i = (int)rank[q] + 1;
+      }
+    }
+  }
+  __syncthreads();
+  const uint64_t WK = sh.res.WK;
+  const int nK = sh.bcast_i;
+  const uint64_t rr = draw_point(u, WK);
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int i = threadIdx.x + q * NT;
+    if (i < n && (int)rank[q] < nK && Sx[q] <= rr && rr < Sx[q] + w[q])
+      sh.res.token = (uint32_t)(key[q] & 0xFFFFFFFFu);
+  }
+  __syncthreads();
+}
+
+// --------------------------------------------------- general-path sort
 
 struct SortScratch {
+  Cand *in;  // [GCAP]
   Cand *mid;
   uint32_t *tmp;
   uint64_t *S;
   uint32_t *bcnt, *boff;
 };
 
-// Sort in[0..n) by (x desc, gid asc) in place; computes S[j] = inclusive
-// prefix of the weights.  Block-wide (all NT threads of one CTA).
+// Sort in[0..n) by (x desc, gid asc) in place; S[j] = inclusive prefix of
+// the weights.  Block-wide.
 __device__ void tail_sort_scan(Cand *in, int n, float m, const SortScratch &s, CtaSh &sh) {
   const uint32_t km = okey(m);
   uint64_t kmin = ~0ull, kmax = 0;
@@ -472,7 +731,7 @@ __device__ void tail_sort_scan(Cand *in, int n, float m, const SortScratch &s, C
   const uint64_t span = n > 0 ? kmax - kmin : 0;
   const int bits = span ? 64 - __clzll((long long)span) : 0;
   const int shift = bits > 10 ? bits - 10 : 0;
-  for (int b = threadIdx.x; b < NBK; b += NT) s.bcnt[b] = 0;
+  for (int b = threadIdx.x; b < GBK; b += NT) s.bcnt[b] = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += NT) {
     const uint32_t b = (uint32_t)((ckey(km, in[i].x, in[i].gid) - kmin) >> shift);
@@ -480,8 +739,8 @@ __device__ void tail_sort_scan(Cand *in, int n, float m, const SortScratch &s, C
     s.tmp[i] = (b << 16) | pos;
   }
   __syncthreads();
-  {  // exclusive scan of bucket counts, NBK / NT per thread
-    constexpr int PER = NBK / NT;
+  {
+    constexpr int PER = GBK / NT;
     uint32_t loc[PER];
     uint32_t sum = 0;
 #pragma unroll
@@ -516,7 +775,6 @@ __device__ void tail_sort_scan(Cand *in, int n, float m, const SortScratch &s, C
     in[st + rank] = c;
   }
   __syncthreads();
-  // weights and inclusive prefix sums: contiguous segments per thread
   const int seg = (n + NT - 1) / NT;
   const int a = min(n, (int)threadIdx.x * seg), bnd = min(n, a + seg);
   uint64_t loc = 0;
@@ -536,75 +794,52 @@ __device__ void tail_sort_scan(Cand *in, int n, float m, const SortScratch &s, C
 
 __device__ __forceinline__ uint64_t S_excl(const uint64_t *S, int j) { return j ? S[j - 1] : 0; }
 
-// Fast tail over a sorted prefix of value-A holding all of A: resolves
-// top_k, top_p and the draw.  Sets res.token / WK / ckK.  Block-wide.
-__device__ void fast_resolve(const Row &r, Cand *in, int n, float m, float u, const uint64_t *S, CtaSh &sh) {
-  const uint32_t km = okey(m);
-  const int nA = r.topk ? min(n, r.K) : n;
-  const uint64_t WA = S[nA - 1];
-  int nK = nA;
-  if (r.topp) {
-    const double thr = __dmul_rn((double)r.P, (double)WA);
-    int c = 0;
-    for (int j = threadIdx.x; j < nA; j += NT) c += ((double)S_excl(S, j) < thr) ? 1 : 0;
-    // the predicate holds on a prefix, so its count is the kept-set size
-    uint64_t tot;
-    block_exscan_u64((uint64_t)c, tot, sh);
-    nK = max(1, (int)tot);
-  }
-  const uint64_t WK = S[nK - 1];
-  const uint64_t rr = draw_point(u, WK);
-  for (int j = threadIdx.x; j < nK; j += NT) {
-    if (S_excl(S, j) <= rr && rr < S[j]) sh.res.token = in[j].gid;
-  }
-  if (threadIdx.x == 0) {
-    sh.res.WK = WK;
-    sh.res.ckK = ckey(km, in[nK - 1].x, in[nK - 1].gid);
-  }
-  __syncthreads();
-}
-
 // ------------------------------------------------------- kernel sections
 
 struct Layout {
   uint8_t *data;
-  uint32_t *map_mask, *map_spec;
-  int2 *ht;
+  uint8_t *map_mask, *map_spec;
+  int2 *ht;   // {pos, count}
+  int *queue;  // [QCAP] vector indices queued by a scan
   Cand *spec;
-  Cand *tail;
+  Cand *lcand;
+  int32_t *bias_id;
+  float *bias_val;
   uint8_t *work;
-  // work area views
   uint32_t *l1c;
   uint64_t *l1m;
   uint32_t *refc;
   uint64_t *refm;
   SortScratch gsort;
-  SortScratch fsort;
+  int *gqueue;
 };
 
 __device__ __forceinline__ Layout make_layout(uint8_t *smem, const Plan &pl) {
   Layout L;
   L.data = smem;
   L.work = smem + pl.off_work;
-  L.map_mask = reinterpret_cast<uint32_t *>(L.work);
-  L.map_spec = reinterpret_cast<uint32_t *>(L.work + pl.map_bytes);
+  L.map_mask = L.work;
+  L.map_spec = L.work + pl.map_bytes;
   L.ht = reinterpret_cast<int2 *>(L.work + 2 * pl.map_bytes);
+  L.queue = reinterpret_cast<int *>(L.work + 2 * pl.map_bytes);  // the table is dead once specials are final
   L.spec = reinterpret_cast<Cand *>(smem + pl.off_spec);
-  L.tail = reinterpret_cast<Cand *>(smem + pl.off_tail);
-  L.l1c = reinterpret_cast<uint32_t *>(L.work);
-  L.l1m = reinterpret_cast<uint64_t *>(L.work + 4096);
-  L.refc = reinterpret_cast<uint32_t *>(L.work + 12288);
-  L.refm = reinterpret_cast<uint64_t *>(L.work + 16384);
-  L.gsort.mid = reinterpret_cast<Cand *>(L.work + 12288);
-  L.gsort.tmp = reinterpret_cast<uint32_t *>(L.work + 20480);
-  L.gsort.S = reinterpret_cast<uint64_t *>(L.work + 24576);
-  L.gsort.bcnt = reinterpret_cast<uint32_t *>(L.work + 32768);
-  L.gsort.boff = reinterpret_cast<uint32_t *>(L.work + 36864);
-  L.fsort.mid = reinterpret_cast<Cand *>(smem);
-  L.fsort.tmp = reinterpret_cast<uint32_t *>(smem + 16384);
-  L.fsort.S = reinterpret_cast<uint64_t *>(smem + 24576);
-  L.fsort.bcnt = reinterpret_cast<uint32_t *>(smem + 40960);
-  L.fsort.boff = reinterpret_cast<uint32_t *>(smem + 45056);
+  L.lcand = reinterpret_cast<Cand *>(smem + pl.off_lcand);
+  L.bias_id = reinterpret_cast<int32_t *>(smem + pl.off_bias);
+  L.bias_val = reinterpret_cast<float *>(smem + pl.off_bias + BIAS_SMEM * 4);
+  // general-path area: after the bitmaps (which every scan still reads),
+  // over the hash table / scan queue that are dead by then
+  uint8_t *g = L.work + 2 * pl.map_bytes;
+  L.l1c = reinterpret_cast<uint32_t *>(g);
+  L.l1m = reinterpret_cast<uint64_t *>(g + 4096);
+  L.refc = reinterpret_cast<uint32_t *>(g + 12288);
+  L.refm = reinterpret_cast<uint64_t *>(g + 16384);
+  L.gsort.mid = reinterpret_cast<Cand *>(g + 12288);
+  L.gsort.tmp = reinterpret_cast<uint32_t *>(g + 20480);
+  L.gsort.S = reinterpret_cast<uint64_t *>(g + 24576);
+  L.gsort.bcnt = reinterpret_cast<uint32_t *>(g + 32768);
+  L.gsort.boff = reinterpret_cast<uint32_t *>(g + 36864);
+  L.gsort.in = reinterpret_cast<Cand *>(g + 40960);
+  L.gqueue = reinterpret_cast<int *>(g + 49152);  // general-path scan queue
   return L;
 }
 
@@ -612,7 +847,7 @@ __device__ __forceinline__ uint32_t ht_hash(uint32_t k, int cap) {
   return (k * 2654435761u) & (uint32_t)(cap - 1);
 }
 
-// Insert element index e (row-relative) with count increment c.
+// Insert element position e (row-relative) with count increment c.
 __device__ __forceinline__ bool ht_insert(int2 *ht, int cap, int e, int c) {
   uint32_t h = ht_hash((uint32_t)e, cap);
   for (int probe = 0; probe < cap; ++probe) {
@@ -626,17 +861,28 @@ __device__ __forceinline__ bool ht_insert(int2 *ht, int cap, int e, int c) {
   return false;
 }
 
+__device__ __forceinline__ int ht_find(const int2 *ht, int cap, int e) {
+  uint32_t h = ht_hash((uint32_t)e, cap);
+  for (int probe = 0; probe < cap; ++probe) {
+    const int k = ht[h].x;
+    if (k == e) return (int)h;
+    if (k == -1) return -1;
+    h = (h + 1) & (uint32_t)(cap - 1);
+  }
+  return -1;
+}
+
 __device__ __forceinline__ uint32_t allowed32(const uint32_t *aw, int64_t nwords, int64_t g) {
   const int64_t w = g >> 5;
   const int sh = (int)(g & 31);
-  uint32_t lo = w < nwords ? aw[w] : 0u;
-  uint32_t hi = (sh && w + 1 < nwords) ? aw[w + 1] : 0u;
+  const uint32_t lo = w < nwords ? aw[w] : 0u;
+  const uint32_t hi = (sh && w + 1 < nwords) ? aw[w + 1] : 0u;
   return sh ? ((lo >> sh) | (hi << (32 - sh))) : lo;
 }
 
 // State updates + scalar outputs for one row (called by one thread).
 __device__ __forceinline__ void write_row_outputs(const mstar_sampler_params_t &p, int row, int slot, uint32_t token,
-                                                  uint32_t status, bool drew) {
+                                                  uint32_t status) {
   if (p.out_ids) p.out_ids[row] = (int64_t)token;
   if (p.out_ids32) p.out_ids32[row] = (int32_t)token;
   if (p.out_status) p.out_status[row] = (int32_t)status;
@@ -649,7 +895,6 @@ __device__ __forceinline__ void write_row_outputs(const mstar_sampler_params_t &
   if ((p.flags & MSTAR_FLAG_UPDATE_SEEN) && p.seen_bits) {
     atomicOr(&p.seen_bits[(int64_t)slot * p.seen_words + (token >> 5)], 1u << (token & 31));
   }
-  (void)drew;
 }
 
 // ------------------------------------------------------------ the kernel
@@ -693,82 +938,59 @@ __global__ void __launch_bounds__(NT, 1)
     return;
   }
 
-  Row r;
-  row_init(r, p, row, slot);
   const Layout L = make_layout(smem, pl);
+  constexpr int es = (int)sizeof(T);
+  const uint8_t *rowp = static_cast<const uint8_t *>(p.logits) + (int64_t)row * p.ld * es;
 
   // ---- slice geometry (a slice past the end of a short row is empty)
   const int64_t c0 = min((int64_t)rank * pl.slice, (int64_t)p.V);
   const int64_t c1 = min((int64_t)p.V, c0 + pl.slice);
-  const uint8_t *rowp = static_cast<const uint8_t *>(r.rowp);
-  const uintptr_t a_c0 = reinterpret_cast<uintptr_t>(rowp + c0 * pl.es);
-  const uintptr_t a_c1 = reinterpret_cast<uintptr_t>(rowp + c1 * pl.es);
+  const uintptr_t a_c0 = reinterpret_cast<uintptr_t>(rowp + c0 * es);
+  const uintptr_t a_c1 = reinterpret_cast<uintptr_t>(rowp + c1 * es);
   const uintptr_t a_al = a_c0 & ~(uintptr_t)15;
-  const int64_t c0al = c0 - (int64_t)((a_c0 - a_al) / pl.es);
+  const int64_t c0al = c0 - (int64_t)((a_c0 - a_al) / es);
   const uintptr_t b0 = (a_c0 + 15) & ~(uintptr_t)15;
   const uintptr_t b1 = a_c1 & ~(uintptr_t)15;
   const int64_t nbulk = (b1 > b0) ? (int64_t)(b1 - b0) : 0;
-  const int hv = (int)((b0 - a_al) / 16);                 // head fringe vectors (0 or 1)
-  const int nbv = (int)(nbulk / 16);                      // bulk vectors
-  const int nvec = (int)((a_c1 - a_al + 15) / 16);        // all vectors of the slice
+  const int hv = (int)((b0 - a_al) / 16);           // head fringe vectors (0 or 1)
+  const int nbv = (int)(nbulk / 16);                // bulk vectors
+  const int nvec = (int)((a_c1 - a_al + 15) / 16);  // all vectors of the slice
   const int nchunk = (int)((nbulk + CHUNK_BYTES - 1) / CHUNK_BYTES);
-  const int64_t pos0_gid = r.gbase + c0al;                // gid of data position 0
   uint4 *data4 = reinterpret_cast<uint4 *>(L.data);
 
-  // ---- setup: barriers, bulk copies, bitmaps, specials
+  // ---- issue the bulk copies first
   if (tid == 0) {
     for (int j = 0; j < nchunk; ++j) mbar_init(&sh.mbar[j], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    sh.cta_max = -INFINITY;
-    sh.tail_count = 0;
-    sh.min_gid = 0xFFFFFFFFu;
-    sh.status = 0;
-    sh.n_spec = 0;
-    sh.ht_fail = 0;
-    sh.tp_ovf = 0;
-  }
-  const int map_words = pl.map_bytes / 4;
-  for (int i = tid; i < map_words; i += NT) {
-    L.map_spec[i] = 0u;
-  }
-  for (int i = tid; i < pl.ht_cap; i += NT) L.ht[i] = make_int2(-1, 0);
-  __syncthreads();
-  if (tid == 0) {
     for (int j = 0; j < nchunk; ++j) {
       const uint32_t bytes = (uint32_t)min((int64_t)CHUNK_BYTES, nbulk - (int64_t)j * CHUNK_BYTES);
       mbar_expect_tx(&sh.mbar[j], bytes);
       bulk_g2s(L.data + (b0 - a_al) + (int64_t)j * CHUNK_BYTES,
                reinterpret_cast<const void *>(b0 + (uintptr_t)j * CHUNK_BYTES), bytes, &sh.mbar[j]);
     }
+    sh.cta_max = -INFINITY;
+    sh.nloc = 0;
+    sh.min_gid = 0xFFFFFFFFu;
+    sh.status = 0;
+    sh.n_spec = 0;
+    sh.ht_fail = 0;
+    sh.tp_ovf = 0;
   }
-  // fringe vectors: plain loads (positions outside the slice get -inf)
-  for (int k = tid; k < nvec; k += NT) {
-    if (k >= hv && k < hv + nbv) continue;
-    uint4 v;
-    uint8_t *vb = reinterpret_cast<uint8_t *>(&v);
-    for (int j = 0; j < VEC; ++j) {
-      const int64_t e = c0al + (int64_t)k * VEC + j;
-      if (e >= c0 && e < c1) {
-        if (sizeof(T) == 2) {
-          const uint16_t h = static_cast<const uint16_t *>(r.rowp)[e];
-          memcpy(vb + 2 * j, &h, 2);
-        } else {
-          const uint32_t w = static_cast<const uint32_t *>(r.rowp)[e];
-          memcpy(vb + 4 * j, &w, 4);
-        }
-      } else {
-        if (sizeof(T) == 2) {
-          const uint16_t h = 0xFF80u;
-          memcpy(vb + 2 * j, &h, 2);
-        } else {
-          const uint32_t w = 0xFF800000u;
-          memcpy(vb + 4 * j, &w, 4);
-        }
-      }
-    }
-    data4[k] = v;
+
+  Row r;
+  row_init(r, p, row, slot, p.V);
+  const int64_t pos0_gid = r.gbase + c0al;  // gid of data position 0
+  const bool has_hist = p.hist_ids && p.hist_len;
+  const bool has_spec = has_hist || p.seen_bits || p.bias_ids;
+
+  // ---- setup while the copies fly
+  const int map_words = pl.map_bytes / 4;
+  uint32_t *mask32 = reinterpret_cast<uint32_t *>(L.map_mask);
+  uint32_t *spec32 = reinterpret_cast<uint32_t *>(L.map_spec);
+  if (has_spec) {
+    for (int i = tid; i < map_words; i += NT) spec32[i] = 0u;
+    for (int i = tid; i < pl.ht_cap; i += NT) L.ht[i] = make_int2(-1, 0);
   }
-  // mask bitmap: outside-slice positions and disallowed ids
   {
     const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)slot * p.allowed_words : nullptr;
     for (int wi = tid; wi < map_words; wi += NT) {
@@ -786,11 +1008,31 @@ __global__ void __launch_bounds__(NT, 1)
         const uint32_t bits = allowed32(aw, p.allowed_words, r.gbase + e0 + lo_in) << lo_in;
         dis = inmask & ~bits;
       }
-      L.map_mask[wi] = ~inmask | dis;
+      mask32[wi] = ~inmask | dis;
     }
   }
+  // fringe vectors: plain loads (positions outside the slice are masked)
+  auto load_fringe = [&](int k) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const int64_t e = c0al + (int64_t)k * VEC + j;
+      const uint32_t bits = (e >= c0 && e < c1) ? Elem<T>::load_bits(rowp, e) : Elem<T>::neg_inf();
+      Elem<T>::set_bits(v, j, bits);
+    }
+    data4[k] = v;
+  };
+  for (int k = tid; k < hv; k += NT) load_fringe(k);
+  for (int k = hv + nbv + tid; k < nvec; k += NT) load_fringe(k);
+  if (p.bias_ids && p.NB <= BIAS_SMEM) {
+    for (int j = tid; j < p.NB; j += NT) {
+      L.bias_id[j] = p.bias_ids[(int64_t)slot * p.NB + j];
+      L.bias_val[j] = p.bias_vals[(int64_t)slot * p.NB + j];
+    }
+  }
+  if (has_spec) __syncthreads();  // table and bitmap zeroed
   // specials: history / seen bits / bias ids that fall in [c0, c1)
-  if (p.hist_ids && p.hist_len) {
+  if (has_hist) {
     const int32_t len = p.hist_len[slot];
     const int n = min(len, p.H);
     const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
@@ -798,22 +1040,24 @@ __global__ void __launch_bounds__(NT, 1)
       const int64_t e = (int64_t)h[j] - r.gbase;
       if (e >= c0 && e < c1) {
         if (!ht_insert(L.ht, pl.ht_cap, (int)e, 1)) sh.ht_fail = 1;
-        atomicOr(&L.map_spec[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
+        atomicOr(&spec32[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
       }
     }
   } else if (p.seen_bits) {
     const uint32_t *sw = p.seen_bits + (int64_t)slot * p.seen_words;
     const int64_t g0 = r.gbase + c0, g1 = r.gbase + c1;
-    for (int64_t w = (g0 >> 5) + tid; w <= ((g1 - 1) >> 5); w += NT) {
-      uint32_t bits = sw[w];
-      while (bits) {
-        const int b = __ffs(bits) - 1;
-        bits &= bits - 1;
-        const int64_t g = (w << 5) + b;
-        if (g < g0 || g >= g1) continue;
-        const int64_t e = g - r.gbase;
-        if (!ht_insert(L.ht, pl.ht_cap, (int)e, 1)) sh.ht_fail = 1;
-        atomicOr(&L.map_spec[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
+    if (g1 > g0) {
+      for (int64_t w = (g0 >> 5) + tid; w <= ((g1 - 1) >> 5); w += NT) {
+        uint32_t bits = sw[w];
+        while (bits) {
+          const int b = __ffs(bits) - 1;
+          bits &= bits - 1;
+          const int64_t g = (w << 5) + b;
+          if (g < g0 || g >= g1) continue;
+          const int64_t e = g - r.gbase;
+          if (!ht_insert(L.ht, pl.ht_cap, (int)e, 1)) sh.ht_fail = 1;
+          atomicOr(&spec32[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
+        }
       }
     }
   }
@@ -825,28 +1069,61 @@ __global__ void __launch_bounds__(NT, 1)
       const int64_t e = (int64_t)g - r.gbase;
       if (e >= c0 && e < c1) {
         if (!ht_insert(L.ht, pl.ht_cap, (int)e, 0)) sh.ht_fail = 1;
-        atomicOr(&L.map_spec[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
+        atomicOr(&spec32[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
       }
     }
   }
-  __syncthreads();
-  // finalize specials from global memory (overlaps the bulk copies)
-  float spec_max = -INFINITY;
+  __syncthreads();  // bitmaps, table, fringe vectors complete
+
+  // ---- pass A: patch + raw max, chunk by chunk as the bulk copies land
+  float rawmax = -INFINITY;
+  bool timed_out = false;
   {
+    auto process = [&](int k, uint4 v) {
+      uint32_t b = Elem<T>::bits_of(L.map_mask, k);
+      if (has_spec) b |= Elem<T>::bits_of(L.map_spec, k);
+      if (b) v = Elem<T>::mask_out(v, b);
+      rawmax = fmaxf(rawmax, Elem<T>::vmax(v));
+    };
+    for (int k = tid; k < hv; k += NT) process(k, data4[k]);
+    for (int k = hv + nbv + tid; k < nvec; k += NT) process(k, data4[k]);
+    constexpr int CV = CHUNK_BYTES / 16;
+    for (int j = 0; j < nchunk; ++j) {
+      if (!mbar_wait(&sh.mbar[j], 0)) timed_out = true;
+      const int kb = hv + j * CV, ke = hv + min(nbv, (j + 1) * CV);
+      for (int k0 = kb + tid; k0 < ke; k0 += NT * 4) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (k0 + u * NT < ke) v[u] = data4[k0 + u * NT];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (k0 + u * NT < ke) process(k0 + u * NT, v[u]);
+      }
+    }
+  }
+  if (timed_out) atomicOr(&sh.status, MSTAR_STATUS_TIMEOUT);
+  __syncthreads();  // every chunk has landed
+  // finalize specials: bias (list order) -> penalties -> mask -> transform
+  float spec_max = -INFINITY;
+  if (has_spec) {
     const float R = p.rep_pen ? p.rep_pen[slot] : 1.0f;
     const float F = p.freq_pen ? p.freq_pen[slot] : 0.0f;
     const float Pp = p.pres_pen ? p.pres_pen[slot] : 0.0f;
+    const bool bias_smem = p.bias_ids && p.NB <= BIAS_SMEM;
     const int32_t *bi = p.bias_ids ? p.bias_ids + (int64_t)slot * p.NB : nullptr;
     const float *bv = p.bias_vals ? p.bias_vals + (int64_t)slot * p.NB : nullptr;
     for (int i = tid; i < pl.ht_cap; i += NT) {
       const int2 ent = L.ht[i];
       if (ent.x < 0) continue;
       const int64_t e = ent.x;
-      float v = Elem<T>::load(r.rowp, e);
-      if (bi && bv) {
+      float v = Elem<T>::smem_elem(L.data, e - c0al);
+      if (bi) {
         const int32_t gid = (int32_t)(e + r.gbase);
-        for (int j = 0; j < p.NB; ++j)
-          if (bi[j] == gid) v = __fadd_rn(v, bv[j]);
+        for (int j = 0; j < p.NB; ++j) {
+          const int32_t id = bias_smem ? L.bias_id[j] : bi[j];
+          if (id == gid) v = __fadd_rn(v, bias_smem ? L.bias_val[j] : bv[j]);
+        }
       }
       if (ent.y > 0) {
         v = (v > 0.0f) ? __fdiv_rn(v, R) : __fmul_rn(v, R);
@@ -854,7 +1131,7 @@ __global__ void __launch_bounds__(NT, 1)
         v = __fsub_rn(v, Pp);
       }
       const int64_t pos = e - c0al;
-      const bool masked = (L.map_mask[pos >> 5] >> (pos & 31)) & 1u;
+      const bool masked = (L.map_mask[pos >> 3] >> (pos & 7)) & 1u;
       float x;
       if (v != v) x = v;
       else if (masked) x = -INFINITY;
@@ -865,107 +1142,114 @@ __global__ void __launch_bounds__(NT, 1)
       spec_max = fmaxf(spec_max, x);
     }
   }
-  __syncthreads();
-  const int nspec = min((int)sh.n_spec, pl.spec_cap);
-
-  // ---- pass A: patch + raw max, chunk by chunk as the bulk copies land
-  float rawmax = -INFINITY;
-  bool timed_out = false;
-  {
-    auto process = [&](int k) {
-      uint4 v = data4[k];
-      const uint32_t mb = Elem<T>::bits_of(L.map_mask, k), sb = Elem<T>::bits_of(L.map_spec, k);
-      if (mb | sb) {
-        Elem<T>::patch(v, mb, sb);
-        data4[k] = v;
-      }
-      rawmax = fmaxf(rawmax, Elem<T>::vmax(v));
-    };
-    for (int k = tid; k < nvec; k += NT)
-      if (k < hv || k >= hv + nbv) process(k);
-    constexpr int CV = CHUNK_BYTES / 16;
-    for (int j = 0; j < nchunk; ++j) {
-      if (!mbar_wait(&sh.mbar[j], 0)) timed_out = true;
-      const int kb = hv + j * CV, ke = hv + min(nbv, (j + 1) * CV);
-      for (int k = kb + tid; k < ke; k += NT) process(k);
-    }
-  }
-  if (timed_out) atomicOr(&sh.status, MSTAR_STATUS_TIMEOUT);
-  if (sh.ht_fail && tid == 0) atomicOr(&sh.status, MSTAR_STATUS_SPECIAL_OVERFLOW);
   {
     const float xm = r.greedy ? rawmax : __fmul_rn(rawmax, r.invT);
     const float cm = block_max_f32(fmaxf(xm, spec_max), sh);
-    if (tid == 0) sh.cta_max = cm;
-  }
-  cluster.sync();  // #1: maxima published; leader counters initialised
-
-  // ---- row max and thresholds
-  float m = -INFINITY;
-  for (int q = 0; q < S; ++q) m = fmaxf(m, *cluster.map_shared_rank(&sh.cta_max, q));
-  CtaSh *lead = cluster.map_shared_rank(&sh, 0);
-  Cand *lead_tail = cluster.map_shared_rank(L.tail, 0);
-  if (sh.status && tid == 0) atomicOr(&lead->status, sh.status);
-  const bool empty = !(m > -INFINITY);
-  const bool one = r.greedy || r.K == 1;
-  float u = 0.0f;
-  if (!empty) {
-    compute_thresholds<T>(r, m, sh);
-    const float xA = sh.xA, rA = sh.rA;
-    const uint32_t km = okey(m);
-    (void)km;
-    // ---- pass C: compaction of value-A (or lowest id at the max)
-    if (one) {
-      uint32_t best = 0xFFFFFFFFu;
-      for_each_value<T>(data4, nvec, pos0_gid, L.spec, nspec, rA, xA, r.greedy, r.invT,
-                        [&](float x, uint32_t gid) { best = min(best, gid); });
-      for (int o = 16; o; o >>= 1) best = min(best, __shfl_xor_sync(~0u, best, o));
-      if ((tid & 31) == 0 && best != 0xFFFFFFFFu) atomicMin(&lead->min_gid, best);
-    } else {
-      for_each_value<T>(data4, nvec, pos0_gid, L.spec, nspec, rA, xA, r.greedy, r.invT,
-                        [&](float x, uint32_t gid) {
-                          const uint32_t idx = atomicAdd(&lead->tail_count, 1u);
-                          if (idx < (uint32_t)TAIL_CAP) lead_tail[idx] = Cand{x, gid};
-                        });
+    if (tid == 0) {
+      sh.cta_max = cm;
+      if (sh.ht_fail) sh.status |= MSTAR_STATUS_SPECIAL_OVERFLOW;
     }
   }
-  cluster.sync();  // #2: candidates complete
+  const int nspec = min((int)sh.n_spec, pl.spec_cap);
+  const Slice sl{data4, L.map_mask, L.map_spec, nvec, has_spec, pos0_gid};
+  cluster.sync();  // #1: maxima published
 
-  const uint32_t ncand = lead->tail_count;
+  // ---- row max, threshold, pass C
+  float m = -INFINITY;
+  for (int q = 0; q < S; ++q) m = fmaxf(m, *cluster.map_shared_rank(&sh.cta_max, q));
+  const bool empty = !(m > -INFINITY);
+  const bool one = r.greedy || r.K == 1;
+  if (!empty) {
+    if (tid < 32) {
+      const float t = choose_theta(r, m);
+      if (tid == 0) sh.theta = t;
+    }
+    __syncthreads();
+    const float theta = sh.theta;
+    if (one) {
+      uint32_t best = 0xFFFFFFFFu;
+      for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.queue, QCAP, &sh.qcount,
+                        [&](float x, uint32_t gid) { best = min(best, gid); });
+      best = block_min_u32(best, sh);
+      if (tid == 0) sh.min_gid = best;
+    } else {
+      for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.queue, QCAP, &sh.qcount, [&](float x, uint32_t gid) {
+        const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+        if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
+      });
+    }
+  }
+  cluster.sync();  // #2: local candidate lists complete
+
+  // every CTA takes the same decision from the published counts
+  uint32_t ncand = 0, status_all = 0;
+  bool lovf = false;
+  for (int q = 0; q < S; ++q) {
+    const CtaSh *peer = cluster.map_shared_rank(&sh, q);
+    const uint32_t c = peer->nloc;
+    lovf |= c > (uint32_t)LCAP;
+    ncand += min(c, (uint32_t)LCAP);
+    status_all |= peer->status;
+  }
+  const float theta = empty ? INFINITY : sh.theta;
   const bool force_general = (p.flags & MSTAR_FLAG_FORCE_GENERAL) != 0;
-  const bool fast = empty || one || (ncand <= (uint32_t)TAIL_CAP && !force_general);
+  const bool fast = empty || one || (!lovf && ncand <= (uint32_t)TAIL_CAP && !force_general);
+  float u = 0.0f;
   if (rank == 0) {
     if (tid == 0) {
       sh.res.m = m;
-      sh.res.xA = empty ? INFINITY : sh.xA;
+      sh.res.theta = theta;
       sh.res.greedy = r.greedy;
       sh.res.empty = empty;
       sh.res.token = 0;
       sh.res.WK = 0;
       sh.res.ckK = 0;
+      sh.res.status = status_all;
     }
-    __syncthreads();
-    if (!empty) {
+    if (!empty && !one) {
       if (p.uniforms) u = p.uniforms[row];
       else u = philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
     }
   }
-  int nemit = 0;  // TP: sorted candidates to emit from L.tail
+  uint32_t *rec = MODE == 1 ? tp_send + (int64_t)row * pl.rec_words : nullptr;
+  int nemit = 0;                                  // TP: candidates emitted in order
+  const LeanScratch lean = lean_scratch(L.data);  // the leader's slice data is dead by then
+
+  // Leader: gather every CTA's list into dst (DSMEM reads); returns the count.
+  auto gather = [&](Cand *dst, int cap) -> int {
+    int off = 0;
+    for (int q = 0; q < S; ++q) {
+      const CtaSh *peer = cluster.map_shared_rank(&sh, q);
+      const int c = (int)min(peer->nloc, (uint32_t)LCAP);
+      const Cand *src = cluster.map_shared_rank(L.lcand, q);
+      for (int i = tid; i < c; i += NT)
+        if (off + i < cap) dst[off + i] = src[i];
+      off += c;
+    }
+    __syncthreads();
+    return min(off, cap);
+  };
+
   if (fast) {
     if (rank == 0 && !empty) {
+      __syncthreads();
       if (one) {
         if (tid == 0) {
-          sh.res.token = sh.min_gid;
+          uint32_t best = 0xFFFFFFFFu;
+          for (int q = 0; q < S; ++q) best = min(best, cluster.map_shared_rank(&sh, q)->min_gid);
+          sh.res.token = best;
           sh.res.WK = 4294967296ull;
-          sh.res.ckK = ((uint64_t)0 << 32) | sh.min_gid;
+          sh.res.ckK = (uint64_t)best;
         }
         __syncthreads();
         nemit = -1;
       } else {
-        tail_sort_scan(L.tail, (int)ncand, m, L.fsort, sh);
+        const int n = gather(lean.cand, TAIL_CAP);
         if (MODE == 0) {
-          fast_resolve(r, L.tail, (int)ncand, m, u, L.fsort.S, sh);
+          lean_tail(r, n, m, theta, u, lean, sh, nullptr, 0);
         } else {
-          nemit = r.topk ? min((int)ncand, r.K) : (int)ncand;
+          nemit = r.topk ? min(n, r.K) : n;
+          if (nemit <= pl.tp_cap) lean_tail(r, n, m, theta, u, lean, sh, rec, nemit);
         }
       }
     }
@@ -975,10 +1259,9 @@ __global__ void __launch_bounds__(NT, 1)
     if (rank == 0 && tid == 0) {
       memset(&P, 0, sizeof(P));
       P.state = ST_START;
-      atomicOr(&sh.status, MSTAR_STATUS_GENERAL);
+      sh.res.status |= MSTAR_STATUS_GENERAL;
     }
     const uint32_t km = okey(m);
-    const float xA = sh.xA, rA = sh.rA;
     for (int round = 0; round < MAX_ROUNDS; ++round) {
       if (rank == 0) {
         // ================= leader planning (block-wide) =================
@@ -988,7 +1271,7 @@ __global__ void __launch_bounds__(NT, 1)
           __syncthreads();
           if (state == ST_START) {
             if (tid == 0) {
-              const uint32_t DA = km - okey(xA);
+              const uint32_t DA = km - okey(theta);
               P.l1lo = 0;
               P.l1hi = ((uint64_t)DA << 32) | 0xFFFFFFFFull;
               const int bits = 64 - __clzll((long long)(P.l1hi - P.l1lo));
@@ -1004,7 +1287,6 @@ __global__ void __launch_bounds__(NT, 1)
             break;
           }
           if (state == ST_AFTER_L1 || state == ST_LOC_AFTER_REF) {
-            // inclusive prefix of the level's bins
             uint32_t *C = state == ST_AFTER_L1 ? L.l1c : L.refc;
             uint64_t *M = state == ST_AFTER_L1 ? L.l1m : L.refm;
             constexpr int PER = NBIN / NT;
@@ -1016,10 +1298,8 @@ __global__ void __launch_bounds__(NT, 1)
               sc += lc[q];
               sm += lm[q];
             }
-            uint64_t tc, tm;
-            uint64_t oc = block_exscan_u64(sc, tc, sh);
-            __syncthreads();
-            uint64_t om = block_exscan_u64(sm, tm, sh);
+            uint64_t oc, om, tc, tm;
+            block_exscan2_u64(sc, sm, oc, om, tc, tm, sh);
 #pragma unroll
             for (int q = 0; q < PER; ++q) {
               oc += lc[q];
@@ -1040,7 +1320,6 @@ __global__ void __launch_bounds__(NT, 1)
                 P.base_c = 0;
                 P.base_m = 0;
                 const bool needA = r.topk && P.N > (uint64_t)r.K;
-                // smallest prefix [l1lo, end of bin b_end] containing A
                 int b_end = P.nbins - 1;
                 if (needA) {
                   for (int b = 0; b < P.nbins; ++b)
@@ -1085,13 +1364,9 @@ __global__ void __launch_bounds__(NT, 1)
                 }
               }
               __syncthreads();
-              if (P.state == ST_AFTER_PREFIX) {
-                if (tid == 0) sh.tail_count = 0;
-                break;
-              }
+              if (P.state == ST_AFTER_PREFIX) break;
               continue;
             }
-            // ST_LOC_AFTER_REF: switch to the refined level
             if (tid == 0) {
               P.level = 1;
               P.state = ST_LOC_BIN;
@@ -1117,7 +1392,7 @@ __global__ void __launch_bounds__(NT, 1)
               const int b = sh.bcast_i;
               if (b < 0) {  // cannot happen for consistent inputs; finish defensively
                 P.state = ST_FINISH;
-                atomicOr(&sh.status, MSTAR_STATUS_EMPTY);
+                sh.res.status |= MSTAR_STATUS_EMPTY;
               } else {
                 const uint64_t blo = P.lo + ((uint64_t)b << P.shift);
                 const uint64_t bhi = u64min(P.hi, blo + (1ull << P.shift) - 1);
@@ -1126,7 +1401,6 @@ __global__ void __launch_bounds__(NT, 1)
                 P.cbase_m = P.base_m + (b ? M[b - 1] : 0);
                 if (cnt <= (uint64_t)GCAP || P.shift == 0) {
                   sh.cmd = Cmd{OP_COMPACT, 0, blo, bhi, 0, 0};
-                  sh.tail_count = 0;
                   P.state = ST_LOC_AFTER_COMPACT;
                 } else {
                   P.base_c = P.cbase_c;
@@ -1152,21 +1426,22 @@ __global__ void __launch_bounds__(NT, 1)
             break;
           }
           if (state == ST_AFTER_PREFIX) {
-            const int n = (int)min(sh.tail_count, (uint32_t)TAIL_CAP);
-            tail_sort_scan(L.tail, n, m, L.fsort, sh);
+            const int n = gather(lean.cand, TAIL_CAP);
             if (MODE == 0) {
-              fast_resolve(r, L.tail, n, m, u, L.fsort.S, sh);
+              lean_tail(r, n, m, theta, u, lean, sh, nullptr, 0);
             } else {
               nemit = r.topk ? min(n, r.K) : n;
+              if (nemit <= pl.tp_cap) lean_tail(r, n, m, theta, u, lean, sh, rec, nemit);
             }
             if (tid == 0) P.state = ST_FINISH;
             __syncthreads();
             continue;
           }
           if (state == ST_LOC_AFTER_COMPACT) {
-            const int n = (int)min(sh.tail_count, (uint32_t)GCAP);
-            tail_sort_scan(L.tail, n, m, L.gsort, sh);
+            const int n = gather(L.gsort.in, GCAP);
+            tail_sort_scan(L.gsort.in, n, m, L.gsort, sh);
             const uint64_t *Sx = L.gsort.S;
+            const Cand *sorted = L.gsort.in;
             if (tid == 0) sh.bcast_i = -1;
             __syncthreads();
             for (int j = tid; j < n; j += NT) {
@@ -1182,11 +1457,10 @@ __global__ void __launch_bounds__(NT, 1)
               const int j = sh.bcast_i;
               if (j < 0) {
                 P.state = ST_FINISH;
-                atomicOr(&sh.status, MSTAR_STATUS_EMPTY);
+                sh.res.status |= MSTAR_STATUS_EMPTY;
               } else {
-                const uint64_t ck = ckey(km, L.tail[j].x, L.tail[j].gid);
-                const uint64_t se = P.cbase_m + S_excl(Sx, j), si = P.cbase_m + Sx[j];
-                // back to L1 for the next query
+                const uint64_t ck = ckey(km, sorted[j].x, sorted[j].gid);
+                const uint64_t si = P.cbase_m + Sx[j];
                 P.level = 0;
                 P.lo = P.l1lo;
                 P.hi = P.l1hi;
@@ -1227,7 +1501,7 @@ __global__ void __launch_bounds__(NT, 1)
                   P.tpoint = draw_point(u, P.WK);
                   P.state = ST_LOC_BIN;
                 } else {  // draw
-                  sh.res.token = L.tail[j].gid;
+                  sh.res.token = sorted[j].gid;
                   sh.res.WK = P.WK;
                   sh.res.ckK = P.ckK;
                   P.state = ST_FINISH;
@@ -1235,10 +1509,7 @@ __global__ void __launch_bounds__(NT, 1)
               }
             }
             __syncthreads();
-            if (P.state == ST_AFTER_PREFIX) {
-              if (tid == 0) sh.tail_count = 0;
-              break;
-            }
+            if (P.state == ST_AFTER_PREFIX) break;
             continue;
           }
           if (state == ST_FINISH) {
@@ -1249,7 +1520,7 @@ __global__ void __launch_bounds__(NT, 1)
         __syncthreads();
       }
       cluster.sync();  // command published
-      const Cmd cmd = lead->cmd;
+      const Cmd cmd = cluster.map_shared_rank(&sh, 0)->cmd;
       if (cmd.op == OP_DONE) break;
       if (cmd.op == OP_HIST) {
         uint32_t *hc = rank == 0 ? (cmd.target == TGT_L1 ? L.l1c : L.refc) : L.l1c;
@@ -1261,15 +1532,13 @@ __global__ void __launch_bounds__(NT, 1)
           }
           __syncthreads();
         }
-        for_each_value<T>(data4, nvec, pos0_gid, L.spec, nspec, rA, xA, r.greedy, r.invT,
-                          [&](float x, uint32_t gid) {
-                            const uint64_t ck = ckey(km, x, gid);
-                            if (ck < cmd.lo || ck > cmd.hi) return;
-                            const int b = (int)((ck - cmd.lo) >> cmd.shift);
-                            atomicAdd(&hc[b], 1u);
-                            atomicAdd((unsigned long long *)&hm[b],
-                                      (unsigned long long)spec_w_from_e(spec_e(x, m)));
-                          });
+        for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount, [&](float x, uint32_t gid) {
+          const uint64_t ck = ckey(km, x, gid);
+          if (ck < cmd.lo || ck > cmd.hi) return;
+          const int b = (int)((ck - cmd.lo) >> cmd.shift);
+          atomicAdd(&hc[b], 1u);
+          atomicAdd((unsigned long long *)&hm[b], (unsigned long long)spec_w_from_e(spec_e(x, m)));
+        });
         if (rank != 0) {
           __syncthreads();
           uint32_t *rc = cluster.map_shared_rank(cmd.target == TGT_L1 ? L.l1c : L.refc, 0);
@@ -1281,14 +1550,15 @@ __global__ void __launch_bounds__(NT, 1)
             }
           }
         }
-      } else {  // OP_COMPACT
-        for_each_value<T>(data4, nvec, pos0_gid, L.spec, nspec, rA, xA, r.greedy, r.invT,
-                          [&](float x, uint32_t gid) {
-                            const uint64_t ck = ckey(km, x, gid);
-                            if (ck < cmd.lo || ck > cmd.hi) return;
-                            const uint32_t idx = atomicAdd(&lead->tail_count, 1u);
-                            if (idx < (uint32_t)TAIL_CAP) lead_tail[idx] = Cand{x, gid};
-                          });
+      } else {  // OP_COMPACT into the CTA-local list
+        if (tid == 0) sh.nloc = 0;
+        __syncthreads();
+        for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount, [&](float x, uint32_t gid) {
+          const uint64_t ck = ckey(km, x, gid);
+          if (ck < cmd.lo || ck > cmd.hi) return;
+          const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+          if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
+        });
       }
       cluster.sync();  // round results complete
     }
@@ -1299,36 +1569,30 @@ __global__ void __launch_bounds__(NT, 1)
     __syncthreads();
     if (MODE == 0) {
       if (tid == 0) {
-        uint32_t status = sh.status;
+        uint32_t status = sh.res.status;
         uint32_t token = sh.res.token;
         if (empty) {
           status |= MSTAR_STATUS_EMPTY;
           token = (uint32_t)r.gbase;
         }
         sh.res.status = status;
-        write_row_outputs(p, row, slot, token, status, !empty);
+        write_row_outputs(p, row, slot, token, status);
       }
     } else {
-      uint32_t *rec = tp_send + (int64_t)row * pl.rec_words;
       const bool ovf = sh.tp_ovf || (nemit > pl.tp_cap);
       if (tid == 0) {
         rec[0] = __float_as_uint(empty ? -INFINITY : m);
-        uint32_t st = sh.status | (ovf ? MSTAR_STATUS_TP_OVERFLOW : 0u) | (empty ? MSTAR_STATUS_EMPTY : 0u);
+        const uint32_t st =
+            sh.res.status | (ovf ? MSTAR_STATUS_TP_OVERFLOW : 0u) | (empty ? MSTAR_STATUS_EMPTY : 0u);
         if (nemit < 0) {
           rec[1] = 1;
           rec[4] = __float_as_uint(m);
-          rec[5] = sh.min_gid;
+          rec[5] = sh.res.token;
         } else {
           rec[1] = ovf ? 0u : (uint32_t)nemit;
         }
         rec[2] = st;
         rec[3] = 0;
-      }
-      if (!ovf && nemit > 0) {
-        for (int j = tid; j < nemit; j += NT) {
-          rec[4 + 2 * j] = __float_as_uint(L.tail[j].x);
-          rec[5 + 2 * j] = L.tail[j].gid;
-        }
       }
     }
   }
@@ -1336,7 +1600,7 @@ __global__ void __launch_bounds__(NT, 1)
   // ---- debug dense outputs (recomputed from global memory)
   if (MODE == 0 && (p.out_x || p.out_kept || p.out_probs)) {
     cluster.sync();
-    const Result res = lead->res;
+    const Result res = cluster.map_shared_rank(&sh, 0)->res;
     const uint32_t kmm = okey(res.m);
     const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)slot * p.allowed_words : nullptr;
     auto emit = [&](int64_t e, float x) {
@@ -1344,11 +1608,11 @@ __global__ void __launch_bounds__(NT, 1)
       const uint32_t gid = (uint32_t)(e + r.gbase);
       bool kept = false;
       float prob = 0.0f;
-      if (!res.empty) {
+      if (!res.empty && x == x) {
         if (res.greedy) {
           kept = gid == res.token;
           prob = kept ? 1.0f : 0.0f;
-        } else if (x >= res.xA && ckey(kmm, x, gid) <= res.ckK) {
+        } else if (x > -INFINITY && x <= res.m && ckey(kmm, x, gid) <= res.ckK) {
           kept = true;
           prob = (float)__ddiv_rn((double)spec_w_from_e(spec_e(x, res.m)), (double)res.WK);
         }
@@ -1358,12 +1622,12 @@ __global__ void __launch_bounds__(NT, 1)
       if (p.out_probs) p.out_probs[o] = prob;
     };
     for (int64_t e = c0 + tid; e < c1; e += NT) {
-      float v = Elem<T>::load(r.rowp, e);
+      const float v = Elem<T>::load(r.rowp, e);
       const int64_t g = e + r.gbase;
       const bool allowed = !aw || ((aw[g >> 5] >> (g & 31)) & 1u);
       float x;
-      if (!allowed) x = (v != v) ? v : -INFINITY;
-      else if (v != v) x = v;
+      if (v != v) x = v;
+      else if (!allowed) x = -INFINITY;
       else x = r.greedy ? v : __fmul_rn(v, r.invT);
       emit(e, x);
     }
@@ -1392,17 +1656,8 @@ __global__ void __launch_bounds__(NT, 1)
     return;
   }
   Row r;
-  mstar_sampler_params_t pg = p;
-  pg.V = (int32_t)V_global;
-  pg.vocab_offset = 0;
-  row_init(r, pg, row, slot);
-  Cand *tail = reinterpret_cast<Cand *>(smem + FAST_SCRATCH);
-  SortScratch fs;
-  fs.mid = reinterpret_cast<Cand *>(smem);
-  fs.tmp = reinterpret_cast<uint32_t *>(smem + 16384);
-  fs.S = reinterpret_cast<uint64_t *>(smem + 24576);
-  fs.bcnt = reinterpret_cast<uint32_t *>(smem + 40960);
-  fs.boff = reinterpret_cast<uint32_t *>(smem + 45056);
+  row_init(r, p, row, slot, V_global);
+  const LeanScratch lean = lean_scratch(smem);
   float m = -INFINITY;
   uint32_t status = 0;
   for (int q = 0; q < tp_world; ++q) {
@@ -1412,40 +1667,43 @@ __global__ void __launch_bounds__(NT, 1)
   }
   status &= ~(uint32_t)MSTAR_STATUS_EMPTY;
   if (tid == 0) {
-    sh.tail_count = 0;
-    sh.min_gid = 0xFFFFFFFFu;
+    sh.nloc = 0;
     sh.res.token = 0;
+    sh.theta = 0.0f;
   }
-  __syncthreads();
   const bool empty = !(m > -INFINITY);
   const bool one = r.greedy || r.K == 1;
+  if (!empty && tid < 32) {
+    const float t = choose_theta(r, m);
+    if (tid == 0) sh.theta = t;
+  }
+  __syncthreads();
   if (!empty) {
-    if (!one) compute_thresholds<float>(r, m, sh);
-    const float xA = one ? m : sh.xA;
+    const float theta = sh.theta;
+    uint32_t best = 0xFFFFFFFFu;
     for (int q = 0; q < tp_world; ++q) {
       const uint32_t *rec = recv + ((int64_t)q * p.B + row) * rec_words;
       const int n = (int)min(rec[1], (uint32_t)tp_cap);
       for (int j = tid; j < n; j += NT) {
         const float x = __uint_as_float(rec[4 + 2 * j]);
         const uint32_t gid = rec[5 + 2 * j];
-        if (!(x >= xA)) continue;
         if (one) {
-          atomicMin(&sh.min_gid, gid);
-        } else {
-          const uint32_t idx = atomicAdd(&sh.tail_count, 1u);
-          if (idx < (uint32_t)TAIL_CAP) tail[idx] = Cand{x, gid};
+          if (x == m) best = min(best, gid);
+        } else if (x >= theta && pred_A(r, x, m)) {
+          const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+          if (idx < (uint32_t)TAIL_CAP) lean.cand[idx] = Cand{x, gid};
         }
       }
     }
-    __syncthreads();
     if (one) {
-      if (tid == 0) sh.res.token = sh.min_gid;
+      best = block_min_u32(best, sh);
+      if (tid == 0) sh.res.token = best;
     } else {
-      const int n = (int)min(sh.tail_count, (uint32_t)TAIL_CAP);
-      float u = p.uniforms ? p.uniforms[row]
-                           : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
-      tail_sort_scan(tail, n, m, fs, sh);
-      fast_resolve(r, tail, n, m, u, fs.S, sh);
+      __syncthreads();
+      const int n = (int)min(sh.nloc, (uint32_t)TAIL_CAP);
+      const float u = p.uniforms ? p.uniforms[row]
+                                 : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
+      lean_tail(r, n, m, theta, u, lean, sh, nullptr, 0);
     }
   }
   __syncthreads();
@@ -1455,7 +1713,7 @@ __global__ void __launch_bounds__(NT, 1)
       status |= MSTAR_STATUS_EMPTY;
       token = 0;
     }
-    write_row_outputs(p, row, slot, token, status, !empty);
+    write_row_outputs(p, row, slot, token, status);
   }
 }
 
@@ -1518,14 +1776,12 @@ static int max_smem_optin() {
 
 static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Plan &pl) {
   const int es = p->dtype == MSTAR_DTYPE_BF16 ? 2 : 4;
-  const int64_t row_bytes = (int64_t)p->V * es;
   const int spec_max = (p->hist_ids ? p->H : (p->seen_bits ? (p->seen_cap > 0 ? p->seen_cap : 2048) : 0)) +
                        (p->bias_ids ? p->NB : 0);
   const int spec_cap = std::max(16, spec_max);
   const int ht_cap = next_pow2(std::max(32, 2 * spec_cap));
   const int static_bytes = (int)sizeof(CtaSh);
   const int budget = max_smem_optin() - static_bytes - 1024;
-  int S = p->cluster_size;
   auto need = [&](int s, Plan &q) {
     int64_t slice = (p->V + s - 1) / s;
     slice = (slice + 63) / 64 * 64;
@@ -1533,41 +1789,39 @@ static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Pl
     q.es = es;
     q.slice = slice;
     const int64_t span_bytes = slice * es + 32;
-    q.data_bytes = (int)std::max<int64_t>(FAST_SCRATCH, (span_bytes + 127) / 128 * 128);
+    q.data_bytes = (int)std::max<int64_t>(LEAN_SCRATCH, (span_bytes + 127) / 128 * 128);
     const int64_t nvec = (span_bytes + 15) / 16;
     const int64_t positions = nvec * (16 / es);
     q.map_bytes = (int)(((positions + 31) / 32) * 4);
     q.map_bytes = (q.map_bytes + 127) / 128 * 128;
     q.ht_cap = ht_cap;
     q.spec_cap = spec_cap;
-    const int work = std::max(WORK_BYTES_MIN, 2 * q.map_bytes + ht_cap * 8);
+    const int work = 2 * q.map_bytes + std::max(WORK_BYTES_MIN, std::max(ht_cap * 8, QCAP * 4));
     q.off_work = q.data_bytes;
     q.off_spec = q.off_work + (work + 127) / 128 * 128;
-    q.off_tail = q.off_spec + (spec_cap * 8 + 127) / 128 * 128;
-    q.smem_bytes = q.off_tail + TAIL_CAP * 8;
+    q.off_lcand = q.off_spec + (spec_cap * 8 + 127) / 128 * 128;
+    q.off_bias = q.off_lcand + LCAP * 8;
+    const int bias_bytes = p->bias_ids && p->NB <= BIAS_SMEM ? BIAS_SMEM * 8 : 0;
+    q.smem_bytes = q.off_bias + bias_bytes;
     q.mode = mode;
     q.tp_cap = tp_cap;
     q.rec_words = 4 + 2 * tp_cap;
     return q.smem_bytes <= budget && slice * es <= (int64_t)MAX_CHUNKS * CHUNK_BYTES;
   };
-  if (S > 0) {
-    if (S > 16) return fail(MSTAR_ERR_INVALID, "cluster_size must be <= 16");
-    if (!need(S, pl)) return fail(MSTAR_ERR_UNSUPPORTED, "row does not fit the requested cluster size");
+  if (p->cluster_size > 0) {
+    if (p->cluster_size > 16) return fail(MSTAR_ERR_INVALID, "cluster_size must be <= 16");
+    if (!need(p->cluster_size, pl)) return fail(MSTAR_ERR_UNSUPPORTED, "row does not fit the requested cluster size");
     return MSTAR_OK;
   }
-  // smallest cluster whose slices fit; prefer <= 8 (portable)
   for (int s = 1; s <= 16; ++s) {
     if (need(s, pl)) return MSTAR_OK;
   }
-  (void)row_bytes;
   return fail(MSTAR_ERR_UNSUPPORTED, "row too large for a 16-CTA cluster");
 }
 
 template <typename T, int MODE>
 static int launch_T(const mstar_sampler_params_t *p, const Plan &pl, uint32_t *send, cudaStream_t st) {
   auto kern = sampler_kernel<T, MODE>;
-  static int configured_smem[2] = {0, 0};
-  (void)configured_smem;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.smem_bytes);
   if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   if (pl.S > 8) {
@@ -1631,13 +1885,15 @@ int mstar_sampler_step(const mstar_sampler_params_t *p, void *stream) {
 int32_t mstar_sampler_tp_record_words(int32_t tp_cap) { return 4 + 2 * tp_cap; }
 
 int mstar_sampler_tp_local(const mstar_sampler_params_t *p, int32_t tp_cap, uint32_t *send, void *stream) {
+  if (!p) return fail(MSTAR_ERR_INVALID, "params is NULL");
   mstar_sampler_params_t q = *p;
   if (!q.out_ids && !q.out_ids32) q.out_ids32 = reinterpret_cast<int32_t *>(send);  // not written in TP mode
   int rc = validate(&q);
   if (rc) return rc;
   if (!send) return fail(MSTAR_ERR_INVALID, "send is NULL");
   if (tp_cap < 1 || tp_cap > TAIL_CAP) return fail(MSTAR_ERR_INVALID, "tp_cap must be in [1, 2048]");
-  if (q.out_x || q.out_kept || q.out_probs) return fail(MSTAR_ERR_UNSUPPORTED, "dense debug outputs are single-shard only");
+  if (q.out_x || q.out_kept || q.out_probs)
+    return fail(MSTAR_ERR_UNSUPPORTED, "dense debug outputs are single-shard only");
   q.flags &= ~(MSTAR_FLAG_UPDATE_HISTORY | MSTAR_FLAG_UPDATE_SEEN | MSTAR_FLAG_ADVANCE_OFFSET);
   return launch(&q, 1, tp_cap, send, static_cast<cudaStream_t>(stream));
 }
@@ -1650,7 +1906,7 @@ int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int3
   if (tp_world < 1 || tp_world * tp_cap > TAIL_CAP)
     return fail(MSTAR_ERR_INVALID, "tp_world * tp_cap must be in [1, 2048]");
   if (V_global < p->V) return fail(MSTAR_ERR_INVALID, "V_global < V");
-  const int smem = FAST_SCRATCH + TAIL_CAP * 8;
+  const int smem = LEAN_SCRATCH;
   cudaError_t e = cudaFuncSetAttribute(tp_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   tp_merge_kernel<<<p->B, NT, smem, static_cast<cudaStream_t>(stream)>>>(*p, tp_cap, tp_world, 4 + 2 * tp_cap,

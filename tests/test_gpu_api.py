@@ -1,0 +1,120 @@
+"""GPU: the drop-in Python interface (mstar_rs_b200.sampling) against the
+oracle, eager and replayed from a captured CUDA graph the way the Orpheus
+engine captures its batched decode step (orpheus.py:322-366, :394-431)."""
+import numpy as np
+import pytest
+
+from mstar_rs_b200.workloads import Batch, pack_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg_rows(rng, n):
+    return dict(temperature=rng.uniform(0.3, 1.4, n).astype(np.float32),
+                top_k=rng.choice(np.array([0, 5, 40], np.int32), n),
+                top_p=rng.uniform(0.6, 1.0, n).astype(np.float32),
+                min_p=rng.choice(np.array([0.0, 0.02], np.float32), n),
+                rep_pen=rng.uniform(1.0, 1.4, n).astype(np.float32),
+                pres_pen=rng.uniform(0, 0.5, n).astype(np.float32),
+                freq_pen=rng.uniform(0, 0.5, n).astype(np.float32))
+
+
+def test_eager_sampler_matches_oracle(oracle_lib):
+    import torch
+
+    from mstar_rs_b200 import sampling
+
+    rng = np.random.default_rng(5)
+    n, V, H = 6, 5003, 32
+    cfg = _cfg_rows(rng, n)
+    seeds = rng.integers(0, 2**62, n).astype(np.uint64)
+    hist = rng.integers(0, V, (n, H)).astype(np.int32)
+    smp = sampling.Sampler(device="cuda", history=H)
+    rids = [f"q{i}" for i in range(n)]
+    for i, r in enumerate(rids):
+        smp.add_request(r)
+        smp.set_config(r, vocab_size=V, temperature=float(cfg["temperature"][i]), top_k=int(cfg["top_k"][i]),
+                       top_p=float(cfg["top_p"][i]), min_p=float(cfg["min_p"][i]),
+                       repetition_penalty=float(cfg["rep_pen"][i]),
+                       presence_penalty=float(cfg["pres_pen"][i]), frequency_penalty=float(cfg["freq_pen"][i]))
+        smp._sampling_config[r].set_seed(int(seeds[i]))
+        smp.set_history(r, hist[i].tolist())
+    hist_now = [list(h) for h in hist]
+    for step in range(3):
+        x = (rng.standard_normal((n, V)) * 2).astype(np.float32)
+        order = rng.permutation(n)
+        tok = smp.sample([rids[i] for i in order], torch.from_numpy(x[order]).cuda()).cpu().numpy()
+        case = Batch(logits=x[order], temperature=cfg["temperature"][order], top_k=cfg["top_k"][order],
+                     top_p=cfg["top_p"][order], min_p=cfg["min_p"][order], rep_pen=cfg["rep_pen"][order],
+                     pres_pen=cfg["pres_pen"][order], freq_pen=cfg["freq_pen"][order],
+                     hist_ids=np.array([hist_now[i][-H:] + [-1] * (H - len(hist_now[i][-H:])) for i in order],
+                                       np.int32),
+                     hist_len=np.array([min(len(hist_now[i]), H) for i in order], np.int32),
+                     seed=seeds[order], offset=np.full(n, step, np.uint64))
+        ref = oracle_lib.run(case)["ids"]
+        np.testing.assert_array_equal(tok, ref, err_msg=f"step {step}")
+        for j, i in enumerate(order):
+            hist_now[i].append(int(tok[j]))
+
+
+def test_graph_replay_matches_oracle(oracle_lib):
+    """SamplerBuffers + CudaGraphableSampler captured in a CUDA graph; the
+    per-row RNG offsets and seen bits advance in-graph across replays."""
+    import torch
+
+    from mstar_rs_b200 import sampling
+
+    rng = np.random.default_rng(9)
+    n, V = 4, 3001
+    cfg = _cfg_rows(rng, n)
+    seeds = rng.integers(0, 2**62, n).astype(np.uint64)
+    sbuf = sampling.SamplerBuffers.allocate(8, "cuda", vocab_size=V)
+    rids = [str(i) for i in range(n)]
+    masks = []
+    for i, r in enumerate(rids):
+        c = sampling.SamplingConfig(vocab_size=V, temperature=float(cfg["temperature"][i]),
+                                    top_k=int(cfg["top_k"][i]), top_p=float(cfg["top_p"][i]),
+                                    min_p=float(cfg["min_p"][i]), repetition_penalty=float(cfg["rep_pen"][i]),
+                                    presence_penalty=float(cfg["pres_pen"][i]),
+                                    frequency_penalty=float(cfg["freq_pen"][i]))
+        c.set_seed(int(seeds[i]))
+        sbuf.register_request(r, c)
+        m = sampling.SeenTokenMask.new(r, V, "cuda")
+        m.add_tokens(torch.tensor(rng.integers(0, V, 5), device="cuda"))
+        masks.append(m)
+    g_logits = torch.zeros(n, V, device="cuda")
+    g_out = torch.zeros(n, dtype=torch.int64, device="cuda")
+    sbuf.stage_seen_token_masks(rids, masks)
+    sampler = sbuf.gather_for_request_ids(rids, n, gather_seen_tokens=True)
+
+    def dec():
+        g_out.copy_(sampler.sample(rids, g_logits, apply_penalty=True))
+
+    saved_off = sbuf.offset_buf[:n].clone()
+    saved_seen = sbuf.seen_tokens.buf[:n].clone()
+    torch.cuda.synchronize()
+    for _ in range(2):
+        dec()
+    sbuf.offset_buf[:n].copy_(saved_off)
+    sbuf.seen_tokens.buf[:n].copy_(saved_seen)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        dec()
+    torch.cuda.synchronize()
+
+    seen_host = [m.to_bool().cpu().numpy() for m in masks]
+    for step in range(4):
+        x = (rng.standard_normal((n, V)) * 2).astype(np.float32)
+        g_logits.copy_(torch.from_numpy(x))
+        graph.replay()
+        tok = g_out.cpu().numpy()
+        case = Batch(logits=x, **{k: v for k, v in cfg.items()}, seen_bits=pack_bits(np.stack(seen_host)),
+                     seed=seeds, offset=np.full(n, step, np.uint64))
+        ref = oracle_lib.run(case)["ids"]
+        np.testing.assert_array_equal(tok, ref, err_msg=f"replay {step}")
+        for i in range(n):
+            seen_host[i][tok[i]] = True
+    sampler.sync_seen_token_masks(masks)
+    for i in range(n):
+        np.testing.assert_array_equal(masks[i].to_bool().cpu().numpy(), seen_host[i])
