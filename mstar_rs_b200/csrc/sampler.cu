@@ -50,22 +50,30 @@ namespace cg = cooperative_groups;
 
 namespace mstar {
 
-constexpr int NT = 512;             // threads per CTA
+constexpr int NT = 1024;            // threads per CTA
 constexpr int NWARP = NT / 32;
 constexpr int TAIL_CAP = 2048;      // candidates the fast tail resolves
 constexpr int LCAP = 2048;          // CTA-local candidate list
-constexpr int GCAP = 1024;          // candidates per locate round of the general path
-constexpr int NBIN = 1024;          // histogram bins per general-path round
-constexpr int NBK = 2048;           // buckets of the fast tail
-constexpr int GBK = 1024;           // buckets of the general-path sort
+constexpr int GCAP = 512;           // candidates per locate round of the general path
+constexpr int NBIN_LOG2 = 10;
+constexpr int NBIN = 1 << NBIN_LOG2;  // histogram bins per general-path round
+constexpr int NBK_LOG2 = 11;
+constexpr int NBK = 1 << NBK_LOG2;   // buckets of the fast tail
+constexpr int GBK_LOG2 = 9;
+constexpr int GBK = 1 << GBK_LOG2;   // buckets of the general-path sort
 constexpr int CHUNK_BYTES = 32768;  // bulk-copy granule (one mbarrier each)
 constexpr int MAX_CHUNKS = 8;       // slice data <= 256 KB
 constexpr int MAX_ROUNDS = 96;      // bound on general-path rounds
 constexpr int BIAS_SMEM = 256;      // bias entries staged in shared memory
 constexpr int QCAP = 2048;          // vectors queued by the candidate scan before draining
 constexpr int GQCAP = 1024;         // vectors queued per general-path round
-constexpr int WORK_BYTES_MIN = 52 * 1024;
+constexpr int GEN_BYTES = 12288 + 14336 + GCAP * 8 + GQCAP * 4;  // L1 | REF/sort | sort input | queue
+static_assert(NBIN * 12 <= 12288, "L1 / REF histograms");
+static_assert(GCAP * 20 + GBK * 8 <= 14336, "general sort scratch");
+static_assert(GBK <= NT && NBIN % NT == 0 && NBK % NT == 0 && TAIL_CAP % NT == 0, "per-thread splits");
+constexpr int WORK_BYTES_MIN = GEN_BYTES;
 constexpr int LEAN_SCRATCH = 72 * 1024;  // fast-tail scratch (the leader's data region)
+static_assert(TAIL_CAP * 24 + NBK * 12 <= LEAN_SCRATCH, "fast tail scratch");
 constexpr unsigned kWaitLimit = 1u << 24;
 
 struct __align__(8) Cand {
@@ -580,7 +588,7 @@ __device__ void lean_tail(const Row &r, int n, float m, float theta, float u, co
   const uint32_t km = okey(m);
   const uint32_t Dth = km - okey(theta);
   const int bits = Dth ? 32 - __clz((int)Dth) : 0;
-  const int dsh = bits > 11 ? bits - 11 : 0;
+  const int dsh = bits > NBK_LOG2 ? bits - NBK_LOG2 : 0;  // d >> dsh < NBK
   for (int b = threadIdx.x; b < NBK; b += NT) {
     s.bcnt[b] = 0;
     s.bmass[b] = 0;
@@ -730,7 +738,7 @@ __device__ void tail_sort_scan(Cand *in, int n, float m, const SortScratch &s, C
   block_minmax_u64(kmin, kmax, sh);
   const uint64_t span = n > 0 ? kmax - kmin : 0;
   const int bits = span ? 64 - __clzll((long long)span) : 0;
-  const int shift = bits > 10 ? bits - 10 : 0;
+  const int shift = bits > GBK_LOG2 ? bits - GBK_LOG2 : 0;  // (key - kmin) >> shift < GBK
   for (int b = threadIdx.x; b < GBK; b += NT) s.bcnt[b] = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += NT) {
@@ -739,22 +747,11 @@ __device__ void tail_sort_scan(Cand *in, int n, float m, const SortScratch &s, C
     s.tmp[i] = (b << 16) | pos;
   }
   __syncthreads();
-  {
-    constexpr int PER = GBK / NT;
-    uint32_t loc[PER];
-    uint32_t sum = 0;
-#pragma unroll
-    for (int q = 0; q < PER; ++q) {
-      loc[q] = s.bcnt[threadIdx.x * PER + q];
-      sum += loc[q];
-    }
+  {  // exclusive scan of the bucket counts (GBK <= NT: one bucket per thread)
+    const uint32_t c = threadIdx.x < GBK ? s.bcnt[threadIdx.x] : 0u;
     uint64_t tot;
-    uint32_t off = (uint32_t)block_exscan_u64(sum, tot, sh);
-#pragma unroll
-    for (int q = 0; q < PER; ++q) {
-      s.boff[threadIdx.x * PER + q] = off;
-      off += loc[q];
-    }
+    const uint32_t off = (uint32_t)block_exscan_u64(c, tot, sh);
+    if (threadIdx.x < GBK) s.boff[threadIdx.x] = off;
   }
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += NT) {
@@ -831,15 +828,15 @@ __device__ __forceinline__ Layout make_layout(uint8_t *smem, const Plan &pl) {
   uint8_t *g = L.work + 2 * pl.map_bytes;
   L.l1c = reinterpret_cast<uint32_t *>(g);
   L.l1m = reinterpret_cast<uint64_t *>(g + 4096);
-  L.refc = reinterpret_cast<uint32_t *>(g + 12288);
+  L.refc = reinterpret_cast<uint32_t *>(g + 12288);  // NBIN counts + NBIN masses
   L.refm = reinterpret_cast<uint64_t *>(g + 16384);
-  L.gsort.mid = reinterpret_cast<Cand *>(g + 12288);
-  L.gsort.tmp = reinterpret_cast<uint32_t *>(g + 20480);
-  L.gsort.S = reinterpret_cast<uint64_t *>(g + 24576);
-  L.gsort.bcnt = reinterpret_cast<uint32_t *>(g + 32768);
-  L.gsort.boff = reinterpret_cast<uint32_t *>(g + 36864);
-  L.gsort.in = reinterpret_cast<Cand *>(g + 40960);
-  L.gqueue = reinterpret_cast<int *>(g + 49152);  // general-path scan queue
+  L.gsort.mid = reinterpret_cast<Cand *>(g + 12288);  // aliases REF (14 KB)
+  L.gsort.tmp = reinterpret_cast<uint32_t *>(g + 12288 + GCAP * 8);
+  L.gsort.S = reinterpret_cast<uint64_t *>(g + 12288 + GCAP * 12);
+  L.gsort.bcnt = reinterpret_cast<uint32_t *>(g + 12288 + GCAP * 20);
+  L.gsort.boff = reinterpret_cast<uint32_t *>(g + 12288 + GCAP * 20 + GBK * 4);
+  L.gsort.in = reinterpret_cast<Cand *>(g + 12288 + 14336);
+  L.gqueue = reinterpret_cast<int *>(g + 12288 + 14336 + GCAP * 8);  // general-path scan queue
   return L;
 }
 
@@ -1275,7 +1272,7 @@ __global__ void __launch_bounds__(NT, 1)
               P.l1lo = 0;
               P.l1hi = ((uint64_t)DA << 32) | 0xFFFFFFFFull;
               const int bits = 64 - __clzll((long long)(P.l1hi - P.l1lo));
-              P.l1shift = bits > 10 ? bits - 10 : 0;
+              P.l1shift = bits > NBIN_LOG2 ? bits - NBIN_LOG2 : 0;
               P.l1nbins = (int)((P.l1hi - P.l1lo) >> P.l1shift) + 1;
               sh.cmd = Cmd{OP_HIST, TGT_L1, P.l1lo, P.l1hi, P.l1shift, P.l1nbins};
               P.state = ST_AFTER_L1;
@@ -1408,7 +1405,7 @@ __global__ void __launch_bounds__(NT, 1)
                   P.lo = blo;
                   P.hi = bhi;
                   const int bits = 64 - __clzll((long long)(bhi - blo));
-                  P.shift = bits > 10 ? bits - 10 : 0;
+                  P.shift = bits > NBIN_LOG2 ? bits - NBIN_LOG2 : 0;
                   P.nbins = (int)((bhi - blo) >> P.shift) + 1;
                   sh.cmd = Cmd{OP_HIST, TGT_REF, blo, bhi, P.shift, P.nbins};
                   P.state = ST_LOC_AFTER_REF;
