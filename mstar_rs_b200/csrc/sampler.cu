@@ -72,8 +72,10 @@ static_assert(NBIN * 12 <= 12288, "L1 / REF histograms");
 static_assert(GCAP * 20 + GBK * 8 <= 14336, "general sort scratch");
 static_assert(GBK <= NT && NBIN % NT == 0 && NBK % NT == 0 && TAIL_CAP % NT == 0, "per-thread splits");
 constexpr int WORK_BYTES_MIN = GEN_BYTES;
-constexpr int LEAN_SCRATCH = 72 * 1024;  // fast-tail scratch (the leader's data region)
-static_assert(TAIL_CAP * 24 + NBK * 12 <= LEAN_SCRATCH, "fast tail scratch");
+constexpr int LEAN_SCRATCH = 112 * 1024;  // fast-tail scratch (the leader's data region)
+constexpr int TW = 128;                  // threads of the fast tail (warps 0-3)
+static_assert(TAIL_CAP * 44 + NBK * 12 <= LEAN_SCRATCH, "fast tail scratch");
+static_assert(TW % 32 == 0 && TW <= NT, "tail threads");
 constexpr unsigned kWaitLimit = 1u << 24;
 
 struct __align__(8) Cand {
@@ -140,6 +142,14 @@ struct Result {
   int greedy, empty;
 };
 
+struct Row {
+  const void *rowp;
+  int64_t V, gbase;  // gbase = vocab_offset
+  float T, invT, Mp, P;
+  int K;             // 0 = off
+  bool greedy, topk, minp, topp;
+};
+
 struct CtaSh {
   uint64_t mbar[MAX_CHUNKS];
   uint32_t red_u32[NWARP];
@@ -154,6 +164,13 @@ struct CtaSh {
   uint32_t ht_fail;
   uint32_t qcount;
   float theta;
+  float m;
+  int fast;
+  uint32_t ncand;
+  uint32_t goff[16], gcnt[16];
+  uint32_t min_all;
+  int nemit;
+  Row row;
   int tp_ovf;
   int bcast_i;
   uint64_t bcast_u64;
@@ -399,13 +416,7 @@ __device__ __forceinline__ void block_exscan2_u64(uint64_t a, uint64_t b, uint64
 
 // ---------------------------------------------------------- row context
 
-struct Row {
-  const void *rowp;
-  int64_t V, gbase;  // gbase = vocab_offset
-  float T, invT, Mp, P;
-  int K;             // 0 = off
-  bool greedy, topk, minp, topp;
-};
+
 
 __device__ __forceinline__ void row_init(Row &r, const mstar_sampler_params_t &p, int row, int slot, int64_t V) {
   r.V = V;
@@ -430,6 +441,14 @@ __device__ __forceinline__ bool pred_A(const Row &r, float x, float m) {
   const float e = spec_e(x, m);
   if (spec_w_from_e(e) == 0) return false;
   return !r.minp || e >= r.Mp;
+}
+
+// Same predicate, also returning the fixed-point weight (0 when false).
+__device__ __forceinline__ uint64_t weight_A(const Row &r, float x, float m) {
+  const float e = spec_e(x, m);
+  const uint64_t w = spec_w_from_e(e);
+  if (w == 0 || (r.minp && !(e >= r.Mp))) return 0;
+  return w;
 }
 
 __device__ __forceinline__ float prev_float(float t) {
@@ -489,7 +508,7 @@ __device__ __forceinline__ uint4 load_masked(const Slice &sl, int k) {
 }
 
 // Iterate the value-A elements this CTA holds (resident vectors and the
-// special list), applying the exact predicate; fn(x, gid).  Phase 1 streams
+// special list), applying the exact predicate; fn(x, gid, w).  Phase 1 streams
 // every vector and queues (warp-aggregated) the few whose transformed max
 // reaches theta; phase 2 drains the queue one vector per thread.  If the
 // queue overflows, phase 2 rescans everything directly.  Block-wide.
@@ -538,7 +557,10 @@ __device__ __forceinline__ void for_each_value(const Slice &sl, const Cand *spec
     for (int j = 0; j < VEC; ++j) {
       const float raw = Elem<T>::get(v, j);
       const float x = r.greedy ? raw : __fmul_rn(raw, r.invT);
-      if (x >= theta && pred_A(r, x, m)) fn(x, gid0 + (uint32_t)j);
+      if (x >= theta) {
+        const uint64_t w = weight_A(r, x, m);
+        if (w) fn(x, gid0 + (uint32_t)j, w);
+      }
     }
   };
   if (nq <= (uint32_t)qcap) {
@@ -551,169 +573,14 @@ __device__ __forceinline__ void for_each_value(const Slice &sl, const Cand *spec
   }
   for (int i = threadIdx.x; i < nspec; i += NT) {
     const Cand c = spec[i];
-    if (c.x >= theta && pred_A(r, c.x, m)) fn(c.x, c.gid);
+    if (c.x >= theta) {
+      const uint64_t w = weight_A(r, c.x, m);
+      if (w) fn(c.x, c.gid, w);
+    }
   }
 }
 
 // ------------------------------------------------------------- fast tail
-
-struct LeanScratch {
-  Cand *cand;       // [TAIL_CAP]
-  uint32_t *bcnt;   // [NBK]
-  uint64_t *bmass;  // [NBK]
-  uint64_t *skey;   // [TAIL_CAP]
-  uint64_t *sw;     // [TAIL_CAP]
-};
-
-__device__ __forceinline__ LeanScratch lean_scratch(uint8_t *base) {
-  LeanScratch s;
-  s.cand = reinterpret_cast<Cand *>(base);
-  s.bcnt = reinterpret_cast<uint32_t *>(base + TAIL_CAP * 8);
-  s.bmass = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 8 + NBK * 4);
-  s.skey = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 8 + NBK * 12);
-  s.sw = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 16 + NBK * 12);
-  return s;
-}
-
-// Resolve top_k / top_p / the draw over n value-A candidates s.cand[0..n)
-// (any order; all x >= theta; all of A among them).  Bucket counting on the
-// order key, exclusive scans of bucket counts and masses, rank inside the
-// bucket, then each query is answered by the one candidate that straddles
-// it.  Block-wide.  With rec != nullptr (TP shard) the first `nemit`
-// candidates in order are written to rec instead.
-__device__ void lean_tail(const Row &r, int n, float m, float theta, float u, const LeanScratch &s, CtaSh &sh,
-                          uint32_t *rec, int nemit) {
-  constexpr int PER = TAIL_CAP / NT;
-  constexpr int BPT = NBK / NT;
-  const uint32_t km = okey(m);
-  const uint32_t Dth = km - okey(theta);
-  const int bits = Dth ? 32 - __clz((int)Dth) : 0;
-  const int dsh = bits > NBK_LOG2 ? bits - NBK_LOG2 : 0;  // d >> dsh < NBK
-  for (int b = threadIdx.x; b < NBK; b += NT) {
-    s.bcnt[b] = 0;
-    s.bmass[b] = 0;
-  }
-  __syncthreads();
-  uint64_t key[PER], w[PER];
-  uint32_t bk[PER], pos[PER];
-  float xv[PER];
-#pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i = threadIdx.x + q * NT;
-    if (i < n) {
-      const Cand c = s.cand[i];
-      const uint32_t d = km - okey(c.x);
-      key[q] = ((uint64_t)d << 32) | c.gid;
-      w[q] = spec_w_from_e(spec_e(c.x, m));
-      xv[q] = c.x;
-      bk[q] = min(d >> dsh, (uint32_t)(NBK - 1));
-      pos[q] = atomicAdd(&s.bcnt[bk[q]], 1u);
-      atomicAdd((unsigned long long *)&s.bmass[bk[q]], (unsigned long long)w[q]);
-    }
-  }
-  __syncthreads();
-  uint64_t tot_c, tot_m;
-  {
-    uint32_t lc[BPT];
-    uint64_t lm[BPT], sc = 0, sm = 0;
-#pragma unroll
-    for (int q = 0; q < BPT; ++q) {
-      lc[q] = s.bcnt[threadIdx.x * BPT + q];
-      lm[q] = s.bmass[threadIdx.x * BPT + q];
-      sc += lc[q];
-      sm += lm[q];
-    }
-    uint64_t pc, pm;
-    block_exscan2_u64(sc, sm, pc, pm, tot_c, tot_m, sh);
-#pragma unroll
-    for (int q = 0; q < BPT; ++q) {  // inclusive prefixes
-      pc += lc[q];
-      pm += lm[q];
-      s.bcnt[threadIdx.x * BPT + q] = (uint32_t)pc;
-      s.bmass[threadIdx.x * BPT + q] = pm;
-    }
-  }
-  __syncthreads();
-#pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i = threadIdx.x + q * NT;
-    if (i < n) {
-      const uint32_t lo = bk[q] ? s.bcnt[bk[q] - 1] : 0u;
-      s.skey[lo + pos[q]] = key[q];
-      s.sw[lo + pos[q]] = w[q];
-    }
-  }
-  __syncthreads();
-  uint32_t rank[PER];
-  uint64_t Sx[PER];
-#pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i = threadIdx.x + q * NT;
-    rank[q] = 0xFFFFFFFFu;
-    Sx[q] = 0;
-    if (i < n) {
-      const uint32_t lo = bk[q] ? s.bcnt[bk[q] - 1] : 0u, hi = s.bcnt[bk[q]];
-      uint32_t rin = 0;
-      uint64_t min_ = 0;
-      for (uint32_t j = lo; j < hi; ++j) {
-        if (s.skey[j] < key[q]) {
-          ++rin;
-          min_ += s.sw[j];
-        }
-      }
-      rank[q] = lo + rin;
-      Sx[q] = (bk[q] ? s.bmass[bk[q] - 1] : 0ull) + min_;
-    }
-  }
-  const int nA = r.topk ? min(n, r.K) : n;
-  if (rec) {  // TP shard: emit the first nemit candidates in order
-#pragma unroll
-    for (int q = 0; q < PER; ++q) {
-      const int i = threadIdx.x + q * NT;
-      if (i < n && (int)rank[q] < nemit) {
-        rec[4 + 2 * rank[q]] = __float_as_uint(xv[q]);
-        rec[5 + 2 * rank[q]] = (uint32_t)(key[q] & 0xFFFFFFFFu);
-      }
-    }
-    __syncthreads();
-    return;
-  }
-  uint64_t WA = tot_m;
-  if (nA < n) {
-#pragma unroll
-    for (int q = 0; q < PER; ++q) {
-      const int i = threadIdx.x + q * NT;
-      if (i < n && (int)rank[q] == nA - 1) sh.bcast_u64 = Sx[q] + w[q];
-    }
-    __syncthreads();
-    WA = sh.bcast_u64;
-  }
-  const double thr = __dmul_rn((double)r.P, (double)WA);
-#pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i = threadIdx.x + q * NT;
-    if (i < n && (int)rank[q] < nA) {
-      const bool kept = rank[q] == 0 || !r.topp || (double)Sx[q] < thr;
-      const bool last = kept && ((int)rank[q] == nA - 1 || (r.topp && !((double)(Sx[q] + w[q]) < thr)));
-      if (last) {
-        sh.res.WK = Sx[q] + w[q];
-        sh.res.ckK = key[q];
-        sh.bcast_i = (int)rank[q] + 1;
-      }
-    }
-  }
-  __syncthreads();
-  const uint64_t WK = sh.res.WK;
-  const int nK = sh.bcast_i;
-  const uint64_t rr = draw_point(u, WK);
-#pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i = threadIdx.x + q * NT;
-    if (i < n && (int)rank[q] < nK && Sx[q] <= rr && rr < Sx[q] + w[q])
-      sh.res.token = (uint32_t)(key[q] & 0xFFFFFFFFu);
-  }
-  __syncthreads();
-}
 
 // --------------------------------------------------- general-path sort
 
@@ -894,6 +761,157 @@ __device__ __forceinline__ void write_row_outputs(const mstar_sampler_params_t &
   }
 }
 
+// --------------------------------------------------------- 4-warp fast tail
+
+__device__ __forceinline__ void tbar() { asm volatile("bar.sync 1, %0;" ::"n"(TW) : "memory"); }
+
+struct TailScr {
+  uint64_t *K;   // [TAIL_CAP] order key per candidate (gathered order)
+  uint64_t *W;   // [TAIL_CAP] weight per candidate
+  uint32_t *P;   // [TAIL_CAP] bucket << 16 | position, then rank
+  uint64_t *RK;  // [TAIL_CAP] keys: bucket order, then rank order
+  uint64_t *RW;  // [TAIL_CAP] weights: bucket order, then rank order
+  uint64_t *RS;  // [TAIL_CAP] exclusive weight prefix in rank order
+  uint32_t *bc;  // [NBK] bucket counts -> inclusive prefix
+  uint64_t *bm;  // [NBK] bucket masses -> inclusive prefix
+};
+
+__device__ __forceinline__ TailScr tail_scratch(uint8_t *base) {
+  TailScr t;
+  t.K = reinterpret_cast<uint64_t *>(base);
+  t.W = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 8);
+  t.RK = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 16);
+  t.RW = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 24);
+  t.RS = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 32);
+  t.P = reinterpret_cast<uint32_t *>(base + TAIL_CAP * 40);
+  t.bc = reinterpret_cast<uint32_t *>(base + TAIL_CAP * 44);
+  t.bm = reinterpret_cast<uint64_t *>(base + TAIL_CAP * 44 + NBK * 4);
+  return t;
+}
+
+// Sort the n candidates in s.K / s.W (order key ascending = x descending,
+// id ascending; keys are distinct) on TW threads: bucket counts of the top
+// key bits, one scan, scatter, rank inside each bucket; leaves keys,
+// weights and exclusive weight prefixes in rank order in s.RK / s.RW / s.RS.
+// Dth bounds the distance key d (top 32 key bits).  Called by threads
+// [0, TW) only; synchronises them with named barrier 1.
+__device__ void tail_sort_small(int n, uint32_t Dth, const TailScr &s, CtaSh &sh) {
+  const int t = threadIdx.x;
+  int nbl = 6;
+  while (nbl < NBK_LOG2 && (1 << nbl) < 2 * n) ++nbl;
+  const int NB = 1 << nbl;
+  const int dbits = Dth ? 32 - __clz((int)Dth) : 0;
+  const int dsh = dbits > nbl ? dbits - nbl : 0;
+  for (int b = t; b < NB; b += TW) {
+    s.bc[b] = 0;
+    s.bm[b] = 0;
+  }
+  tbar();
+  for (int i = t; i < n; i += TW) {
+    const uint32_t b = min((uint32_t)(s.K[i] >> 32) >> dsh, (uint32_t)(NB - 1));
+    const uint32_t pos = atomicAdd(&s.bc[b], 1u);
+    atomicAdd((unsigned long long *)&s.bm[b], (unsigned long long)s.W[i]);
+    s.P[i] = (b << 16) | pos;
+  }
+  tbar();
+  {  // inclusive scans of counts and masses over NB buckets, NB / TW per thread
+    const int per = (NB + TW - 1) / TW;
+    const int b0 = min(NB, t * per), b1 = min(NB, b0 + per);
+    uint32_t c = 0;
+    uint64_t mm = 0;
+    for (int b = b0; b < b1; ++b) {
+      c += s.bc[b];
+      mm += s.bm[b];
+    }
+    const int lane = t & 31, wid = t >> 5;
+    uint32_t ic = c;
+    uint64_t im = mm;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t uc = __shfl_up_sync(~0u, ic, o);
+      const uint64_t um = __shfl_up_sync(~0u, (unsigned long long)im, o);
+      if (lane >= o) {
+        ic += uc;
+        im += um;
+      }
+    }
+    if (lane == 31) {
+      sh.red_u32[wid] = ic;
+      sh.red_u64[wid] = im;
+    }
+    tbar();
+    uint32_t oc = ic - c;
+    uint64_t om = im - mm;
+    for (int w = 0; w < wid; ++w) {
+      oc += sh.red_u32[w];
+      om += sh.red_u64[w];
+    }
+    for (int b = b0; b < b1; ++b) {
+      oc += s.bc[b];
+      om += s.bm[b];
+      s.bc[b] = oc;
+      s.bm[b] = om;
+    }
+  }
+  tbar();
+  for (int i = t; i < n; i += TW) {
+    const uint32_t b = s.P[i] >> 16, pos = s.P[i] & 0xFFFFu;
+    const uint32_t lo = b ? s.bc[b - 1] : 0u;
+    s.RK[lo + pos] = s.K[i];
+    s.RW[lo + pos] = s.W[i];
+  }
+  tbar();
+  for (int i = t; i < n; i += TW) {  // rank inside the bucket
+    const uint32_t b = s.P[i] >> 16;
+    const uint32_t lo = b ? s.bc[b - 1] : 0u, hi = s.bc[b];
+    const uint64_t key = s.K[i];
+    uint32_t rin = 0;
+    uint64_t before = b ? s.bm[b - 1] : 0ull;
+    for (uint32_t j = lo; j < hi; ++j) {
+      if (s.RK[j] < key) {
+        ++rin;
+        before += s.RW[j];
+      }
+    }
+    s.P[i] = lo + rin;
+    s.RS[lo + rin] = before;
+  }
+  tbar();
+  for (int i = t; i < n; i += TW) {  // keys and weights into rank order
+    s.RK[s.P[i]] = s.K[i];
+    s.RW[s.P[i]] = s.W[i];
+  }
+  tbar();
+}
+
+// Queries over the rank-ordered candidates (one thread): top_k, top_p,
+// the inverse-CDF draw.  Writes res.token / res.WK / res.ckK.
+__device__ void tail_resolve(const Row &r, int n, float u, const TailScr &s, Result &res) {
+  const int nA = r.topk ? min(n, r.K) : n;
+  const uint64_t WA = s.RS[nA - 1] + s.RW[nA - 1];
+  int nK = nA;
+  if (r.topp) {
+    const double thr = __dmul_rn((double)r.P, (double)WA);
+    int lo = 0, hi = nA;  // count of ranks j < nA with (double)RS[j] < thr (a prefix)
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if ((double)s.RS[mid] < thr) lo = mid + 1;
+      else hi = mid;
+    }
+    nK = max(lo, 1);
+  }
+  const uint64_t WK = s.RS[nK - 1] + s.RW[nK - 1];
+  const uint64_t rr = draw_point(u, WK);
+  int lo = 0, hi = nK - 1;  // largest j with RS[j] <= rr
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s.RS[mid] <= rr) lo = mid;
+    else hi = mid - 1;
+  }
+  res.token = (uint32_t)(s.RK[lo] & 0xFFFFFFFFu);
+  res.WK = WK;
+  res.ckK = s.RK[nK - 1];
+}
+
 // ------------------------------------------------------------ the kernel
 
 template <typename T, int MODE>
@@ -972,11 +990,12 @@ __global__ void __launch_bounds__(NT, 1)
     sh.n_spec = 0;
     sh.ht_fail = 0;
     sh.tp_ovf = 0;
+    sh.nemit = 0;
+    row_init(sh.row, p, row, slot, p.V);  // staged once; read by all after setup
   }
 
-  Row r;
-  row_init(r, p, row, slot, p.V);
-  const int64_t pos0_gid = r.gbase + c0al;  // gid of data position 0
+  const int64_t gbase = p.vocab_offset;
+  const int64_t pos0_gid = gbase + c0al;  // gid of data position 0
   const bool has_hist = p.hist_ids && p.hist_len;
   const bool has_spec = has_hist || p.seen_bits || p.bias_ids;
 
@@ -1002,7 +1021,7 @@ __global__ void __launch_bounds__(NT, 1)
       }
       uint32_t dis = 0u;
       if (aw && inmask) {
-        const uint32_t bits = allowed32(aw, p.allowed_words, r.gbase + e0 + lo_in) << lo_in;
+        const uint32_t bits = allowed32(aw, p.allowed_words, gbase + e0 + lo_in) << lo_in;
         dis = inmask & ~bits;
       }
       mask32[wi] = ~inmask | dis;
@@ -1034,7 +1053,7 @@ __global__ void __launch_bounds__(NT, 1)
     const int n = min(len, p.H);
     const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
     for (int j = tid; j < n; j += NT) {
-      const int64_t e = (int64_t)h[j] - r.gbase;
+      const int64_t e = (int64_t)h[j] - gbase;
       if (e >= c0 && e < c1) {
         if (!ht_insert(L.ht, pl.ht_cap, (int)e, 1)) sh.ht_fail = 1;
         atomicOr(&spec32[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
@@ -1042,7 +1061,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
   } else if (p.seen_bits) {
     const uint32_t *sw = p.seen_bits + (int64_t)slot * p.seen_words;
-    const int64_t g0 = r.gbase + c0, g1 = r.gbase + c1;
+    const int64_t g0 = gbase + c0, g1 = gbase + c1;
     if (g1 > g0) {
       for (int64_t w = (g0 >> 5) + tid; w <= ((g1 - 1) >> 5); w += NT) {
         uint32_t bits = sw[w];
@@ -1051,7 +1070,7 @@ __global__ void __launch_bounds__(NT, 1)
           bits &= bits - 1;
           const int64_t g = (w << 5) + b;
           if (g < g0 || g >= g1) continue;
-          const int64_t e = g - r.gbase;
+          const int64_t e = g - gbase;
           if (!ht_insert(L.ht, pl.ht_cap, (int)e, 1)) sh.ht_fail = 1;
           atomicOr(&spec32[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
         }
@@ -1063,7 +1082,7 @@ __global__ void __launch_bounds__(NT, 1)
     for (int j = tid; j < p.NB; j += NT) {
       const int32_t g = bi[j];
       if (g < 0) continue;
-      const int64_t e = (int64_t)g - r.gbase;
+      const int64_t e = (int64_t)g - gbase;
       if (e >= c0 && e < c1) {
         if (!ht_insert(L.ht, pl.ht_cap, (int)e, 0)) sh.ht_fail = 1;
         atomicOr(&spec32[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
@@ -1071,6 +1090,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
   }
   __syncthreads();  // bitmaps, table, fringe vectors complete
+  const Row r = sh.row;
 
   // ---- pass A: patch + raw max, chunk by chunk as the bulk copies land
   float rawmax = -INFINITY;
@@ -1151,49 +1171,69 @@ __global__ void __launch_bounds__(NT, 1)
   const Slice sl{data4, L.map_mask, L.map_spec, nvec, has_spec, pos0_gid};
   cluster.sync();  // #1: maxima published
 
-  // ---- row max, threshold, pass C
-  float m = -INFINITY;
-  for (int q = 0; q < S; ++q) m = fmaxf(m, *cluster.map_shared_rank(&sh.cta_max, q));
+  // ---- row max and threshold (warp 0), pass C (all warps)
+  const int lane = tid & 31;
+  if (tid < 32) {
+    float mm = lane < S ? *cluster.map_shared_rank(&sh.cta_max, lane) : -INFINITY;
+    for (int o = 16; o; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(~0u, mm, o));
+    const float th = mm > -INFINITY ? choose_theta(r, mm) : INFINITY;
+    if (lane == 0) {
+      sh.m = mm;
+      sh.theta = th;
+    }
+  }
+  __syncthreads();
+  const float m = sh.m;
   const bool empty = !(m > -INFINITY);
   const bool one = r.greedy || r.K == 1;
+  const float theta = sh.theta;
   if (!empty) {
-    if (tid < 32) {
-      const float t = choose_theta(r, m);
-      if (tid == 0) sh.theta = t;
-    }
-    __syncthreads();
-    const float theta = sh.theta;
     if (one) {
       uint32_t best = 0xFFFFFFFFu;
       for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.queue, QCAP, &sh.qcount,
-                        [&](float x, uint32_t gid) { best = min(best, gid); });
+                        [&](float x, uint32_t gid, uint64_t w) { best = min(best, gid); });
       best = block_min_u32(best, sh);
       if (tid == 0) sh.min_gid = best;
     } else {
-      for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.queue, QCAP, &sh.qcount, [&](float x, uint32_t gid) {
-        const uint32_t idx = atomicAdd(&sh.nloc, 1u);
-        if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
-      });
+      for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.queue, QCAP, &sh.qcount,
+                        [&](float x, uint32_t gid, uint64_t w) {
+                          const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+                          if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
+                        });
     }
   }
   cluster.sync();  // #2: local candidate lists complete
 
-  // every CTA takes the same decision from the published counts
-  uint32_t ncand = 0, status_all = 0;
-  bool lovf = false;
-  for (int q = 0; q < S; ++q) {
-    const CtaSh *peer = cluster.map_shared_rank(&sh, q);
-    const uint32_t c = peer->nloc;
-    lovf |= c > (uint32_t)LCAP;
-    ncand += min(c, (uint32_t)LCAP);
-    status_all |= peer->status;
-  }
-  const float theta = empty ? INFINITY : sh.theta;
+  // every CTA takes the same decision from the published counts (warp 0)
   const bool force_general = (p.flags & MSTAR_FLAG_FORCE_GENERAL) != 0;
-  const bool fast = empty || one || (!lovf && ncand <= (uint32_t)TAIL_CAP && !force_general);
-  float u = 0.0f;
-  if (rank == 0) {
-    if (tid == 0) {
+  if (tid < 32) {
+    uint32_t c = 0, st = 0, mg = 0xFFFFFFFFu;
+    if (lane < S) {
+      const CtaSh *peer = cluster.map_shared_rank(&sh, lane);
+      c = peer->nloc;
+      st = peer->status;
+      mg = peer->min_gid;
+    }
+    const bool lovf = __any_sync(~0u, c > (uint32_t)LCAP);
+    const uint32_t cc = min(c, (uint32_t)LCAP);
+    uint32_t inc = cc;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(~0u, inc, o);
+      if (lane >= o) inc += v;
+    }
+    const uint32_t total = __shfl_sync(~0u, inc, 31);
+    for (int o = 16; o; o >>= 1) {
+      st |= __shfl_xor_sync(~0u, st, o);
+      mg = min(mg, __shfl_xor_sync(~0u, mg, o));
+    }
+    if (lane < 16) {
+      sh.goff[lane] = inc - cc;
+      sh.gcnt[lane] = cc;
+    }
+    if (lane == 0) {
+      sh.ncand = total;
+      sh.min_all = mg;
+      sh.fast = empty || one || (!lovf && total <= (uint32_t)TAIL_CAP && !force_general);
       sh.res.m = m;
       sh.res.theta = theta;
       sh.res.greedy = r.greedy;
@@ -1201,53 +1241,58 @@ __global__ void __launch_bounds__(NT, 1)
       sh.res.token = 0;
       sh.res.WK = 0;
       sh.res.ckK = 0;
-      sh.res.status = status_all;
-    }
-    if (!empty && !one) {
-      if (p.uniforms) u = p.uniforms[row];
-      else u = philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
+      sh.res.status = st;
     }
   }
+  __syncthreads();
+  const bool fast = sh.fast;
   uint32_t *rec = MODE == 1 ? tp_send + (int64_t)row * pl.rec_words : nullptr;
-  int nemit = 0;                                  // TP: candidates emitted in order
-  const LeanScratch lean = lean_scratch(L.data);  // the leader's slice data is dead by then
-
-  // Leader: gather every CTA's list into dst (DSMEM reads); returns the count.
-  auto gather = [&](Cand *dst, int cap) -> int {
-    int off = 0;
+  const uint32_t km = okey(m);
+  auto draw_u = [&]() -> float {
+    if (p.uniforms) return p.uniforms[row];
+    return philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
+  };
+  // Leader, threads [0, TW): gather every CTA's list (DSMEM) as keys and
+  // weights, sort it, then resolve the queries (step) or emit the first
+  // candidates in order (TP shard).  cnt/off describe the lists.
+  auto small_tail = [&](const uint32_t *cnt, const uint32_t *off, int n) {
+    const TailScr ts = tail_scratch(L.data);  // the leader's slice data is dead by then
     for (int q = 0; q < S; ++q) {
-      const CtaSh *peer = cluster.map_shared_rank(&sh, q);
-      const int c = (int)min(peer->nloc, (uint32_t)LCAP);
       const Cand *src = cluster.map_shared_rank(L.lcand, q);
-      for (int i = tid; i < c; i += NT)
-        if (off + i < cap) dst[off + i] = src[i];
-      off += c;
+      const int c = (int)cnt[q], o = (int)off[q];
+      for (int i = tid; i < c; i += TW) {
+        const Cand cd = src[i];
+        ts.K[o + i] = ckey(km, cd.x, cd.gid);
+        ts.W[o + i] = spec_w_from_e(spec_e(cd.x, m));
+      }
     }
-    __syncthreads();
-    return min(off, cap);
+    tbar();
+    tail_sort_small(n, km - okey(theta), ts, sh);
+    if (MODE == 0) {
+      if (tid == 0) tail_resolve(r, n, draw_u(), ts, sh.res);
+    } else {
+      const int ne = r.topk ? min(n, r.K) : n;
+      if (tid == 0) sh.nemit = ne;
+      if (ne <= pl.tp_cap) {
+        for (int j = tid; j < ne; j += TW) {
+          rec[4 + 2 * j] = __float_as_uint(okey_inv(km - (uint32_t)(ts.RK[j] >> 32)));
+          rec[5 + 2 * j] = (uint32_t)(ts.RK[j] & 0xFFFFFFFFu);
+        }
+      }
+    }
   };
 
   if (fast) {
     if (rank == 0 && !empty) {
-      __syncthreads();
       if (one) {
         if (tid == 0) {
-          uint32_t best = 0xFFFFFFFFu;
-          for (int q = 0; q < S; ++q) best = min(best, cluster.map_shared_rank(&sh, q)->min_gid);
-          sh.res.token = best;
+          sh.res.token = sh.min_all;
           sh.res.WK = 4294967296ull;
-          sh.res.ckK = (uint64_t)best;
+          sh.res.ckK = (uint64_t)sh.min_all;
+          sh.nemit = -1;
         }
-        __syncthreads();
-        nemit = -1;
-      } else {
-        const int n = gather(lean.cand, TAIL_CAP);
-        if (MODE == 0) {
-          lean_tail(r, n, m, theta, u, lean, sh, nullptr, 0);
-        } else {
-          nemit = r.topk ? min(n, r.K) : n;
-          if (nemit <= pl.tp_cap) lean_tail(r, n, m, theta, u, lean, sh, rec, nemit);
-        }
+      } else if (tid < TW) {
+        small_tail(sh.gcnt, sh.goff, (int)sh.ncand);
       }
     }
   } else {
@@ -1258,7 +1303,7 @@ __global__ void __launch_bounds__(NT, 1)
       P.state = ST_START;
       sh.res.status |= MSTAR_STATUS_GENERAL;
     }
-    const uint32_t km = okey(m);
+    const float u = rank == 0 && !empty ? draw_u() : 0.0f;
     for (int round = 0; round < MAX_ROUNDS; ++round) {
       if (rank == 0) {
         // ================= leader planning (block-wide) =================
@@ -1423,19 +1468,37 @@ __global__ void __launch_bounds__(NT, 1)
             break;
           }
           if (state == ST_AFTER_PREFIX) {
-            const int n = gather(lean.cand, TAIL_CAP);
-            if (MODE == 0) {
-              lean_tail(r, n, m, theta, u, lean, sh, nullptr, 0);
-            } else {
-              nemit = r.topk ? min(n, r.K) : n;
-              if (nemit <= pl.tp_cap) lean_tail(r, n, m, theta, u, lean, sh, rec, nemit);
+            if (tid < 32) {  // per-CTA counts of the compacted range
+              const uint32_t c = lane < S ? min(cluster.map_shared_rank(&sh, lane)->nloc, (uint32_t)LCAP) : 0u;
+              uint32_t inc = c;
+              for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t v = __shfl_up_sync(~0u, inc, o);
+                if (lane >= o) inc += v;
+              }
+              if (lane < 16) {
+                sh.goff[lane] = inc - c;
+                sh.gcnt[lane] = c;
+              }
+              const uint32_t tot = __shfl_sync(~0u, inc, 31);
+              if (lane == 0) sh.ncand = min(tot, (uint32_t)TAIL_CAP);
             }
+            __syncthreads();
+            if (tid < TW) small_tail(sh.gcnt, sh.goff, (int)sh.ncand);
             if (tid == 0) P.state = ST_FINISH;
             __syncthreads();
             continue;
           }
           if (state == ST_LOC_AFTER_COMPACT) {
-            const int n = gather(L.gsort.in, GCAP);
+            int n = 0;
+            for (int q = 0; q < S; ++q) {  // gather every CTA's list (DSMEM)
+              const int c = (int)min(cluster.map_shared_rank(&sh, q)->nloc, (uint32_t)LCAP);
+              const Cand *src = cluster.map_shared_rank(L.lcand, q);
+              for (int i = tid; i < c; i += NT)
+                if (n + i < GCAP) L.gsort.in[n + i] = src[i];
+              n += c;
+            }
+            n = min(n, GCAP);
+            __syncthreads();
             tail_sort_scan(L.gsort.in, n, m, L.gsort, sh);
             const uint64_t *Sx = L.gsort.S;
             const Cand *sorted = L.gsort.in;
@@ -1529,13 +1592,14 @@ __global__ void __launch_bounds__(NT, 1)
           }
           __syncthreads();
         }
-        for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount, [&](float x, uint32_t gid) {
-          const uint64_t ck = ckey(km, x, gid);
-          if (ck < cmd.lo || ck > cmd.hi) return;
-          const int b = (int)((ck - cmd.lo) >> cmd.shift);
-          atomicAdd(&hc[b], 1u);
-          atomicAdd((unsigned long long *)&hm[b], (unsigned long long)spec_w_from_e(spec_e(x, m)));
-        });
+        for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount,
+                          [&](float x, uint32_t gid, uint64_t w) {
+                            const uint64_t ck = ckey(km, x, gid);
+                            if (ck < cmd.lo || ck > cmd.hi) return;
+                            const int b = (int)((ck - cmd.lo) >> cmd.shift);
+                            atomicAdd(&hc[b], 1u);
+                            atomicAdd((unsigned long long *)&hm[b], (unsigned long long)w);
+                          });
         if (rank != 0) {
           __syncthreads();
           uint32_t *rc = cluster.map_shared_rank(cmd.target == TGT_L1 ? L.l1c : L.refc, 0);
@@ -1550,12 +1614,13 @@ __global__ void __launch_bounds__(NT, 1)
       } else {  // OP_COMPACT into the CTA-local list
         if (tid == 0) sh.nloc = 0;
         __syncthreads();
-        for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount, [&](float x, uint32_t gid) {
-          const uint64_t ck = ckey(km, x, gid);
-          if (ck < cmd.lo || ck > cmd.hi) return;
-          const uint32_t idx = atomicAdd(&sh.nloc, 1u);
-          if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
-        });
+        for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount,
+                          [&](float x, uint32_t gid, uint64_t w) {
+                            const uint64_t ck = ckey(km, x, gid);
+                            if (ck < cmd.lo || ck > cmd.hi) return;
+                            const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+                            if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
+                          });
       }
       cluster.sync();  // round results complete
     }
@@ -1576,6 +1641,7 @@ __global__ void __launch_bounds__(NT, 1)
         write_row_outputs(p, row, slot, token, status);
       }
     } else {
+      const int nemit = sh.nemit;
       const bool ovf = sh.tp_ovf || (nemit > pl.tp_cap);
       if (tid == 0) {
         rec[0] = __float_as_uint(empty ? -INFINITY : m);
@@ -1654,7 +1720,7 @@ __global__ void __launch_bounds__(NT, 1)
   }
   Row r;
   row_init(r, p, row, slot, V_global);
-  const LeanScratch lean = lean_scratch(smem);
+  const TailScr ts = tail_scratch(smem);
   float m = -INFINITY;
   uint32_t status = 0;
   for (int q = 0; q < tp_world; ++q) {
@@ -1677,6 +1743,7 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   if (!empty) {
     const float theta = sh.theta;
+    const uint32_t km = okey(m);
     uint32_t best = 0xFFFFFFFFu;
     for (int q = 0; q < tp_world; ++q) {
       const uint32_t *rec = recv + ((int64_t)q * p.B + row) * rec_words;
@@ -1686,9 +1753,15 @@ __global__ void __launch_bounds__(NT, 1)
         const uint32_t gid = rec[5 + 2 * j];
         if (one) {
           if (x == m) best = min(best, gid);
-        } else if (x >= theta && pred_A(r, x, m)) {
-          const uint32_t idx = atomicAdd(&sh.nloc, 1u);
-          if (idx < (uint32_t)TAIL_CAP) lean.cand[idx] = Cand{x, gid};
+        } else if (x >= theta) {
+          const uint64_t w = weight_A(r, x, m);
+          if (w) {
+            const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+            if (idx < (uint32_t)TAIL_CAP) {
+              ts.K[idx] = ckey(km, x, gid);
+              ts.W[idx] = w;
+            }
+          }
         }
       }
     }
@@ -1698,9 +1771,14 @@ __global__ void __launch_bounds__(NT, 1)
     } else {
       __syncthreads();
       const int n = (int)min(sh.nloc, (uint32_t)TAIL_CAP);
-      const float u = p.uniforms ? p.uniforms[row]
-                                 : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
-      lean_tail(r, n, m, theta, u, lean, sh, nullptr, 0);
+      if (tid < TW) {
+        tail_sort_small(n, km - okey(theta), ts, sh);
+        if (tid == 0) {
+          const float u = p.uniforms ? p.uniforms[row]
+                                     : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
+          tail_resolve(r, n, u, ts, sh.res);
+        }
+      }
     }
   }
   __syncthreads();
