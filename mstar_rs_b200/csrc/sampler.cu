@@ -53,7 +53,7 @@ namespace mstar {
 constexpr int NT = 1024;            // threads per CTA
 constexpr int NWARP = NT / 32;
 constexpr int TAIL_CAP = 2048;      // candidates the fast tail resolves
-constexpr int LCAP = 2048;          // CTA-local candidate list
+constexpr int LCAP = TAIL_CAP;      // CTA-local candidate list (general path)
 constexpr int GCAP = 512;           // candidates per locate round of the general path
 constexpr int NBIN_LOG2 = 10;
 constexpr int NBIN = 1 << NBIN_LOG2;  // histogram bins per general-path round
@@ -89,7 +89,7 @@ struct Plan {
   int32_t es;
   int64_t slice;       // elements per CTA slice
   int32_t data_bytes;  // slice data (>= LEAN_SCRATCH: reused by the fast tail)
-  int32_t map_bytes;   // each of the two bitmaps
+  int32_t map_bytes;   // skip bitmap (one bit per resident position)
   int32_t ht_cap;      // hash table slots (power of two)
   int32_t spec_cap;    // special list entries
   int32_t off_work, off_spec, off_lcand, off_bias;
@@ -156,10 +156,12 @@ struct CtaSh {
   float red_f[NWARP];
   uint64_t red_u64[NWARP];
   uint64_t red_u64b[NWARP];
-  float cta_max;     // read by every CTA of the cluster
-  uint32_t nloc;     // CTA-local candidate count (read by the leader)
-  uint32_t min_gid;  // lowest id at the max in this CTA (greedy / top-1)
-  uint32_t status;   // status bits of this CTA
+  float maxes[16];    // per-CTA maxima, pushed by every CTA of the cluster
+  uint32_t gstat[16];  // per-CTA status bits, pushed
+  uint32_t gmin[16];   // per-CTA lowest id at the max (greedy / top-1), pushed
+  uint32_t nloc;       // CTA-local candidate count
+  uint32_t th_used;    // highest queue threshold (okey) any warp used
+  uint32_t status;     // status bits of this CTA
   uint32_t n_spec;
   uint32_t ht_fail;
   uint32_t qcount;
@@ -187,6 +189,13 @@ __device__ __forceinline__ uint64_t u64max(uint64_t a, uint64_t b) { return a > 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
+
+// Split cluster barrier: a CTA may touch a peer's shared memory only once
+// the peer is known to run, i.e. after a wait matching every CTA's arrive.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -488,22 +497,20 @@ __device__ __forceinline__ uint64_t ckey(uint32_t km, float x, uint32_t gid) {
   return ((uint64_t)(km - okey(x)) << 32) | gid;
 }
 
-// Resident slice view used by the scans: data vectors plus the two bitmaps
-// (disallowed / outside positions, penalised-or-biased positions); lanes
-// flagged in either bitmap read as -inf.
+// Resident slice view used by the scans: data vectors plus the skip bitmap
+// (positions outside the slice, disallowed by the mask, or special: their
+// final value lives in the special list); skipped lanes read as -inf.
 struct Slice {
   const uint4 *data;
-  const uint8_t *mmask, *mspec;
+  const uint8_t *skip;
   int nvec;
-  bool has_spec;
   int64_t pos0_gid;
 };
 
 template <typename T>
 __device__ __forceinline__ uint4 load_masked(const Slice &sl, int k) {
-  uint4 v = sl.data[k];
-  uint32_t b = Elem<T>::bits_of(sl.mmask, k);
-  if (sl.has_spec) b |= Elem<T>::bits_of(sl.mspec, k);
+  const uint4 v = sl.data[k];
+  const uint32_t b = Elem<T>::bits_of(sl.skip, k);
   return b ? Elem<T>::mask_out(v, b) : v;
 }
 
@@ -662,11 +669,11 @@ __device__ __forceinline__ uint64_t S_excl(const uint64_t *S, int j) { return j 
 
 struct Layout {
   uint8_t *data;
-  uint8_t *map_mask, *map_spec;
-  int2 *ht;   // {pos, count}
-  int *queue;  // [QCAP] vector indices queued by a scan
+  uint8_t *skip;
+  int2 *ht;    // {pos, count | HT_MASKED}
+  int *queue;  // [QCAP] vector indices queued by the first scan
   Cand *spec;
-  Cand *lcand;
+  Cand *lcand;  // leader: candidates pushed by every CTA; general path: CTA-local list
   int32_t *bias_id;
   float *bias_val;
   uint8_t *work;
@@ -682,17 +689,16 @@ __device__ __forceinline__ Layout make_layout(uint8_t *smem, const Plan &pl) {
   Layout L;
   L.data = smem;
   L.work = smem + pl.off_work;
-  L.map_mask = L.work;
-  L.map_spec = L.work + pl.map_bytes;
-  L.ht = reinterpret_cast<int2 *>(L.work + 2 * pl.map_bytes);
-  L.queue = reinterpret_cast<int *>(L.work + 2 * pl.map_bytes);  // the table is dead once specials are final
+  L.skip = L.work;
+  L.ht = reinterpret_cast<int2 *>(L.work + pl.map_bytes);
+  L.queue = reinterpret_cast<int *>(L.work + pl.map_bytes + pl.ht_cap * 8);
   L.spec = reinterpret_cast<Cand *>(smem + pl.off_spec);
   L.lcand = reinterpret_cast<Cand *>(smem + pl.off_lcand);
   L.bias_id = reinterpret_cast<int32_t *>(smem + pl.off_bias);
   L.bias_val = reinterpret_cast<float *>(smem + pl.off_bias + BIAS_SMEM * 4);
-  // general-path area: after the bitmaps (which every scan still reads),
-  // over the hash table / scan queue that are dead by then
-  uint8_t *g = L.work + 2 * pl.map_bytes;
+  // general-path area: after the skip bitmap (which every scan still reads),
+  // over the hash table and the first scan's queue, dead by then
+  uint8_t *g = L.work + pl.map_bytes;
   L.l1c = reinterpret_cast<uint32_t *>(g);
   L.l1m = reinterpret_cast<uint64_t *>(g + 4096);
   L.refc = reinterpret_cast<uint32_t *>(g + 12288);  // NBIN counts + NBIN masses
@@ -711,18 +717,24 @@ __device__ __forceinline__ uint32_t ht_hash(uint32_t k, int cap) {
   return (k * 2654435761u) & (uint32_t)(cap - 1);
 }
 
-// Insert element position e (row-relative) with count increment c.
-__device__ __forceinline__ bool ht_insert(int2 *ht, int cap, int e, int c) {
+// Count word flag: the special position is also disallowed by the mask.
+constexpr int HT_MASKED = 1 << 30;
+
+// Insert element position e (row-relative) with count increment c; `slot`
+// receives the entry.  Returns 1 if this call created the entry, 0 if it
+// existed, -1 if the table is full.
+__device__ __forceinline__ int ht_insert(int2 *ht, int cap, int e, int c, int &slot) {
   uint32_t h = ht_hash((uint32_t)e, cap);
   for (int probe = 0; probe < cap; ++probe) {
     const int prev = atomicCAS(&ht[h].x, -1, e);
     if (prev == -1 || prev == e) {
       if (c) atomicAdd(&ht[h].y, c);
-      return true;
+      slot = (int)h;
+      return prev == -1 ? 1 : 0;
     }
     h = (h + 1) & (uint32_t)(cap - 1);
   }
-  return false;
+  return -1;
 }
 
 __device__ __forceinline__ int ht_find(const int2 *ht, int cap, int e) {
@@ -922,7 +934,7 @@ __global__ void __launch_bounds__(NT, 1)
   const int rank = (int)cluster.block_rank();
   const int S = pl.S;
   const int row = blockIdx.y;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ CtaSh sh;
 
@@ -953,6 +965,8 @@ __global__ void __launch_bounds__(NT, 1)
     return;
   }
 
+  cluster_arrive_relaxed();  // matched by the wait before the first remote store
+
   const Layout L = make_layout(smem, pl);
   constexpr int es = (int)sizeof(T);
   const uint8_t *rowp = static_cast<const uint8_t *>(p.logits) + (int64_t)row * p.ld * es;
@@ -973,7 +987,7 @@ __global__ void __launch_bounds__(NT, 1)
   const int nchunk = (int)((nbulk + CHUNK_BYTES - 1) / CHUNK_BYTES);
   uint4 *data4 = reinterpret_cast<uint4 *>(L.data);
 
-  // ---- issue the bulk copies first
+  // ---- issue the bulk copies first; stage the row's parameters
   if (tid == 0) {
     for (int j = 0; j < nchunk; ++j) mbar_init(&sh.mbar[j], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -983,15 +997,15 @@ __global__ void __launch_bounds__(NT, 1)
       bulk_g2s(L.data + (b0 - a_al) + (int64_t)j * CHUNK_BYTES,
                reinterpret_cast<const void *>(b0 + (uintptr_t)j * CHUNK_BYTES), bytes, &sh.mbar[j]);
     }
-    sh.cta_max = -INFINITY;
     sh.nloc = 0;
-    sh.min_gid = 0xFFFFFFFFu;
+    sh.qcount = 0;
     sh.status = 0;
     sh.n_spec = 0;
     sh.ht_fail = 0;
     sh.tp_ovf = 0;
     sh.nemit = 0;
-    row_init(sh.row, p, row, slot, p.V);  // staged once; read by all after setup
+    sh.th_used = 0u;
+    row_init(sh.row, p, row, slot, p.V);
   }
 
   const int64_t gbase = p.vocab_offset;
@@ -999,14 +1013,12 @@ __global__ void __launch_bounds__(NT, 1)
   const bool has_hist = p.hist_ids && p.hist_len;
   const bool has_spec = has_hist || p.seen_bits || p.bias_ids;
 
-  // ---- setup while the copies fly
+  // ---- setup while the copies fly: skip bitmap (outside / disallowed /
+  // special positions) and the specials' hash table
   const int map_words = pl.map_bytes / 4;
-  uint32_t *mask32 = reinterpret_cast<uint32_t *>(L.map_mask);
-  uint32_t *spec32 = reinterpret_cast<uint32_t *>(L.map_spec);
-  if (has_spec) {
-    for (int i = tid; i < map_words; i += NT) spec32[i] = 0u;
+  uint32_t *skip32 = reinterpret_cast<uint32_t *>(L.skip);
+  if (has_spec)
     for (int i = tid; i < pl.ht_cap; i += NT) L.ht[i] = make_int2(-1, 0);
-  }
   {
     const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)slot * p.allowed_words : nullptr;
     for (int wi = tid; wi < map_words; wi += NT) {
@@ -1024,10 +1036,9 @@ __global__ void __launch_bounds__(NT, 1)
         const uint32_t bits = allowed32(aw, p.allowed_words, gbase + e0 + lo_in) << lo_in;
         dis = inmask & ~bits;
       }
-      mask32[wi] = ~inmask | dis;
+      skip32[wi] = ~inmask | dis;
     }
   }
-  // fringe vectors: plain loads (positions outside the slice are masked)
   auto load_fringe = [&](int k) {
     uint4 v = make_uint4(0, 0, 0, 0);
 #pragma unroll
@@ -1046,18 +1057,28 @@ __global__ void __launch_bounds__(NT, 1)
       L.bias_val[j] = p.bias_vals[(int64_t)slot * p.NB + j];
     }
   }
-  if (has_spec) __syncthreads();  // table and bitmap zeroed
-  // specials: history / seen bits / bias ids that fall in [c0, c1)
+  __syncthreads();  // skip words written, table cleared
+  // specials: history / seen bits / bias ids that fall in [c0, c1).  The
+  // thread that creates a table entry sets the position's skip bit and
+  // records whether it was already set (a disallowed position).
+  auto add_special = [&](int64_t e, int cnt) {
+    int h;
+    const int created = ht_insert(L.ht, pl.ht_cap, (int)e, cnt, h);
+    if (created < 0) {
+      sh.ht_fail = 1;
+    } else if (created) {
+      const int64_t pos = e - c0al;
+      const uint32_t bit = 1u << (pos & 31);
+      if (atomicOr(&skip32[pos >> 5], bit) & bit) atomicOr(&L.ht[h].y, HT_MASKED);
+    }
+  };
   if (has_hist) {
     const int32_t len = p.hist_len[slot];
     const int n = min(len, p.H);
     const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
     for (int j = tid; j < n; j += NT) {
       const int64_t e = (int64_t)h[j] - gbase;
-      if (e >= c0 && e < c1) {
-        if (!ht_insert(L.ht, pl.ht_cap, (int)e, 1)) sh.ht_fail = 1;
-        atomicOr(&spec32[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
-      }
+      if (e >= c0 && e < c1) add_special(e, 1);
     }
   } else if (p.seen_bits) {
     const uint32_t *sw = p.seen_bits + (int64_t)slot * p.seen_words;
@@ -1069,10 +1090,7 @@ __global__ void __launch_bounds__(NT, 1)
           const int b = __ffs(bits) - 1;
           bits &= bits - 1;
           const int64_t g = (w << 5) + b;
-          if (g < g0 || g >= g1) continue;
-          const int64_t e = g - gbase;
-          if (!ht_insert(L.ht, pl.ht_cap, (int)e, 1)) sh.ht_fail = 1;
-          atomicOr(&spec32[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
+          if (g >= g0 && g < g1) add_special(g - gbase, 1);
         }
       }
     }
@@ -1083,43 +1101,66 @@ __global__ void __launch_bounds__(NT, 1)
       const int32_t g = bi[j];
       if (g < 0) continue;
       const int64_t e = (int64_t)g - gbase;
-      if (e >= c0 && e < c1) {
-        if (!ht_insert(L.ht, pl.ht_cap, (int)e, 0)) sh.ht_fail = 1;
-        atomicOr(&spec32[(e - c0al) >> 5], 1u << ((e - c0al) & 31));
-      }
+      if (e >= c0 && e < c1) add_special(e, 0);
     }
   }
-  __syncthreads();  // bitmaps, table, fringe vectors complete
+  __syncthreads();  // bitmap, table, fringe vectors complete
   const Row r = sh.row;
+  const Slice sl{data4, L.skip, nvec, pos0_gid};
+  const bool one = r.greedy || r.K == 1;
+  // queue offset: the weakest (lowest) threshold offset the final choice can take
+  float Lq = 0.0f;
+  if (!one) {
+    Lq = -32.0f;
+    if (r.minp) Lq = fmaxf(Lq, __fadd_rn(logf(r.Mp), -1.0f));
+  }
 
-  // ---- pass A: patch + raw max, chunk by chunk as the bulk copies land
-  float rawmax = -INFINITY;
+  // ---- pass A, chunk by chunk as the bulk copies land: masked raw max, and
+  // a queue of the vectors that reach the running threshold (warp max + Lq)
+  float rawmax = -INFINITY, wrun = -INFINITY, th = -INFINITY;
   bool timed_out = false;
+  bool qopen = true;  // warp-uniform: false once the queue overflowed
+  auto enqueue = [&](bool pass, int k) {
+    const unsigned bal = __ballot_sync(~0u, pass);
+    if (bal && qopen) {
+      const int leader = __ffs(bal) - 1;
+      uint32_t base = 0;
+      if (lane == leader) base = atomicAdd(&sh.qcount, (uint32_t)__popc(bal));
+      base = __shfl_sync(~0u, base, leader);
+      if (pass) {
+        const uint32_t idx = base + (uint32_t)__popc(bal & ((1u << lane) - 1u));
+        if (idx < (uint32_t)QCAP) L.queue[idx] = k;
+      }
+      qopen = base + (uint32_t)__popc(bal) <= (uint32_t)QCAP;
+    }
+  };
+  auto block = [&](int kb, int ke) {  // vectors [kb, ke): uniform trip count per warp
+    for (int base = kb; base < ke; base += NT * 2) {
+      const int k0 = base + tid, k1 = base + NT + tid;
+      float m0 = -INFINITY, m1 = -INFINITY;
+      if (k0 < ke) m0 = Elem<T>::vmax(load_masked<T>(sl, k0));
+      if (k1 < ke) m1 = Elem<T>::vmax(load_masked<T>(sl, k1));
+      rawmax = fmaxf(rawmax, fmaxf(m0, m1));
+      const float x0 = r.greedy ? m0 : __fmul_rn(m0, r.invT), x1 = r.greedy ? m1 : __fmul_rn(m1, r.invT);
+      float wm = fmaxf(x0, x1);
+      for (int o = 16; o; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(~0u, wm, o));
+      wrun = fmaxf(wrun, wm);
+      th = __fadd_rn(wrun, Lq);
+      enqueue(k0 < ke && x0 >= th, k0);
+      enqueue(k1 < ke && x1 >= th, k1);
+    }
+  };
+  block(0, hv);
+  block(hv + nbv, nvec);
   {
-    auto process = [&](int k, uint4 v) {
-      uint32_t b = Elem<T>::bits_of(L.map_mask, k);
-      if (has_spec) b |= Elem<T>::bits_of(L.map_spec, k);
-      if (b) v = Elem<T>::mask_out(v, b);
-      rawmax = fmaxf(rawmax, Elem<T>::vmax(v));
-    };
-    for (int k = tid; k < hv; k += NT) process(k, data4[k]);
-    for (int k = hv + nbv + tid; k < nvec; k += NT) process(k, data4[k]);
     constexpr int CV = CHUNK_BYTES / 16;
     for (int j = 0; j < nchunk; ++j) {
       if (!mbar_wait(&sh.mbar[j], 0)) timed_out = true;
-      const int kb = hv + j * CV, ke = hv + min(nbv, (j + 1) * CV);
-      for (int k0 = kb + tid; k0 < ke; k0 += NT * 4) {
-        uint4 v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (k0 + u * NT < ke) v[u] = data4[k0 + u * NT];
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (k0 + u * NT < ke) process(k0 + u * NT, v[u]);
-      }
+      block(hv + j * CV, hv + min(nbv, (j + 1) * CV));
     }
   }
   if (timed_out) atomicOr(&sh.status, MSTAR_STATUS_TIMEOUT);
+  if (lane == 0 && th > -INFINITY) atomicMax(&sh.th_used, okey(th));
   __syncthreads();  // every chunk has landed
   // finalize specials: bias (list order) -> penalties -> mask -> transform
   float spec_max = -INFINITY;
@@ -1134,27 +1175,26 @@ __global__ void __launch_bounds__(NT, 1)
       const int2 ent = L.ht[i];
       if (ent.x < 0) continue;
       const int64_t e = ent.x;
+      const int cnt = ent.y & ~HT_MASKED;
       float v = Elem<T>::smem_elem(L.data, e - c0al);
       if (bi) {
-        const int32_t gid = (int32_t)(e + r.gbase);
+        const int32_t gid = (int32_t)(e + gbase);
         for (int j = 0; j < p.NB; ++j) {
           const int32_t id = bias_smem ? L.bias_id[j] : bi[j];
           if (id == gid) v = __fadd_rn(v, bias_smem ? L.bias_val[j] : bv[j]);
         }
       }
-      if (ent.y > 0) {
+      if (cnt > 0) {
         v = (v > 0.0f) ? __fdiv_rn(v, R) : __fmul_rn(v, R);
-        v = __fsub_rn(v, __fmul_rn(F, (float)ent.y));
+        v = __fsub_rn(v, __fmul_rn(F, (float)cnt));
         v = __fsub_rn(v, Pp);
       }
-      const int64_t pos = e - c0al;
-      const bool masked = (L.map_mask[pos >> 3] >> (pos & 7)) & 1u;
       float x;
       if (v != v) x = v;
-      else if (masked) x = -INFINITY;
+      else if (ent.y & HT_MASKED) x = -INFINITY;
       else x = r.greedy ? v : __fmul_rn(v, r.invT);
       const uint32_t idx = atomicAdd(&sh.n_spec, 1u);
-      if ((int)idx < pl.spec_cap) L.spec[idx] = Cand{x, (uint32_t)(e + r.gbase)};
+      if ((int)idx < pl.spec_cap) L.spec[idx] = Cand{x, (uint32_t)(e + gbase)};
       else sh.ht_fail = 1;
       spec_max = fmaxf(spec_max, x);
     }
@@ -1162,60 +1202,90 @@ __global__ void __launch_bounds__(NT, 1)
   {
     const float xm = r.greedy ? rawmax : __fmul_rn(rawmax, r.invT);
     const float cm = block_max_f32(fmaxf(xm, spec_max), sh);
-    if (tid == 0) {
-      sh.cta_max = cm;
-      if (sh.ht_fail) sh.status |= MSTAR_STATUS_SPECIAL_OVERFLOW;
-    }
+    cluster_wait();  // every CTA of the cluster is running
+    if (tid < S) cluster.map_shared_rank(&sh, tid)->maxes[rank] = cm;  // push to every CTA
+    if (tid == 0 && sh.ht_fail) sh.status |= MSTAR_STATUS_SPECIAL_OVERFLOW;
   }
   const int nspec = min((int)sh.n_spec, pl.spec_cap);
-  const Slice sl{data4, L.map_mask, L.map_spec, nvec, has_spec, pos0_gid};
   cluster.sync();  // #1: maxima published
 
-  // ---- row max and threshold (warp 0), pass C (all warps)
-  const int lane = tid & 31;
+  // ---- row max and threshold (warp 0), candidates (all warps)
   if (tid < 32) {
-    float mm = lane < S ? *cluster.map_shared_rank(&sh.cta_max, lane) : -INFINITY;
+    float mm = lane < S ? sh.maxes[lane] : -INFINITY;
     for (int o = 16; o; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(~0u, mm, o));
-    const float th = mm > -INFINITY ? choose_theta(r, mm) : INFINITY;
+    const float t = mm > -INFINITY ? choose_theta(r, mm) : INFINITY;
     if (lane == 0) {
       sh.m = mm;
-      sh.theta = th;
+      sh.theta = t;
     }
   }
   __syncthreads();
   const float m = sh.m;
   const bool empty = !(m > -INFINITY);
-  const bool one = r.greedy || r.K == 1;
   const float theta = sh.theta;
+  const uint32_t km = okey(m);
+  const int capq = TAIL_CAP / S;  // candidates each CTA may push to the leader
+  Cand *const lead_cand = cluster.map_shared_rank(L.lcand, 0);
   if (!empty) {
-    if (one) {
-      uint32_t best = 0xFFFFFFFFu;
-      for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.queue, QCAP, &sh.qcount,
-                        [&](float x, uint32_t gid, uint64_t w) { best = min(best, gid); });
-      best = block_min_u32(best, sh);
-      if (tid == 0) sh.min_gid = best;
+    // the queue holds every vector reaching theta unless it overflowed or a
+    // warp used a higher threshold than theta (then rescan everything)
+    const bool rescan = sh.qcount > (uint32_t)QCAP || (sh.th_used != 0u && sh.th_used > okey(theta));
+    uint32_t best = 0xFFFFFFFFu;
+    auto take = [&](float x, uint32_t gid) {
+      if (one) {
+        if (x == m) best = min(best, gid);
+        return;
+      }
+      if (!(x >= theta)) return;
+      if (weight_A(r, x, m) == 0) return;
+      const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+      if (idx < (uint32_t)capq) lead_cand[rank * capq + idx] = Cand{x, gid};
+    };
+    auto scan_vec = [&](int k) {
+      const uint4 v = load_masked<T>(sl, k);
+      const float vm = Elem<T>::vmax(v);
+      if (!((r.greedy ? vm : __fmul_rn(vm, r.invT)) >= (one ? m : theta))) return;
+      const uint32_t gid0 = (uint32_t)(pos0_gid + (int64_t)k * VEC);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float raw = Elem<T>::get(v, j);
+        take(r.greedy ? raw : __fmul_rn(raw, r.invT), gid0 + (uint32_t)j);
+      }
+    };
+    if (!rescan) {
+      const int nq = (int)sh.qcount;
+      for (int i = tid; i < nq; i += NT) scan_vec(L.queue[i]);
     } else {
-      for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.queue, QCAP, &sh.qcount,
-                        [&](float x, uint32_t gid, uint64_t w) {
-                          const uint32_t idx = atomicAdd(&sh.nloc, 1u);
-                          if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
-                        });
+      for (int k = tid; k < nvec; k += NT) scan_vec(k);
     }
+    for (int i = tid; i < nspec; i += NT) take(L.spec[i].x, L.spec[i].gid);
+    if (one) {
+      best = block_min_u32(best, sh);
+    } else {
+      __syncthreads();
+    }
+    if (tid < S) {  // push this CTA's count / status / lowest id to every CTA
+      CtaSh *peer = cluster.map_shared_rank(&sh, tid);
+      peer->gcnt[rank] = sh.nloc;
+      peer->gstat[rank] = sh.status;
+      peer->gmin[rank] = best;
+    }
+  } else if (tid < S) {
+    CtaSh *peer = cluster.map_shared_rank(&sh, tid);
+    peer->gcnt[rank] = 0;
+    peer->gstat[rank] = sh.status;
+    peer->gmin[rank] = 0xFFFFFFFFu;
   }
-  cluster.sync();  // #2: local candidate lists complete
+  cluster.sync();  // #2: candidates and counts delivered
 
-  // every CTA takes the same decision from the published counts (warp 0)
+  // every CTA takes the same decision from the delivered counts
   const bool force_general = (p.flags & MSTAR_FLAG_FORCE_GENERAL) != 0;
   if (tid < 32) {
-    uint32_t c = 0, st = 0, mg = 0xFFFFFFFFu;
-    if (lane < S) {
-      const CtaSh *peer = cluster.map_shared_rank(&sh, lane);
-      c = peer->nloc;
-      st = peer->status;
-      mg = peer->min_gid;
-    }
-    const bool lovf = __any_sync(~0u, c > (uint32_t)LCAP);
-    const uint32_t cc = min(c, (uint32_t)LCAP);
+    const uint32_t c = lane < S ? sh.gcnt[lane] : 0u;
+    uint32_t st = lane < S ? sh.gstat[lane] : 0u;
+    uint32_t mg = lane < S ? sh.gmin[lane] : 0xFFFFFFFFu;
+    const bool ovf = __any_sync(~0u, c > (uint32_t)capq);
+    const uint32_t cc = min(c, (uint32_t)capq);
     uint32_t inc = cc;
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t v = __shfl_up_sync(~0u, inc, o);
@@ -1233,7 +1303,7 @@ __global__ void __launch_bounds__(NT, 1)
     if (lane == 0) {
       sh.ncand = total;
       sh.min_all = mg;
-      sh.fast = empty || one || (!lovf && total <= (uint32_t)TAIL_CAP && !force_general);
+      sh.fast = empty || one || (!ovf && !force_general);
       sh.res.m = m;
       sh.res.theta = theta;
       sh.res.greedy = r.greedy;
@@ -1246,22 +1316,23 @@ __global__ void __launch_bounds__(NT, 1)
   }
   __syncthreads();
   const bool fast = sh.fast;
+  const bool debug = MODE == 0 && (p.out_x || p.out_kept || p.out_probs);
   uint32_t *rec = MODE == 1 ? tp_send + (int64_t)row * pl.rec_words : nullptr;
-  const uint32_t km = okey(m);
   auto draw_u = [&]() -> float {
     if (p.uniforms) return p.uniforms[row];
     return philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
   };
-  // Leader, threads [0, TW): gather every CTA's list (DSMEM) as keys and
-  // weights, sort it, then resolve the queries (step) or emit the first
-  // candidates in order (TP shard).  cnt/off describe the lists.
-  auto small_tail = [&](const uint32_t *cnt, const uint32_t *off, int n) {
+  // Leader, threads [0, TW): the candidate lists (CTA q's list at
+  // L.lcand + q * stride of the leader, or at L.lcand of CTA q when
+  // `remote`; cnt[q] entries placed at off[q]) as keys and weights, sorted,
+  // then the queries (step) or the first candidates in order (TP shard).
+  auto small_tail = [&](const uint32_t *cnt, const uint32_t *off, int stride, bool remote, int n) {
     const TailScr ts = tail_scratch(L.data);  // the leader's slice data is dead by then
     for (int q = 0; q < S; ++q) {
-      const Cand *src = cluster.map_shared_rank(L.lcand, q);
-      const int c = (int)cnt[q], o = (int)off[q];
+      const int o = (int)off[q], c = min((int)cnt[q], n - o);
+      const Cand *list = remote ? cluster.map_shared_rank(L.lcand, q) : L.lcand + q * stride;
       for (int i = tid; i < c; i += TW) {
-        const Cand cd = src[i];
+        const Cand cd = list[i];
         ts.K[o + i] = ckey(km, cd.x, cd.gid);
         ts.W[o + i] = spec_w_from_e(spec_e(cd.x, m));
       }
@@ -1283,6 +1354,7 @@ __global__ void __launch_bounds__(NT, 1)
   };
 
   if (fast) {
+    if (rank != 0 && !debug) return;  // nothing of this CTA is read any more
     if (rank == 0 && !empty) {
       if (one) {
         if (tid == 0) {
@@ -1292,7 +1364,7 @@ __global__ void __launch_bounds__(NT, 1)
           sh.nemit = -1;
         }
       } else if (tid < TW) {
-        small_tail(sh.gcnt, sh.goff, (int)sh.ncand);
+        small_tail(sh.gcnt, sh.goff, capq, false, (int)sh.ncand);
       }
     }
   } else {
@@ -1483,7 +1555,7 @@ __global__ void __launch_bounds__(NT, 1)
               if (lane == 0) sh.ncand = min(tot, (uint32_t)TAIL_CAP);
             }
             __syncthreads();
-            if (tid < TW) small_tail(sh.gcnt, sh.goff, (int)sh.ncand);
+            if (tid < TW) small_tail(sh.gcnt, sh.goff, 0, true, (int)sh.ncand);
             if (tid == 0) P.state = ST_FINISH;
             __syncthreads();
             continue;
@@ -1635,7 +1707,7 @@ __global__ void __launch_bounds__(NT, 1)
         uint32_t token = sh.res.token;
         if (empty) {
           status |= MSTAR_STATUS_EMPTY;
-          token = (uint32_t)r.gbase;
+          token = (uint32_t)gbase;
         }
         sh.res.status = status;
         write_row_outputs(p, row, slot, token, status);
@@ -1661,14 +1733,14 @@ __global__ void __launch_bounds__(NT, 1)
   }
 
   // ---- debug dense outputs (recomputed from global memory)
-  if (MODE == 0 && (p.out_x || p.out_kept || p.out_probs)) {
+  if (debug) {
     cluster.sync();
     const Result res = cluster.map_shared_rank(&sh, 0)->res;
     const uint32_t kmm = okey(res.m);
     const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)slot * p.allowed_words : nullptr;
     auto emit = [&](int64_t e, float x) {
       const int64_t o = (int64_t)row * p.V + e;
-      const uint32_t gid = (uint32_t)(e + r.gbase);
+      const uint32_t gid = (uint32_t)(e + gbase);
       bool kept = false;
       float prob = 0.0f;
       if (!res.empty && x == x) {
@@ -1685,8 +1757,8 @@ __global__ void __launch_bounds__(NT, 1)
       if (p.out_probs) p.out_probs[o] = prob;
     };
     for (int64_t e = c0 + tid; e < c1; e += NT) {
-      const float v = Elem<T>::load(r.rowp, e);
-      const int64_t g = e + r.gbase;
+      const float v = Elem<T>::load(rowp, e);
+      const int64_t g = e + gbase;
       const bool allowed = !aw || ((aw[g >> 5] >> (g & 31)) & 1u);
       float x;
       if (v != v) x = v;
@@ -1695,9 +1767,9 @@ __global__ void __launch_bounds__(NT, 1)
       emit(e, x);
     }
     __syncthreads();
-    for (int i = tid; i < nspec; i += NT) emit((int64_t)L.spec[i].gid - r.gbase, L.spec[i].x);
+    for (int i = tid; i < nspec; i += NT) emit((int64_t)L.spec[i].gid - gbase, L.spec[i].x);
   }
-  cluster.sync();  // keep shared memory alive until every remote access is done
+  if (!fast || debug) cluster.sync();  // keep shared memory alive until every remote access is done
 }
 
 // ------------------------------------------------------------ TP merge
@@ -1871,11 +1943,11 @@ static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Pl
     q.map_bytes = (q.map_bytes + 127) / 128 * 128;
     q.ht_cap = ht_cap;
     q.spec_cap = spec_cap;
-    const int work = 2 * q.map_bytes + std::max(WORK_BYTES_MIN, std::max(ht_cap * 8, QCAP * 4));
+    const int work = q.map_bytes + std::max(WORK_BYTES_MIN, ht_cap * 8 + QCAP * 4);
     q.off_work = q.data_bytes;
     q.off_spec = q.off_work + (work + 127) / 128 * 128;
     q.off_lcand = q.off_spec + (spec_cap * 8 + 127) / 128 * 128;
-    q.off_bias = q.off_lcand + LCAP * 8;
+    q.off_bias = q.off_lcand + TAIL_CAP * 8;
     const int bias_bytes = p->bias_ids && p->NB <= BIAS_SMEM ? BIAS_SMEM * 8 : 0;
     q.smem_bytes = q.off_bias + bias_bytes;
     q.mode = mode;
