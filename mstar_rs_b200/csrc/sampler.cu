@@ -73,9 +73,8 @@ static_assert(GCAP * 20 + GBK * 8 <= 14336, "general sort scratch");
 static_assert(GBK <= NT && NBIN % NT == 0 && NBK % NT == 0 && TAIL_CAP % NT == 0, "per-thread splits");
 constexpr int WORK_BYTES_MIN = GEN_BYTES;
 constexpr int LEAN_SCRATCH = 112 * 1024;  // fast-tail scratch (the leader's data region)
-constexpr int TW = 128;                  // threads of the fast tail (warps 0-3)
 static_assert(TAIL_CAP * 44 + NBK * 12 <= LEAN_SCRATCH, "fast tail scratch");
-static_assert(TW % 32 == 0 && TW <= NT, "tail threads");
+static_assert(NBK % NT == 0 && NBK / NT <= 2, "tail bucket scan");
 constexpr unsigned kWaitLimit = 1u << 24;
 
 struct __align__(8) Cand {
@@ -145,7 +144,7 @@ struct Result {
 struct Row {
   const void *rowp;
   int64_t V, gbase;  // gbase = vocab_offset
-  float T, invT, Mp, P;
+  float T, invT, Mp, lnMp, P;
   int K;             // 0 = off
   bool greedy, topk, minp, topp;
 };
@@ -160,8 +159,14 @@ struct CtaSh {
   uint32_t gstat[16];  // per-CTA status bits, pushed
   uint32_t gmin[16];   // per-CTA lowest id at the max (greedy / top-1), pushed
   uint32_t nloc;       // CTA-local candidate count
-  uint32_t th_used;    // highest queue threshold (okey) any warp used
+  uint32_t runmax;     // okey of the raw running max the queue threshold follows
+  uint32_t cmax;       // okey of the CTA max (transformed)
+  uint32_t best;       // lowest id at the max (greedy / top-1)
   uint32_t status;     // status bits of this CTA
+  uint64_t kmin, kmax;  // tail: key range
+  uint32_t npass;       // tail: candidates passing the value-A predicate
+  uint32_t cnt_k;       // tail: ranks kept by top_p
+  float u;              // the row's uniform draw
   uint32_t n_spec;
   uint32_t ht_fail;
   uint32_t qcount;
@@ -237,6 +242,14 @@ struct Elem;
 template <>
 struct Elem<float> {
   static constexpr int VEC = 4;
+  // running-max accumulator of the first pass
+  using Acc = float;
+  static __device__ __forceinline__ Acc acc_init() { return -INFINITY; }
+  static __device__ __forceinline__ Acc vred(const uint4 &v) {
+    return fmaxf(fmaxf(__uint_as_float(v.x), __uint_as_float(v.y)), fmaxf(__uint_as_float(v.z), __uint_as_float(v.w)));
+  }
+  static __device__ __forceinline__ Acc acc_max(Acc a, Acc b) { return fmaxf(a, b); }
+  static __device__ __forceinline__ float acc_f(Acc a) { return a; }
   static __device__ __forceinline__ float get(const uint4 &v, int j) {
     const uint32_t w = j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
     return __uint_as_float(w);
@@ -278,6 +291,22 @@ struct Elem<float> {
 template <>
 struct Elem<__nv_bfloat16> {
   static constexpr int VEC = 8;
+  // running-max accumulator of the first pass: a bf16 pair (max of the
+  // even and of the odd lanes), reduced to one float only when read
+  using Acc = uint32_t;
+  static __device__ __forceinline__ Acc acc_init() { return 0xFF80FF80u; }
+  static __device__ __forceinline__ Acc hmax_bits(uint32_t a, uint32_t b) {
+    const __nv_bfloat162 r = __hmax2(*reinterpret_cast<const __nv_bfloat162 *>(&a),
+                                     *reinterpret_cast<const __nv_bfloat162 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+  }
+  static __device__ __forceinline__ Acc vred(const uint4 &v) {
+    return hmax_bits(hmax_bits(v.x, v.y), hmax_bits(v.z, v.w));
+  }
+  static __device__ __forceinline__ Acc acc_max(Acc a, Acc b) { return hmax_bits(a, b); }
+  static __device__ __forceinline__ float acc_f(Acc a) {
+    return fmaxf(__uint_as_float(a << 16), __uint_as_float(a & 0xFFFF0000u));
+  }
   static __device__ __forceinline__ float get(const uint4 &v, int j) {
     const uint32_t w = (j >> 1) == 0 ? v.x : (j >> 1) == 1 ? v.y : (j >> 1) == 2 ? v.z : v.w;
     return __uint_as_float((j & 1) ? (w & 0xFFFF0000u) : (w << 16));
@@ -441,6 +470,7 @@ __device__ __forceinline__ void row_init(Row &r, const mstar_sampler_params_t &p
   const float Mp = p.min_p ? p.min_p[slot] : 0.0f;
   r.minp = Mp > 0.0f;
   r.Mp = fminf(Mp, 1.0f);
+  r.lnMp = r.minp ? logf(r.Mp) : 0.0f;
   r.P = p.top_p ? p.top_p[slot] : 1.0f;
   r.topp = r.P < 1.0f;
 }
@@ -483,7 +513,7 @@ __device__ float choose_theta(const Row &r, float m) {
     ok = spec_w_from_e(spec_e(prev_float(t), m)) == 0;
   } else if (lane < 6 && r.minp) {
     const float off = lane == 3 ? -0.002f : lane == 4 ? -0.1f : -1.0f;
-    t = __fadd_rn(m, __fadd_rn(logf(r.Mp), off));
+    t = __fadd_rn(m, __fadd_rn(r.lnMp, off));
     ok = !(spec_e(prev_float(t), m) >= r.Mp);
   }
   const unsigned bal = __ballot_sync(~0u, ok);
@@ -773,13 +803,18 @@ __device__ __forceinline__ void write_row_outputs(const mstar_sampler_params_t &
   }
 }
 
-// --------------------------------------------------------- 4-warp fast tail
-
-__device__ __forceinline__ void tbar() { asm volatile("bar.sync 1, %0;" ::"n"(TW) : "memory"); }
+// ------------------------------------------------------------- the tail
+//
+// The candidate tail runs on all NT threads of one CTA: gather the
+// candidates as (order key, weight) pairs, sort them by key, then resolve
+// top_k / top_p / the inverse-CDF draw from exact u64 prefix sums of the
+// fixed-point weights.  The value-A predicate (positive weight, min_p) is
+// monotone in x, so candidates that fail it (weight 0) sort behind every
+// candidate that passes: the A set is the first `npass` ranks.
 
 struct TailScr {
   uint64_t *K;   // [TAIL_CAP] order key per candidate (gathered order)
-  uint64_t *W;   // [TAIL_CAP] weight per candidate
+  uint64_t *W;   // [TAIL_CAP] weight per candidate (0 = fails the predicate)
   uint32_t *P;   // [TAIL_CAP] bucket << 16 | position, then rank
   uint64_t *RK;  // [TAIL_CAP] keys: bucket order, then rank order
   uint64_t *RW;  // [TAIL_CAP] weights: bucket order, then rank order
@@ -801,41 +836,85 @@ __device__ __forceinline__ TailScr tail_scratch(uint8_t *base) {
   return t;
 }
 
-// Sort the n candidates in s.K / s.W (order key ascending = x descending,
-// id ascending; keys are distinct) on TW threads: bucket counts of the top
-// key bits, one scan, scatter, rank inside each bucket; leaves keys,
-// weights and exclusive weight prefixes in rank order in s.RK / s.RW / s.RS.
-// Dth bounds the distance key d (top 32 key bits).  Called by threads
-// [0, TW) only; synchronises them with named barrier 1.
-__device__ void tail_sort_small(int n, uint32_t Dth, const TailScr &s, CtaSh &sh) {
-  const int t = threadIdx.x;
+__device__ __forceinline__ int tail_log2_buckets(int n) {
   int nbl = 6;
   while (nbl < NBK_LOG2 && (1 << nbl) < 2 * n) ++nbl;
-  const int NB = 1 << nbl;
-  const int dbits = Dth ? 32 - __clz((int)Dth) : 0;
-  const int dsh = dbits > nbl ? dbits - nbl : 0;
-  for (int b = t; b < NB; b += TW) {
+  return nbl;
+}
+
+// Called before the barrier that precedes tail_gather.
+__device__ __forceinline__ void tail_reset(CtaSh &sh) {
+  sh.kmin = ~0ull;
+  sh.kmax = 0ull;
+  sh.npass = 0u;
+  sh.cnt_k = 0u;
+}
+
+// Per-thread part of the gather: key and weight of one candidate.
+__device__ __forceinline__ void tail_put(const Row &r, float m, uint32_t km, const Cand &cd, int i,
+                                         const TailScr &s, uint64_t &kmn, uint64_t &kmx, uint32_t &np) {
+  const uint64_t k = ckey(km, cd.x, cd.gid);
+  const uint64_t w = weight_A(r, cd.x, m);
+  s.K[i] = k;
+  s.W[i] = w;
+  kmn = u64min(kmn, k);
+  kmx = u64max(kmx, k);
+  np += w != 0;
+}
+
+// Gather epilogue: key range, pass count, cleared buckets.  Block-wide;
+// ends with a barrier.
+__device__ __forceinline__ void tail_gather_end(uint64_t kmn, uint64_t kmx, uint32_t np, const TailScr &s,
+                                                CtaSh &sh) {
+  for (int o = 16; o; o >>= 1) {
+    kmn = u64min(kmn, (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)kmn, o));
+    kmx = u64max(kmx, (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)kmx, o));
+  }
+  np = __reduce_add_sync(~0u, np);
+  if ((threadIdx.x & 31) == 0) {
+    if (np) atomicAdd(&sh.npass, np);
+    if (kmn <= kmx) {
+      atomicMin((unsigned long long *)&sh.kmin, (unsigned long long)kmn);
+      atomicMax((unsigned long long *)&sh.kmax, (unsigned long long)kmx);
+    }
+  }
+  for (int b = threadIdx.x; b < NBK; b += NT) {
     s.bc[b] = 0;
     s.bm[b] = 0;
   }
-  tbar();
-  for (int i = t; i < n; i += TW) {
-    const uint32_t b = min((uint32_t)(s.K[i] >> 32) >> dsh, (uint32_t)(NB - 1));
+  __syncthreads();
+}
+
+// Sort the n gathered candidates (distinct keys) by key ascending: bucket
+// counts / masses over the keys' actual range, one scan, scatter, rank inside
+// each bucket.  Leaves keys, weights and exclusive weight prefixes in rank
+// order in RK / RW / RS.  Block-wide; ends with a barrier.
+__device__ void tail_sort(int n, const TailScr &s, CtaSh &sh) {
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const int nbl = tail_log2_buckets(n);
+  const int NB = 1 << nbl;
+  const uint64_t kmin = sh.kmin;
+  const uint64_t range = sh.kmax - kmin;
+  const int bits = range ? 64 - __clzll((long long)range) : 0;
+  const int bsh = bits > nbl ? bits - nbl : 0;
+  for (int i = t; i < n; i += NT) {
+    const uint32_t b = (uint32_t)((s.K[i] - kmin) >> bsh);
     const uint32_t pos = atomicAdd(&s.bc[b], 1u);
     atomicAdd((unsigned long long *)&s.bm[b], (unsigned long long)s.W[i]);
     s.P[i] = (b << 16) | pos;
   }
-  tbar();
-  {  // inclusive scans of counts and masses over NB buckets, NB / TW per thread
-    const int per = (NB + TW - 1) / TW;
-    const int b0 = min(NB, t * per), b1 = min(NB, b0 + per);
+  __syncthreads();
+  {  // inclusive scans of counts and masses; NB / NT (<= 2) buckets per thread
+    constexpr int PER = NBK / NT;
+    const int b0 = t * PER;
     uint32_t c = 0;
     uint64_t mm = 0;
-    for (int b = b0; b < b1; ++b) {
-      c += s.bc[b];
-      mm += s.bm[b];
-    }
-    const int lane = t & 31, wid = t >> 5;
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+      if (b0 + j < NB) {
+        c += s.bc[b0 + j];
+        mm += s.bm[b0 + j];
+      }
     uint32_t ic = c;
     uint64_t im = mm;
     for (int o = 1; o < 32; o <<= 1) {
@@ -850,29 +929,39 @@ __device__ void tail_sort_small(int n, uint32_t Dth, const TailScr &s, CtaSh &sh
       sh.red_u32[wid] = ic;
       sh.red_u64[wid] = im;
     }
-    tbar();
-    uint32_t oc = ic - c;
-    uint64_t om = im - mm;
-    for (int w = 0; w < wid; ++w) {
-      oc += sh.red_u32[w];
-      om += sh.red_u64[w];
+    __syncthreads();
+    uint32_t wc = sh.red_u32[lane];
+    uint64_t wm = sh.red_u64[lane];
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t uc = __shfl_up_sync(~0u, wc, o);
+      const uint64_t um = __shfl_up_sync(~0u, (unsigned long long)wm, o);
+      if (lane >= o) {
+        wc += uc;
+        wm += um;
+      }
     }
-    for (int b = b0; b < b1; ++b) {
-      oc += s.bc[b];
-      om += s.bm[b];
-      s.bc[b] = oc;
-      s.bm[b] = om;
-    }
+    const uint32_t pc = __shfl_sync(~0u, wc, (wid + 31) & 31);
+    const uint64_t pm = __shfl_sync(~0u, (unsigned long long)wm, (wid + 31) & 31);
+    uint32_t oc = (wid ? pc : 0u) + ic - c;
+    uint64_t om = (wid ? pm : 0ull) + im - mm;
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+      if (b0 + j < NB) {
+        oc += s.bc[b0 + j];
+        om += s.bm[b0 + j];
+        s.bc[b0 + j] = oc;
+        s.bm[b0 + j] = om;
+      }
   }
-  tbar();
-  for (int i = t; i < n; i += TW) {
+  __syncthreads();
+  for (int i = t; i < n; i += NT) {  // bucket order
     const uint32_t b = s.P[i] >> 16, pos = s.P[i] & 0xFFFFu;
     const uint32_t lo = b ? s.bc[b - 1] : 0u;
     s.RK[lo + pos] = s.K[i];
     s.RW[lo + pos] = s.W[i];
   }
-  tbar();
-  for (int i = t; i < n; i += TW) {  // rank inside the bucket
+  __syncthreads();
+  for (int i = t; i < n; i += NT) {  // rank inside the bucket
     const uint32_t b = s.P[i] >> 16;
     const uint32_t lo = b ? s.bc[b - 1] : 0u, hi = s.bc[b];
     const uint64_t key = s.K[i];
@@ -887,48 +976,494 @@ __device__ void tail_sort_small(int n, uint32_t Dth, const TailScr &s, CtaSh &sh
     s.P[i] = lo + rin;
     s.RS[lo + rin] = before;
   }
-  tbar();
-  for (int i = t; i < n; i += TW) {  // keys and weights into rank order
+  __syncthreads();
+  for (int i = t; i < n; i += NT) {  // keys and weights into rank order
     s.RK[s.P[i]] = s.K[i];
     s.RW[s.P[i]] = s.W[i];
   }
-  tbar();
+  __syncthreads();
 }
 
-// Queries over the rank-ordered candidates (one thread): top_k, top_p,
-// the inverse-CDF draw.  Writes res.token / res.WK / res.ckK.
-__device__ void tail_resolve(const Row &r, int n, float u, const TailScr &s, Result &res) {
-  const int nA = r.topk ? min(n, r.K) : n;
-  const uint64_t WA = s.RS[nA - 1] + s.RW[nA - 1];
-  int nK = nA;
-  if (r.topp) {
-    const double thr = __dmul_rn((double)r.P, (double)WA);
-    int lo = 0, hi = nA;  // count of ranks j < nA with (double)RS[j] < thr (a prefix)
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      if ((double)s.RS[mid] < thr) lo = mid + 1;
-      else hi = mid;
+// top_k, top_p and the inverse-CDF draw over the rank-ordered candidates
+// (sh.npass of them pass the predicate).  Writes res.token / WK / ckK.
+// Block-wide; ends with a barrier.
+__device__ void tail_resolve(const Row &r, float u, const TailScr &s, CtaSh &sh) {
+  const int t = threadIdx.x;
+  const int np = (int)sh.npass;
+  const int nA = r.topk ? min(np, r.K) : np;
+  if (nA <= 0) {  // no candidate carries weight: the leading one stands
+    if (t == 0) {
+      sh.res.token = (uint32_t)(s.RK[0] & 0xFFFFFFFFu);
+      sh.res.WK = 0;
+      sh.res.ckK = s.RK[0];
     }
-    nK = max(lo, 1);
+    __syncthreads();
+    return;
+  }
+  int nK = nA;
+  if (r.topp) {  // kept ranks: j == 0 or S_j < P * W_A (a prefix)
+    const double thr = __dmul_rn((double)r.P, (double)(s.RS[nA - 1] + s.RW[nA - 1]));
+    uint32_t c = 0;
+    for (int j = t; j < nA; j += NT) c += (double)s.RS[j] < thr;
+    c = __reduce_add_sync(~0u, c);
+    if ((t & 31) == 0 && c) atomicAdd(&sh.cnt_k, c);
+    __syncthreads();
+    nK = max((int)sh.cnt_k, 1);
   }
   const uint64_t WK = s.RS[nK - 1] + s.RW[nK - 1];
   const uint64_t rr = draw_point(u, WK);
-  int lo = 0, hi = nK - 1;  // largest j with RS[j] <= rr
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (s.RS[mid] <= rr) lo = mid;
-    else hi = mid - 1;
+  for (int j = t; j < nK; j += NT)
+    if (s.RS[j] <= rr && rr < s.RS[j] + s.RW[j]) sh.res.token = (uint32_t)(s.RK[j] & 0xFFFFFFFFu);
+  if (t == 0) {
+    sh.res.WK = WK;
+    sh.res.ckK = s.RK[nK - 1];
   }
-  res.token = (uint32_t)(s.RK[lo] & 0xFFFFFFFFu);
-  res.WK = WK;
-  res.ckK = s.RK[nK - 1];
+  __syncthreads();
+}
+
+// TP shard record: the A set in order (top_k-limited) as (x bits, id)
+// pairs.  Block-wide; ends with a barrier.
+__device__ void tail_emit(const Row &r, uint32_t km, int tp_cap, uint32_t *rec, const TailScr &s, CtaSh &sh) {
+  const int np = (int)sh.npass;
+  const int ne = r.topk ? min(np, r.K) : np;
+  if (ne <= tp_cap) {
+    for (int j = threadIdx.x; j < ne; j += NT) {
+      rec[4 + 2 * j] = __float_as_uint(okey_inv(km - (uint32_t)(s.RK[j] >> 32)));
+      rec[5 + 2 * j] = (uint32_t)(s.RK[j] & 0xFFFFFFFFu);
+    }
+  }
+  if (threadIdx.x == 0) sh.nemit = ne;
+  __syncthreads();
 }
 
 // ------------------------------------------------------------ the kernel
 
+// What the out-of-line paths (general rounds, dense debug outputs) share
+// with the kernel body.
+struct RowCtx {
+  const mstar_sampler_params_t *p;
+  const Plan *pl;
+  Layout L;
+  Slice sl;
+  Row r;
+  const uint8_t *rowp;
+  float m, theta, u;
+  uint32_t km;
+  int nspec, rank, S, row, slot;
+  int64_t c0, c1, gbase;
+  uint32_t *rec;  // TP shard record (MODE 1)
+  bool empty;
+};
+
+__device__ __forceinline__ float xform(const Row &r, float v) { return r.greedy ? v : __fmul_rn(v, r.invT); }
+
+// General path: leader-driven rounds of histogram (count + mass) and
+// compaction over the still-resident slices until every boundary (top_k,
+// top_p, the draw) is pinned to a bin small enough to sort.  Executed by
+// every CTA of the cluster.
+template <typename T, int MODE>
+__device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int rank = c.rank, S = c.S;
+  const Layout &L = c.L;
+  const Slice &sl = c.sl;
+  const Row &r = c.r;
+  const Plan &pl = *c.pl;
+  const float m = c.m, theta = c.theta, u = c.u;
+  const uint32_t km = c.km;
+  const int nspec = c.nspec;
+  uint32_t *rec = c.rec;
+  Planner &P = sh.pl;
+  if (rank == 0 && tid == 0) {
+    memset(&P, 0, sizeof(P));
+    P.state = ST_START;
+    sh.res.status |= MSTAR_STATUS_GENERAL;
+    tail_reset(sh);
+  }
+  for (int round = 0; round < MAX_ROUNDS; ++round) {
+    if (rank == 0) {
+      // ================= leader planning (block-wide) =================
+      for (int guard = 0; guard < 16; ++guard) {
+        __syncthreads();
+        const int state = P.state;
+        __syncthreads();
+        if (state == ST_START) {
+          if (tid == 0) {
+            const uint32_t DA = km - okey(theta);
+            P.l1lo = 0;
+            P.l1hi = ((uint64_t)DA << 32) | 0xFFFFFFFFull;
+            const int bits = 64 - __clzll((long long)(P.l1hi - P.l1lo));
+            P.l1shift = bits > NBIN_LOG2 ? bits - NBIN_LOG2 : 0;
+            P.l1nbins = (int)((P.l1hi - P.l1lo) >> P.l1shift) + 1;
+            sh.cmd = Cmd{OP_HIST, TGT_L1, P.l1lo, P.l1hi, P.l1shift, P.l1nbins};
+            P.state = ST_AFTER_L1;
+          }
+          for (int b = tid; b < NBIN; b += NT) {
+            L.l1c[b] = 0;
+            L.l1m[b] = 0;
+          }
+          break;
+        }
+        if (state == ST_AFTER_L1 || state == ST_LOC_AFTER_REF) {
+          uint32_t *C = state == ST_AFTER_L1 ? L.l1c : L.refc;
+          uint64_t *M = state == ST_AFTER_L1 ? L.l1m : L.refm;
+          constexpr int PER = NBIN / NT;
+          uint64_t lc[PER], lm[PER], sc = 0, sm = 0;
+#pragma unroll
+          for (int q = 0; q < PER; ++q) {
+            lc[q] = C[tid * PER + q];
+            lm[q] = M[tid * PER + q];
+            sc += lc[q];
+            sm += lm[q];
+          }
+          uint64_t oc, om, tc, tm;
+          block_exscan2_u64(sc, sm, oc, om, tc, tm, sh);
+#pragma unroll
+          for (int q = 0; q < PER; ++q) {
+            oc += lc[q];
+            om += lm[q];
+            C[tid * PER + q] = (uint32_t)oc;
+            M[tid * PER + q] = om;
+          }
+          __syncthreads();
+          if (state == ST_AFTER_L1) {
+            if (tid == 0) {
+              P.N = tc;
+              P.Wv = tm;
+              P.level = 0;
+              P.lo = P.l1lo;
+              P.hi = P.l1hi;
+              P.shift = P.l1shift;
+              P.nbins = P.l1nbins;
+              P.base_c = 0;
+              P.base_m = 0;
+              const bool needA = r.topk && P.N > (uint64_t)r.K;
+              int b_end = P.nbins - 1;
+              if (needA) {
+                for (int b = 0; b < P.nbins; ++b)
+                  if ((uint64_t)L.l1c[b] > (uint64_t)(r.K - 1)) {
+                    b_end = b;
+                    break;
+                  }
+              }
+              const uint64_t pre = L.l1c[b_end];
+              if (pre <= (uint64_t)TAIL_CAP) {
+                const uint64_t bhi = u64min(P.l1hi, P.l1lo + (((uint64_t)b_end + 1) << P.l1shift) - 1);
+                sh.cmd = Cmd{OP_COMPACT, 0, P.l1lo, bhi, 0, 0};
+                P.state = ST_AFTER_PREFIX;
+              } else if (needA) {
+                P.stage = 0;
+                P.qkind = Q_COUNT;
+                P.tcount = (uint64_t)(r.K - 1);
+                P.state = ST_LOC_BIN;
+              } else if (MODE == 1) {
+                P.state = ST_FINISH;
+                sh.tp_ovf = 1;
+              } else {
+                P.WA = P.Wv;
+                P.ckA = P.l1hi;
+                P.stage = 1;
+                if (r.topp) {
+                  P.thr = __dmul_rn((double)r.P, (double)P.WA);
+                  if (!(0.0 < P.thr)) {
+                    P.qkind = Q_COUNT;
+                    P.tcount = 0;
+                  } else {
+                    P.qkind = Q_LASTLT;
+                  }
+                } else {
+                  P.WK = P.WA;
+                  P.ckK = P.ckA;
+                  P.stage = 2;
+                  P.qkind = Q_POINT;
+                  P.tpoint = draw_point(u, P.WK);
+                }
+                P.state = ST_LOC_BIN;
+              }
+            }
+            __syncthreads();
+            if (P.state == ST_AFTER_PREFIX) break;
+            continue;
+          }
+          if (tid == 0) {
+            P.level = 1;
+            P.state = ST_LOC_BIN;
+          }
+          continue;
+        }
+        if (state == ST_LOC_BIN) {
+          const uint32_t *C = P.level == 0 ? L.l1c : L.refc;
+          const uint64_t *M = P.level == 0 ? L.l1m : L.refm;
+          if (tid == 0) sh.bcast_i = -1;
+          __syncthreads();
+          for (int b = tid; b < P.nbins; b += NT) {
+            const uint64_t pc0 = P.base_c + (b ? C[b - 1] : 0), pc1 = P.base_c + C[b];
+            const uint64_t pm0 = P.base_m + (b ? M[b - 1] : 0), pm1 = P.base_m + M[b];
+            bool hit = false;
+            if (P.qkind == Q_COUNT) hit = pc0 <= P.tcount && P.tcount < pc1;
+            else if (P.qkind == Q_POINT) hit = pm0 <= P.tpoint && P.tpoint < pm1;
+            if (hit) sh.bcast_i = b;
+            if (P.qkind == Q_LASTLT && pc1 > pc0 && (double)pm0 < P.thr) atomicMax(&sh.bcast_i, b);
+          }
+          __syncthreads();
+          if (tid == 0) {
+            const int b = sh.bcast_i;
+            if (b < 0) {  // cannot happen for consistent inputs; finish defensively
+              P.state = ST_FINISH;
+              sh.res.status |= MSTAR_STATUS_EMPTY;
+            } else {
+              const uint64_t blo = P.lo + ((uint64_t)b << P.shift);
+              const uint64_t bhi = u64min(P.hi, blo + (1ull << P.shift) - 1);
+              const uint64_t cnt = (uint64_t)C[b] - (b ? C[b - 1] : 0);
+              P.cbase_c = P.base_c + (b ? C[b - 1] : 0);
+              P.cbase_m = P.base_m + (b ? M[b - 1] : 0);
+              if (cnt <= (uint64_t)GCAP || P.shift == 0) {
+                sh.cmd = Cmd{OP_COMPACT, 0, blo, bhi, 0, 0};
+                P.state = ST_LOC_AFTER_COMPACT;
+              } else {
+                P.base_c = P.cbase_c;
+                P.base_m = P.cbase_m;
+                P.lo = blo;
+                P.hi = bhi;
+                const int bits = 64 - __clzll((long long)(bhi - blo));
+                P.shift = bits > NBIN_LOG2 ? bits - NBIN_LOG2 : 0;
+                P.nbins = (int)((bhi - blo) >> P.shift) + 1;
+                sh.cmd = Cmd{OP_HIST, TGT_REF, blo, bhi, P.shift, P.nbins};
+                P.state = ST_LOC_AFTER_REF;
+              }
+            }
+          }
+          __syncthreads();
+          if (P.state == ST_LOC_AFTER_REF) {
+            for (int b = tid; b < NBIN; b += NT) {
+              L.refc[b] = 0;
+              L.refm[b] = 0;
+            }
+          }
+          if (P.state == ST_FINISH) continue;
+          break;
+        }
+        if (state == ST_AFTER_PREFIX) {
+          if (tid < 32) {  // per-CTA counts of the compacted range
+            const uint32_t c = lane < S ? min(cluster.map_shared_rank(&sh, lane)->nloc, (uint32_t)LCAP) : 0u;
+            uint32_t inc = c;
+            for (int o = 1; o < 32; o <<= 1) {
+              const uint32_t v = __shfl_up_sync(~0u, inc, o);
+              if (lane >= o) inc += v;
+            }
+            if (lane < 16) {
+              sh.goff[lane] = inc - c;
+              sh.gcnt[lane] = c;
+            }
+            const uint32_t tot = __shfl_sync(~0u, inc, 31);
+            if (lane == 0) sh.ncand = min(tot, (uint32_t)TAIL_CAP);
+          }
+          __syncthreads();
+          {  // every CTA's compacted list, over DSMEM, into the tail
+            const int n = (int)sh.ncand;
+            const TailScr ts = tail_scratch(L.data);  // the leader's slice data is dead by now
+            uint64_t kmn = ~0ull, kmx = 0ull;
+            uint32_t np = 0;
+            for (int q = 0; q < S; ++q) {
+              const int o = (int)sh.goff[q], cq = min((int)sh.gcnt[q], n - o);
+              const Cand *list = cluster.map_shared_rank(L.lcand, q);
+              for (int i = tid; i < cq; i += NT) tail_put(r, m, km, list[i], o + i, ts, kmn, kmx, np);
+            }
+            tail_gather_end(kmn, kmx, np, ts, sh);
+            tail_sort(n, ts, sh);
+            if (MODE == 0) tail_resolve(r, u, ts, sh);
+            else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
+          }
+          if (tid == 0) P.state = ST_FINISH;
+          __syncthreads();
+          continue;
+        }
+        if (state == ST_LOC_AFTER_COMPACT) {
+          int n = 0;
+          for (int q = 0; q < S; ++q) {  // gather every CTA's list (DSMEM)
+            const int c = (int)min(cluster.map_shared_rank(&sh, q)->nloc, (uint32_t)LCAP);
+            const Cand *src = cluster.map_shared_rank(L.lcand, q);
+            for (int i = tid; i < c; i += NT)
+              if (n + i < GCAP) L.gsort.in[n + i] = src[i];
+            n += c;
+          }
+          n = min(n, GCAP);
+          __syncthreads();
+          tail_sort_scan(L.gsort.in, n, m, L.gsort, sh);
+          const uint64_t *Sx = L.gsort.S;
+          const Cand *sorted = L.gsort.in;
+          if (tid == 0) sh.bcast_i = -1;
+          __syncthreads();
+          for (int j = tid; j < n; j += NT) {
+            const uint64_t se = P.cbase_m + S_excl(Sx, j), si = P.cbase_m + Sx[j];
+            bool hit = false;
+            if (P.qkind == Q_COUNT) hit = (P.cbase_c + j) == P.tcount;
+            else if (P.qkind == Q_POINT) hit = se <= P.tpoint && P.tpoint < si;
+            if (hit) sh.bcast_i = j;
+            if (P.qkind == Q_LASTLT && (double)se < P.thr) atomicMax(&sh.bcast_i, j);
+          }
+          __syncthreads();
+          if (tid == 0) {
+            const int j = sh.bcast_i;
+            if (j < 0) {
+              P.state = ST_FINISH;
+              sh.res.status |= MSTAR_STATUS_EMPTY;
+            } else {
+              const uint64_t ck = ckey(km, sorted[j].x, sorted[j].gid);
+              const uint64_t si = P.cbase_m + Sx[j];
+              P.level = 0;
+              P.lo = P.l1lo;
+              P.hi = P.l1hi;
+              P.shift = P.l1shift;
+              P.nbins = P.l1nbins;
+              P.base_c = 0;
+              P.base_m = 0;
+              if (P.stage == 0) {  // A boundary (top_k)
+                P.WA = si;
+                P.ckA = ck;
+                if (MODE == 1 || r.K <= TAIL_CAP) {
+                  sh.cmd = Cmd{OP_COMPACT, 0, P.l1lo, ck, 0, 0};
+                  P.state = ST_AFTER_PREFIX;
+                } else {
+                  P.stage = 1;
+                  if (r.topp) {
+                    P.thr = __dmul_rn((double)r.P, (double)P.WA);
+                    if (!(0.0 < P.thr)) {
+                      P.qkind = Q_COUNT;
+                      P.tcount = 0;
+                    } else {
+                      P.qkind = Q_LASTLT;
+                    }
+                  } else {
+                    P.WK = P.WA;
+                    P.ckK = P.ckA;
+                    P.stage = 2;
+                    P.qkind = Q_POINT;
+                    P.tpoint = draw_point(u, P.WK);
+                  }
+                  P.state = ST_LOC_BIN;
+                }
+              } else if (P.stage == 1) {  // top-p boundary: last kept element
+                P.WK = si;
+                P.ckK = ck;
+                P.stage = 2;
+                P.qkind = Q_POINT;
+                P.tpoint = draw_point(u, P.WK);
+                P.state = ST_LOC_BIN;
+              } else {  // draw
+                sh.res.token = sorted[j].gid;
+                sh.res.WK = P.WK;
+                sh.res.ckK = P.ckK;
+                P.state = ST_FINISH;
+              }
+            }
+          }
+          __syncthreads();
+          if (P.state == ST_AFTER_PREFIX) break;
+          continue;
+        }
+        if (state == ST_FINISH) {
+          if (tid == 0) sh.cmd = Cmd{OP_DONE, 0, 0, 0, 0, 0};
+          break;
+        }
+      }
+      __syncthreads();
+    }
+    cluster.sync();  // command published
+    const Cmd cmd = cluster.map_shared_rank(&sh, 0)->cmd;
+    if (cmd.op == OP_DONE) break;
+    if (cmd.op == OP_HIST) {
+      uint32_t *hc = rank == 0 ? (cmd.target == TGT_L1 ? L.l1c : L.refc) : L.l1c;
+      uint64_t *hm = rank == 0 ? (cmd.target == TGT_L1 ? L.l1m : L.refm) : L.l1m;
+      if (rank != 0) {
+        for (int b = tid; b < NBIN; b += NT) {
+          hc[b] = 0;
+          hm[b] = 0;
+        }
+        __syncthreads();
+      }
+      for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount,
+                        [&](float x, uint32_t gid, uint64_t w) {
+                          const uint64_t ck = ckey(km, x, gid);
+                          if (ck < cmd.lo || ck > cmd.hi) return;
+                          const int b = (int)((ck - cmd.lo) >> cmd.shift);
+                          atomicAdd(&hc[b], 1u);
+                          atomicAdd((unsigned long long *)&hm[b], (unsigned long long)w);
+                        });
+      if (rank != 0) {
+        __syncthreads();
+        uint32_t *rc = cluster.map_shared_rank(cmd.target == TGT_L1 ? L.l1c : L.refc, 0);
+        uint64_t *rm = cluster.map_shared_rank(cmd.target == TGT_L1 ? L.l1m : L.refm, 0);
+        for (int b = tid; b < cmd.nbins; b += NT) {
+          if (hc[b]) {
+            atomicAdd(&rc[b], hc[b]);
+            atomicAdd((unsigned long long *)&rm[b], (unsigned long long)hm[b]);
+          }
+        }
+      }
+    } else {  // OP_COMPACT into the CTA-local list
+      if (tid == 0) sh.nloc = 0;
+      __syncthreads();
+      for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount,
+                        [&](float x, uint32_t gid, uint64_t w) {
+                          const uint64_t ck = ckey(km, x, gid);
+                          if (ck < cmd.lo || ck > cmd.hi) return;
+                          const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+                          if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
+                        });
+    }
+    cluster.sync();  // round results complete
+  }
+}
+
+// Dense debug outputs (processed logits, kept mask, probabilities),
+// recomputed from global memory.  Every CTA of the cluster, after a cluster
+// barrier that published the leader's result.
+template <typename T>
+__device__ __forceinline__ void debug_dense(const RowCtx &c, CtaSh &sh) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const mstar_sampler_params_t &p = *c.p;
+  const Row &r = c.r;
+  const Result res = cluster.map_shared_rank(&sh, 0)->res;
+  const uint32_t kmm = okey(res.m);
+  const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)c.slot * p.allowed_words : nullptr;
+  auto emit = [&](int64_t e, float x) {
+    const int64_t o = (int64_t)c.row * p.V + e;
+    const uint32_t gid = (uint32_t)(e + c.gbase);
+    bool kept = false;
+    float prob = 0.0f;
+    if (!res.empty && x == x) {
+      if (res.greedy) {
+        kept = gid == res.token;
+        prob = kept ? 1.0f : 0.0f;
+      } else if (x > -INFINITY && x <= res.m && ckey(kmm, x, gid) <= res.ckK) {
+        kept = true;
+        prob = (float)__ddiv_rn((double)spec_w_from_e(spec_e(x, res.m)), (double)res.WK);
+      }
+    }
+    if (p.out_x) p.out_x[o] = x;
+    if (p.out_kept) p.out_kept[o] = kept ? 1 : 0;
+    if (p.out_probs) p.out_probs[o] = prob;
+  };
+  for (int64_t e = c.c0 + threadIdx.x; e < c.c1; e += NT) {
+    const float v = Elem<T>::load(c.rowp, e);
+    const int64_t g = e + c.gbase;
+    const bool allowed = !aw || ((aw[g >> 5] >> (g & 31)) & 1u);
+    float x;
+    if (v != v) x = v;
+    else if (!allowed) x = -INFINITY;
+    else x = xform(r, v);
+    emit(e, x);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < c.nspec; i += NT) emit((int64_t)c.L.spec[i].gid - c.gbase, c.L.spec[i].x);
+}
+
 template <typename T, int MODE>
 __global__ void __launch_bounds__(NT, 1)
     sampler_kernel(const mstar_sampler_params_t p, const Plan pl, uint32_t *tp_send) {
+  using Acc = typename Elem<T>::Acc;
   constexpr int VEC = Elem<T>::VEC;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
@@ -964,7 +1499,6 @@ __global__ void __launch_bounds__(NT, 1)
     }
     return;
   }
-
   cluster_arrive_relaxed();  // matched by the wait before the first remote store
 
   const Layout L = make_layout(smem, pl);
@@ -1004,8 +1538,14 @@ __global__ void __launch_bounds__(NT, 1)
     sh.ht_fail = 0;
     sh.tp_ovf = 0;
     sh.nemit = 0;
-    sh.th_used = 0u;
+    sh.runmax = okey(-INFINITY);
+    sh.cmax = okey(-INFINITY);
+    sh.best = 0xFFFFFFFFu;
+    tail_reset(sh);
     row_init(sh.row, p, row, slot, p.V);
+  } else if (MODE == 0 && tid == 32) {
+    sh.u = p.uniforms ? p.uniforms[row]
+                      : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
   }
 
   const int64_t gbase = p.vocab_offset;
@@ -1013,31 +1553,32 @@ __global__ void __launch_bounds__(NT, 1)
   const bool has_hist = p.hist_ids && p.hist_len;
   const bool has_spec = has_hist || p.seen_bits || p.bias_ids;
 
-  // ---- setup while the copies fly: skip bitmap (outside / disallowed /
-  // special positions) and the specials' hash table
+  // ---- setup while the copies fly: the skip bitmap (disallowed and
+  // special positions; positions outside the slice are -inf in the data)
+  // and the specials' hash table
   const int map_words = pl.map_bytes / 4;
   uint32_t *skip32 = reinterpret_cast<uint32_t *>(L.skip);
   if (has_spec)
     for (int i = tid; i < pl.ht_cap; i += NT) L.ht[i] = make_int2(-1, 0);
-  {
-    const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)slot * p.allowed_words : nullptr;
+  if (p.allowed_bits) {
+    const uint32_t *aw = p.allowed_bits + (int64_t)slot * p.allowed_words;
     for (int wi = tid; wi < map_words; wi += NT) {
       const int64_t e0 = c0al + (int64_t)wi * 32;
       const int64_t lo_in = min((int64_t)32, max((int64_t)0, c0 - e0));
       const int64_t hi_in = min((int64_t)32, max((int64_t)0, c1 - e0));
-      uint32_t inmask = 0u;
+      uint32_t dis = 0u;
       if (hi_in > lo_in) {
         const uint32_t hm = hi_in == 32 ? ~0u : ((1u << hi_in) - 1u);
         const uint32_t lm = lo_in == 32 ? ~0u : ((1u << lo_in) - 1u);
-        inmask = hm & ~lm;
-      }
-      uint32_t dis = 0u;
-      if (aw && inmask) {
+        const uint32_t inmask = hm & ~lm;
         const uint32_t bits = allowed32(aw, p.allowed_words, gbase + e0 + lo_in) << lo_in;
         dis = inmask & ~bits;
       }
-      skip32[wi] = ~inmask | dis;
+      skip32[wi] = dis;
     }
+  } else {
+    uint4 *s4 = reinterpret_cast<uint4 *>(L.skip);
+    for (int i = tid; i < map_words / 4; i += NT) s4[i] = make_uint4(0u, 0u, 0u, 0u);
   }
   auto load_fringe = [&](int k) {
     uint4 v = make_uint4(0, 0, 0, 0);
@@ -1058,68 +1599,76 @@ __global__ void __launch_bounds__(NT, 1)
     }
   }
   __syncthreads();  // skip words written, table cleared
-  // specials: history / seen bits / bias ids that fall in [c0, c1).  The
-  // thread that creates a table entry sets the position's skip bit and
-  // records whether it was already set (a disallowed position).
-  auto add_special = [&](int64_t e, int cnt) {
-    int h;
-    const int created = ht_insert(L.ht, pl.ht_cap, (int)e, cnt, h);
-    if (created < 0) {
-      sh.ht_fail = 1;
-    } else if (created) {
-      const int64_t pos = e - c0al;
-      const uint32_t bit = 1u << (pos & 31);
-      if (atomicOr(&skip32[pos >> 5], bit) & bit) atomicOr(&L.ht[h].y, HT_MASKED);
-    }
-  };
-  if (has_hist) {
-    const int32_t len = p.hist_len[slot];
-    const int n = min(len, p.H);
-    const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
-    for (int j = tid; j < n; j += NT) {
-      const int64_t e = (int64_t)h[j] - gbase;
-      if (e >= c0 && e < c1) add_special(e, 1);
-    }
-  } else if (p.seen_bits) {
-    const uint32_t *sw = p.seen_bits + (int64_t)slot * p.seen_words;
-    const int64_t g0 = gbase + c0, g1 = gbase + c1;
-    if (g1 > g0) {
-      for (int64_t w = (g0 >> 5) + tid; w <= ((g1 - 1) >> 5); w += NT) {
-        uint32_t bits = sw[w];
-        while (bits) {
-          const int b = __ffs(bits) - 1;
-          bits &= bits - 1;
-          const int64_t g = (w << 5) + b;
-          if (g >= g0 && g < g1) add_special(g - gbase, 1);
+  if (has_spec) {
+    // specials: history / seen bits / bias ids that fall in [c0, c1).  The
+    // thread that creates a table entry sets the position's skip bit and
+    // records whether it was already set (a disallowed position).
+    auto add_special = [&](int64_t e, int cnt) {
+      int h;
+      const int created = ht_insert(L.ht, pl.ht_cap, (int)e, cnt, h);
+      if (created < 0) {
+        sh.ht_fail = 1;
+      } else if (created) {
+        const int64_t pos = e - c0al;
+        const uint32_t bit = 1u << (pos & 31);
+        if (atomicOr(&skip32[pos >> 5], bit) & bit) atomicOr(&L.ht[h].y, HT_MASKED);
+      }
+    };
+    if (has_hist) {
+      const int32_t len = p.hist_len[slot];
+      const int n = min(len, p.H);
+      const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
+      for (int j = tid; j < n; j += NT) {
+        const int64_t e = (int64_t)h[j] - gbase;
+        if (e >= c0 && e < c1) add_special(e, 1);
+      }
+    } else if (p.seen_bits) {
+      const uint32_t *sw = p.seen_bits + (int64_t)slot * p.seen_words;
+      const int64_t g0 = gbase + c0, g1 = gbase + c1;
+      if (g1 > g0) {
+        for (int64_t w = (g0 >> 5) + tid; w <= ((g1 - 1) >> 5); w += NT) {
+          uint32_t bits = sw[w];
+          while (bits) {
+            const int b = __ffs(bits) - 1;
+            bits &= bits - 1;
+            const int64_t g = (w << 5) + b;
+            if (g >= g0 && g < g1) add_special(g - gbase, 1);
+          }
         }
       }
     }
-  }
-  if (p.bias_ids && p.bias_vals) {
-    const int32_t *bi = p.bias_ids + (int64_t)slot * p.NB;
-    for (int j = tid; j < p.NB; j += NT) {
-      const int32_t g = bi[j];
-      if (g < 0) continue;
-      const int64_t e = (int64_t)g - gbase;
-      if (e >= c0 && e < c1) add_special(e, 0);
+    if (p.bias_ids && p.bias_vals) {
+      const int32_t *bi = p.bias_ids + (int64_t)slot * p.NB;
+      for (int j = tid; j < p.NB; j += NT) {
+        const int32_t g = bi[j];
+        if (g < 0) continue;
+        const int64_t e = (int64_t)g - gbase;
+        if (e >= c0 && e < c1) add_special(e, 0);
+      }
     }
+    __syncthreads();  // bitmap and table complete
   }
-  __syncthreads();  // bitmap, table, fringe vectors complete
   const Row r = sh.row;
   const Slice sl{data4, L.skip, nvec, pos0_gid};
   const bool one = r.greedy || r.K == 1;
-  // queue offset: the weakest (lowest) threshold offset the final choice can take
-  float Lq = 0.0f;
-  if (!one) {
-    Lq = -32.0f;
-    if (r.minp) Lq = fmaxf(Lq, __fadd_rn(logf(r.Mp), -1.0f));
-  }
 
   // ---- pass A, chunk by chunk as the bulk copies land: masked raw max, and
-  // a queue of the vectors that reach the running threshold (warp max + Lq)
-  float rawmax = -INFINITY, wrun = -INFINITY, th = -INFINITY;
-  bool timed_out = false;
-  bool qopen = true;  // warp-uniform: false once the queue overflowed
+  // a queue of the vectors whose max reaches the running threshold
+  // thr(M) = M - |M| 2^-10 + lq T (1 + 2^-10), M a raw max seen so far and
+  // lq the lowest threshold offset the final value threshold can take.
+  float lq = 0.0f;
+  if (!one) {
+    lq = -33.0f;
+    if (r.minp) lq = fmaxf(lq, __fadd_rn(r.lnMp, -1.25f));
+  }
+  const float lqr = one ? 0.0f : __fmul_rn(lq, __fmul_rn(r.T, 1.0009765625f));
+  auto thr_of = [&](float M) -> float {
+    if (M == -INFINITY || M == INFINITY) return M;
+    return __fadd_rn(__fmaf_rn(fabsf(M), -0x1p-10f, M), lqr);
+  };
+  Acc racc = Elem<T>::acc_init();
+  float runM = -INFINITY;
+  bool boot = true, qopen = true, timed_out = false;
   auto enqueue = [&](bool pass, int k) {
     const unsigned bal = __ballot_sync(~0u, pass);
     if (bal && qopen) {
@@ -1134,34 +1683,66 @@ __global__ void __launch_bounds__(NT, 1)
       qopen = base + (uint32_t)__popc(bal) <= (uint32_t)QCAP;
     }
   };
-  auto block = [&](int kb, int ke) {  // vectors [kb, ke): uniform trip count per warp
-    for (int base = kb; base < ke; base += NT * 2) {
-      const int k0 = base + tid, k1 = base + NT + tid;
-      float m0 = -INFINITY, m1 = -INFINITY;
-      if (k0 < ke) m0 = Elem<T>::vmax(load_masked<T>(sl, k0));
-      if (k1 < ke) m1 = Elem<T>::vmax(load_masked<T>(sl, k1));
-      rawmax = fmaxf(rawmax, fmaxf(m0, m1));
-      const float x0 = r.greedy ? m0 : __fmul_rn(m0, r.invT), x1 = r.greedy ? m1 : __fmul_rn(m1, r.invT);
-      float wm = fmaxf(x0, x1);
-      for (int o = 16; o; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(~0u, wm, o));
-      wrun = fmaxf(wrun, wm);
-      th = __fadd_rn(wrun, Lq);
-      enqueue(k0 < ke && x0 >= th, k0);
-      enqueue(k1 < ke && x1 >= th, k1);
+  auto process = [&](int kb, int ke) {  // vectors [kb, ke); uniform trip count
+    float th = -INFINITY;
+    if (!boot) {
+      runM = okey_inv(*reinterpret_cast<volatile uint32_t *>(&sh.runmax));
+      th = thr_of(runM);
     }
+    float cmx = -INFINITY;
+    for (int base = kb; base < ke; base += 2 * NT) {
+      const int k0 = base + tid, k1 = k0 + NT;
+      float v0 = -INFINITY, v1 = -INFINITY;
+      if (k0 < ke) {
+        const Acc a = Elem<T>::vred(load_masked<T>(sl, k0));
+        racc = Elem<T>::acc_max(racc, a);
+        v0 = Elem<T>::acc_f(a);
+      }
+      if (k1 < ke) {
+        const Acc a = Elem<T>::vred(load_masked<T>(sl, k1));
+        racc = Elem<T>::acc_max(racc, a);
+        v1 = Elem<T>::acc_f(a);
+      }
+      const float vm = fmaxf(v0, v1);
+      if (boot) {  // first block: the warp's own max sets the threshold
+        float w = vm;
+        for (int o = 16; o; o >>= 1) w = fmaxf(w, __shfl_xor_sync(~0u, w, o));
+        th = thr_of(w);
+        runM = w;
+        if (lane == 0 && w > -INFINITY) atomicMax(&sh.runmax, okey(w));
+        boot = false;
+      }
+      cmx = fmaxf(cmx, vm);
+      enqueue(v0 > -INFINITY && v0 >= th, k0);
+      enqueue(v1 > -INFINITY && v1 >= th, k1);
+    }
+    if (cmx > runM) atomicMax(&sh.runmax, okey(cmx));
   };
-  block(0, hv);
-  block(hv + nbv, nvec);
   {
+    // blocks in order: bulk chunk 0 (it sets the threshold), the fringe
+    // vectors (head, tail), then the remaining chunks as they land
     constexpr int CV = CHUNK_BYTES / 16;
-    for (int j = 0; j < nchunk; ++j) {
-      if (!mbar_wait(&sh.mbar[j], 0)) timed_out = true;
-      block(hv + j * CV, hv + min(nbv, (j + 1) * CV));
+    const int nblk = nchunk + 2;
+    for (int bi = 0; bi < nblk; ++bi) {
+      int kb, ke;
+      if (bi == 1) {
+        kb = 0;
+        ke = hv;
+      } else if (bi == 2) {
+        kb = hv + nbv;
+        ke = nvec;
+      } else {
+        const int j = bi == 0 ? 0 : bi - 2;
+        if (j >= nchunk) continue;
+        if (!mbar_wait(&sh.mbar[j], 0)) timed_out = true;
+        kb = hv + j * CV;
+        ke = hv + min(nbv, (j + 1) * CV);
+      }
+      process(kb, ke);
     }
   }
   if (timed_out) atomicOr(&sh.status, MSTAR_STATUS_TIMEOUT);
-  if (lane == 0 && th > -INFINITY) atomicMax(&sh.th_used, okey(th));
-  __syncthreads();  // every chunk has landed
+  const float rawmax = Elem<T>::acc_f(racc);
   // finalize specials: bias (list order) -> penalties -> mask -> transform
   float spec_max = -INFINITY;
   if (has_spec) {
@@ -1192,7 +1773,7 @@ __global__ void __launch_bounds__(NT, 1)
       float x;
       if (v != v) x = v;
       else if (ent.y & HT_MASKED) x = -INFINITY;
-      else x = r.greedy ? v : __fmul_rn(v, r.invT);
+      else x = xform(r, v);
       const uint32_t idx = atomicAdd(&sh.n_spec, 1u);
       if ((int)idx < pl.spec_cap) L.spec[idx] = Cand{x, (uint32_t)(e + gbase)};
       else sh.ht_fail = 1;
@@ -1200,16 +1781,18 @@ __global__ void __launch_bounds__(NT, 1)
     }
   }
   {
-    const float xm = r.greedy ? rawmax : __fmul_rn(rawmax, r.invT);
-    const float cm = block_max_f32(fmaxf(xm, spec_max), sh);
-    cluster_wait();  // every CTA of the cluster is running
-    if (tid < S) cluster.map_shared_rank(&sh, tid)->maxes[rank] = cm;  // push to every CTA
-    if (tid == 0 && sh.ht_fail) sh.status |= MSTAR_STATUS_SPECIAL_OVERFLOW;
+    float cm = fmaxf(xform(r, rawmax), spec_max);
+    for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(~0u, cm, o));
+    if (lane == 0 && cm > -INFINITY) atomicMax(&sh.cmax, okey(cm));
   }
+  __syncthreads();  // CTA max, queue, specials complete
+  if (tid == 0 && sh.ht_fail) sh.status |= MSTAR_STATUS_SPECIAL_OVERFLOW;
   const int nspec = min((int)sh.n_spec, pl.spec_cap);
+  cluster_wait();  // every CTA of the cluster runs
+  if (tid < S) cluster.map_shared_rank(&sh, tid)->maxes[rank] = okey_inv(sh.cmax);  // push to every CTA
   cluster.sync();  // #1: maxima published
 
-  // ---- row max and threshold (warp 0), candidates (all warps)
+  // ---- row max and value threshold (warp 0)
   if (tid < 32) {
     float mm = lane < S ? sh.maxes[lane] : -INFINITY;
     for (int o = 16; o; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(~0u, mm, o));
@@ -1225,85 +1808,68 @@ __global__ void __launch_bounds__(NT, 1)
   const float theta = sh.theta;
   const uint32_t km = okey(m);
   const int capq = TAIL_CAP / S;  // candidates each CTA may push to the leader
-  Cand *const lead_cand = cluster.map_shared_rank(L.lcand, 0);
+
+  // ---- candidates: x >= theta (or x == m for greedy / top-1) from the
+  // queued vectors and the specials, pushed into the leader's region
   if (!empty) {
-    // the queue holds every vector reaching theta unless it overflowed or a
-    // warp used a higher threshold than theta (then rescan everything)
-    const bool rescan = sh.qcount > (uint32_t)QCAP || (sh.th_used != 0u && sh.th_used > okey(theta));
+    const float tcut = one ? m : theta;
+    // every queue threshold used was <= thr(CTA raw max): if a value below
+    // it can still reach tcut, or the queue overflowed, scan every vector
+    const float thq = thr_of(okey_inv(sh.runmax));
+    const bool rescan = sh.qcount > (uint32_t)QCAP || (thq > -INFINITY && !(xform(r, prev_float(thq)) < tcut));
+    Cand *const lead = cluster.map_shared_rank(L.lcand, 0) + rank * capq;
     uint32_t best = 0xFFFFFFFFu;
     auto take = [&](float x, uint32_t gid) {
       if (one) {
         if (x == m) best = min(best, gid);
-        return;
+      } else if (x >= theta) {
+        const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+        if (idx < (uint32_t)capq) lead[idx] = Cand{x, gid};
       }
-      if (!(x >= theta)) return;
-      if (weight_A(r, x, m) == 0) return;
-      const uint32_t idx = atomicAdd(&sh.nloc, 1u);
-      if (idx < (uint32_t)capq) lead_cand[rank * capq + idx] = Cand{x, gid};
     };
     auto scan_vec = [&](int k) {
       const uint4 v = load_masked<T>(sl, k);
-      const float vm = Elem<T>::vmax(v);
-      if (!((r.greedy ? vm : __fmul_rn(vm, r.invT)) >= (one ? m : theta))) return;
+      if (!(xform(r, Elem<T>::vmax(v)) >= tcut)) return;
       const uint32_t gid0 = (uint32_t)(pos0_gid + (int64_t)k * VEC);
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        const float raw = Elem<T>::get(v, j);
-        take(r.greedy ? raw : __fmul_rn(raw, r.invT), gid0 + (uint32_t)j);
-      }
+      for (int j = 0; j < VEC; ++j) take(xform(r, Elem<T>::get(v, j)), gid0 + (uint32_t)j);
     };
-    if (!rescan) {
-      const int nq = (int)sh.qcount;
-      for (int i = tid; i < nq; i += NT) scan_vec(L.queue[i]);
-    } else {
-      for (int k = tid; k < nvec; k += NT) scan_vec(k);
-    }
+    const int nscan = rescan ? nvec : (int)sh.qcount;
+    for (int i = tid; i < nscan; i += NT) scan_vec(rescan ? i : L.queue[i]);
     for (int i = tid; i < nspec; i += NT) take(L.spec[i].x, L.spec[i].gid);
-    if (one) {
-      best = block_min_u32(best, sh);
-    } else {
-      __syncthreads();
-    }
-    if (tid < S) {  // push this CTA's count / status / lowest id to every CTA
-      CtaSh *peer = cluster.map_shared_rank(&sh, tid);
-      peer->gcnt[rank] = sh.nloc;
-      peer->gstat[rank] = sh.status;
-      peer->gmin[rank] = best;
-    }
-  } else if (tid < S) {
+    if (best != 0xFFFFFFFFu) atomicMin(&sh.best, best);
+  }
+  __syncthreads();
+  if (tid < S) {  // push this CTA's count / status / lowest id to every CTA
     CtaSh *peer = cluster.map_shared_rank(&sh, tid);
-    peer->gcnt[rank] = 0;
+    peer->gcnt[rank] = sh.nloc;
     peer->gstat[rank] = sh.status;
-    peer->gmin[rank] = 0xFFFFFFFFu;
+    peer->gmin[rank] = sh.best;
   }
   cluster.sync();  // #2: candidates and counts delivered
 
   // every CTA takes the same decision from the delivered counts
-  const bool force_general = (p.flags & MSTAR_FLAG_FORCE_GENERAL) != 0;
+  const bool debug = MODE == 0 && (p.out_x || p.out_kept || p.out_probs);
+  bool fast;
+  {
+    const uint32_t cq = lane < S ? sh.gcnt[lane] : 0u;
+    const bool ovf = __any_sync(~0u, cq > (uint32_t)capq);
+    fast = empty || one || (!ovf && !(p.flags & MSTAR_FLAG_FORCE_GENERAL));
+  }
+  if (fast && rank != 0 && !debug) return;  // nothing of this CTA is read any more
   if (tid < 32) {
-    const uint32_t c = lane < S ? sh.gcnt[lane] : 0u;
-    uint32_t st = lane < S ? sh.gstat[lane] : 0u;
-    uint32_t mg = lane < S ? sh.gmin[lane] : 0xFFFFFFFFu;
-    const bool ovf = __any_sync(~0u, c > (uint32_t)capq);
-    const uint32_t cc = min(c, (uint32_t)capq);
-    uint32_t inc = cc;
+    const uint32_t cq = lane < S ? min(sh.gcnt[lane], (uint32_t)capq) : 0u;
+    uint32_t inc = cq;
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t v = __shfl_up_sync(~0u, inc, o);
       if (lane >= o) inc += v;
     }
-    const uint32_t total = __shfl_sync(~0u, inc, 31);
-    for (int o = 16; o; o >>= 1) {
-      st |= __shfl_xor_sync(~0u, st, o);
-      mg = min(mg, __shfl_xor_sync(~0u, mg, o));
-    }
-    if (lane < 16) {
-      sh.goff[lane] = inc - cc;
-      sh.gcnt[lane] = cc;
-    }
+    const uint32_t st = __reduce_or_sync(~0u, lane < S ? sh.gstat[lane] : 0u);
+    const uint32_t mg = __reduce_min_sync(~0u, lane < S ? sh.gmin[lane] : 0xFFFFFFFFu);
+    if (lane < 16) sh.goff[lane] = inc - cq;
+    if (lane == 31) sh.ncand = inc;
     if (lane == 0) {
-      sh.ncand = total;
       sh.min_all = mg;
-      sh.fast = empty || one || (!ovf && !force_general);
       sh.res.m = m;
       sh.res.theta = theta;
       sh.res.greedy = r.greedy;
@@ -1315,46 +1881,31 @@ __global__ void __launch_bounds__(NT, 1)
     }
   }
   __syncthreads();
-  const bool fast = sh.fast;
-  const bool debug = MODE == 0 && (p.out_x || p.out_kept || p.out_probs);
   uint32_t *rec = MODE == 1 ? tp_send + (int64_t)row * pl.rec_words : nullptr;
-  auto draw_u = [&]() -> float {
-    if (p.uniforms) return p.uniforms[row];
-    return philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
-  };
-  // Leader, threads [0, TW): the candidate lists (CTA q's list at
-  // L.lcand + q * stride of the leader, or at L.lcand of CTA q when
-  // `remote`; cnt[q] entries placed at off[q]) as keys and weights, sorted,
-  // then the queries (step) or the first candidates in order (TP shard).
-  auto small_tail = [&](const uint32_t *cnt, const uint32_t *off, int stride, bool remote, int n) {
-    const TailScr ts = tail_scratch(L.data);  // the leader's slice data is dead by then
-    for (int q = 0; q < S; ++q) {
-      const int o = (int)off[q], c = min((int)cnt[q], n - o);
-      const Cand *list = remote ? cluster.map_shared_rank(L.lcand, q) : L.lcand + q * stride;
-      for (int i = tid; i < c; i += TW) {
-        const Cand cd = list[i];
-        ts.K[o + i] = ckey(km, cd.x, cd.gid);
-        ts.W[o + i] = spec_w_from_e(spec_e(cd.x, m));
-      }
-    }
-    tbar();
-    tail_sort_small(n, km - okey(theta), ts, sh);
-    if (MODE == 0) {
-      if (tid == 0) tail_resolve(r, n, draw_u(), ts, sh.res);
-    } else {
-      const int ne = r.topk ? min(n, r.K) : n;
-      if (tid == 0) sh.nemit = ne;
-      if (ne <= pl.tp_cap) {
-        for (int j = tid; j < ne; j += TW) {
-          rec[4 + 2 * j] = __float_as_uint(okey_inv(km - (uint32_t)(ts.RK[j] >> 32)));
-          rec[5 + 2 * j] = (uint32_t)(ts.RK[j] & 0xFFFFFFFFu);
-        }
-      }
-    }
-  };
-
+  RowCtx ctx;
+  if (!fast || debug) {
+    ctx.p = &p;
+    ctx.pl = &pl;
+    ctx.L = L;
+    ctx.sl = sl;
+    ctx.r = r;
+    ctx.rowp = rowp;
+    ctx.m = m;
+    ctx.theta = theta;
+    ctx.u = MODE == 0 ? sh.u : 0.0f;
+    ctx.km = km;
+    ctx.nspec = nspec;
+    ctx.rank = rank;
+    ctx.S = S;
+    ctx.row = row;
+    ctx.slot = slot;
+    ctx.c0 = c0;
+    ctx.c1 = c1;
+    ctx.gbase = gbase;
+    ctx.rec = rec;
+    ctx.empty = empty;
+  }
   if (fast) {
-    if (rank != 0 && !debug) return;  // nothing of this CTA is read any more
     if (rank == 0 && !empty) {
       if (one) {
         if (tid == 0) {
@@ -1363,339 +1914,23 @@ __global__ void __launch_bounds__(NT, 1)
           sh.res.ckK = (uint64_t)sh.min_all;
           sh.nemit = -1;
         }
-      } else if (tid < TW) {
-        small_tail(sh.gcnt, sh.goff, capq, false, (int)sh.ncand);
+      } else {  // the candidates pushed into this CTA's region, gap-free by goff
+        const int n = (int)sh.ncand;
+        const TailScr ts = tail_scratch(L.data);  // the leader's slice data is dead by now
+        uint64_t kmn = ~0ull, kmx = 0ull;
+        uint32_t np = 0;
+        for (int q = 0; q < S; ++q) {
+          const int cq = min((int)sh.gcnt[q], capq), o = (int)sh.goff[q];
+          for (int i = tid; i < cq; i += NT) tail_put(r, m, km, L.lcand[q * capq + i], o + i, ts, kmn, kmx, np);
+        }
+        tail_gather_end(kmn, kmx, np, ts, sh);
+        tail_sort(n, ts, sh);
+        if (MODE == 0) tail_resolve(r, sh.u, ts, sh);
+        else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
       }
     }
   } else {
-    // ---- general path: leader-driven rounds over the resident slices
-    Planner &P = sh.pl;
-    if (rank == 0 && tid == 0) {
-      memset(&P, 0, sizeof(P));
-      P.state = ST_START;
-      sh.res.status |= MSTAR_STATUS_GENERAL;
-    }
-    const float u = rank == 0 && !empty ? draw_u() : 0.0f;
-    for (int round = 0; round < MAX_ROUNDS; ++round) {
-      if (rank == 0) {
-        // ================= leader planning (block-wide) =================
-        for (int guard = 0; guard < 16; ++guard) {
-          __syncthreads();
-          const int state = P.state;
-          __syncthreads();
-          if (state == ST_START) {
-            if (tid == 0) {
-              const uint32_t DA = km - okey(theta);
-              P.l1lo = 0;
-              P.l1hi = ((uint64_t)DA << 32) | 0xFFFFFFFFull;
-              const int bits = 64 - __clzll((long long)(P.l1hi - P.l1lo));
-              P.l1shift = bits > NBIN_LOG2 ? bits - NBIN_LOG2 : 0;
-              P.l1nbins = (int)((P.l1hi - P.l1lo) >> P.l1shift) + 1;
-              sh.cmd = Cmd{OP_HIST, TGT_L1, P.l1lo, P.l1hi, P.l1shift, P.l1nbins};
-              P.state = ST_AFTER_L1;
-            }
-            for (int b = tid; b < NBIN; b += NT) {
-              L.l1c[b] = 0;
-              L.l1m[b] = 0;
-            }
-            break;
-          }
-          if (state == ST_AFTER_L1 || state == ST_LOC_AFTER_REF) {
-            uint32_t *C = state == ST_AFTER_L1 ? L.l1c : L.refc;
-            uint64_t *M = state == ST_AFTER_L1 ? L.l1m : L.refm;
-            constexpr int PER = NBIN / NT;
-            uint64_t lc[PER], lm[PER], sc = 0, sm = 0;
-#pragma unroll
-            for (int q = 0; q < PER; ++q) {
-              lc[q] = C[tid * PER + q];
-              lm[q] = M[tid * PER + q];
-              sc += lc[q];
-              sm += lm[q];
-            }
-            uint64_t oc, om, tc, tm;
-            block_exscan2_u64(sc, sm, oc, om, tc, tm, sh);
-#pragma unroll
-            for (int q = 0; q < PER; ++q) {
-              oc += lc[q];
-              om += lm[q];
-              C[tid * PER + q] = (uint32_t)oc;
-              M[tid * PER + q] = om;
-            }
-            __syncthreads();
-            if (state == ST_AFTER_L1) {
-              if (tid == 0) {
-                P.N = tc;
-                P.Wv = tm;
-                P.level = 0;
-                P.lo = P.l1lo;
-                P.hi = P.l1hi;
-                P.shift = P.l1shift;
-                P.nbins = P.l1nbins;
-                P.base_c = 0;
-                P.base_m = 0;
-                const bool needA = r.topk && P.N > (uint64_t)r.K;
-                int b_end = P.nbins - 1;
-                if (needA) {
-                  for (int b = 0; b < P.nbins; ++b)
-                    if ((uint64_t)L.l1c[b] > (uint64_t)(r.K - 1)) {
-                      b_end = b;
-                      break;
-                    }
-                }
-                const uint64_t pre = L.l1c[b_end];
-                if (pre <= (uint64_t)TAIL_CAP) {
-                  const uint64_t bhi = u64min(P.l1hi, P.l1lo + (((uint64_t)b_end + 1) << P.l1shift) - 1);
-                  sh.cmd = Cmd{OP_COMPACT, 0, P.l1lo, bhi, 0, 0};
-                  P.state = ST_AFTER_PREFIX;
-                } else if (needA) {
-                  P.stage = 0;
-                  P.qkind = Q_COUNT;
-                  P.tcount = (uint64_t)(r.K - 1);
-                  P.state = ST_LOC_BIN;
-                } else if (MODE == 1) {
-                  P.state = ST_FINISH;
-                  sh.tp_ovf = 1;
-                } else {
-                  P.WA = P.Wv;
-                  P.ckA = P.l1hi;
-                  P.stage = 1;
-                  if (r.topp) {
-                    P.thr = __dmul_rn((double)r.P, (double)P.WA);
-                    if (!(0.0 < P.thr)) {
-                      P.qkind = Q_COUNT;
-                      P.tcount = 0;
-                    } else {
-                      P.qkind = Q_LASTLT;
-                    }
-                  } else {
-                    P.WK = P.WA;
-                    P.ckK = P.ckA;
-                    P.stage = 2;
-                    P.qkind = Q_POINT;
-                    P.tpoint = draw_point(u, P.WK);
-                  }
-                  P.state = ST_LOC_BIN;
-                }
-              }
-              __syncthreads();
-              if (P.state == ST_AFTER_PREFIX) break;
-              continue;
-            }
-            if (tid == 0) {
-              P.level = 1;
-              P.state = ST_LOC_BIN;
-            }
-            continue;
-          }
-          if (state == ST_LOC_BIN) {
-            const uint32_t *C = P.level == 0 ? L.l1c : L.refc;
-            const uint64_t *M = P.level == 0 ? L.l1m : L.refm;
-            if (tid == 0) sh.bcast_i = -1;
-            __syncthreads();
-            for (int b = tid; b < P.nbins; b += NT) {
-              const uint64_t pc0 = P.base_c + (b ? C[b - 1] : 0), pc1 = P.base_c + C[b];
-              const uint64_t pm0 = P.base_m + (b ? M[b - 1] : 0), pm1 = P.base_m + M[b];
-              bool hit = false;
-              if (P.qkind == Q_COUNT) hit = pc0 <= P.tcount && P.tcount < pc1;
-              else if (P.qkind == Q_POINT) hit = pm0 <= P.tpoint && P.tpoint < pm1;
-              if (hit) sh.bcast_i = b;
-              if (P.qkind == Q_LASTLT && pc1 > pc0 && (double)pm0 < P.thr) atomicMax(&sh.bcast_i, b);
-            }
-            __syncthreads();
-            if (tid == 0) {
-              const int b = sh.bcast_i;
-              if (b < 0) {  // cannot happen for consistent inputs; finish defensively
-                P.state = ST_FINISH;
-                sh.res.status |= MSTAR_STATUS_EMPTY;
-              } else {
-                const uint64_t blo = P.lo + ((uint64_t)b << P.shift);
-                const uint64_t bhi = u64min(P.hi, blo + (1ull << P.shift) - 1);
-                const uint64_t cnt = (uint64_t)C[b] - (b ? C[b - 1] : 0);
-                P.cbase_c = P.base_c + (b ? C[b - 1] : 0);
-                P.cbase_m = P.base_m + (b ? M[b - 1] : 0);
-                if (cnt <= (uint64_t)GCAP || P.shift == 0) {
-                  sh.cmd = Cmd{OP_COMPACT, 0, blo, bhi, 0, 0};
-                  P.state = ST_LOC_AFTER_COMPACT;
-                } else {
-                  P.base_c = P.cbase_c;
-                  P.base_m = P.cbase_m;
-                  P.lo = blo;
-                  P.hi = bhi;
-                  const int bits = 64 - __clzll((long long)(bhi - blo));
-                  P.shift = bits > NBIN_LOG2 ? bits - NBIN_LOG2 : 0;
-                  P.nbins = (int)((bhi - blo) >> P.shift) + 1;
-                  sh.cmd = Cmd{OP_HIST, TGT_REF, blo, bhi, P.shift, P.nbins};
-                  P.state = ST_LOC_AFTER_REF;
-                }
-              }
-            }
-            __syncthreads();
-            if (P.state == ST_LOC_AFTER_REF) {
-              for (int b = tid; b < NBIN; b += NT) {
-                L.refc[b] = 0;
-                L.refm[b] = 0;
-              }
-            }
-            if (P.state == ST_FINISH) continue;
-            break;
-          }
-          if (state == ST_AFTER_PREFIX) {
-            if (tid < 32) {  // per-CTA counts of the compacted range
-              const uint32_t c = lane < S ? min(cluster.map_shared_rank(&sh, lane)->nloc, (uint32_t)LCAP) : 0u;
-              uint32_t inc = c;
-              for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t v = __shfl_up_sync(~0u, inc, o);
-                if (lane >= o) inc += v;
-              }
-              if (lane < 16) {
-                sh.goff[lane] = inc - c;
-                sh.gcnt[lane] = c;
-              }
-              const uint32_t tot = __shfl_sync(~0u, inc, 31);
-              if (lane == 0) sh.ncand = min(tot, (uint32_t)TAIL_CAP);
-            }
-            __syncthreads();
-            if (tid < TW) small_tail(sh.gcnt, sh.goff, 0, true, (int)sh.ncand);
-            if (tid == 0) P.state = ST_FINISH;
-            __syncthreads();
-            continue;
-          }
-          if (state == ST_LOC_AFTER_COMPACT) {
-            int n = 0;
-            for (int q = 0; q < S; ++q) {  // gather every CTA's list (DSMEM)
-              const int c = (int)min(cluster.map_shared_rank(&sh, q)->nloc, (uint32_t)LCAP);
-              const Cand *src = cluster.map_shared_rank(L.lcand, q);
-              for (int i = tid; i < c; i += NT)
-                if (n + i < GCAP) L.gsort.in[n + i] = src[i];
-              n += c;
-            }
-            n = min(n, GCAP);
-            __syncthreads();
-            tail_sort_scan(L.gsort.in, n, m, L.gsort, sh);
-            const uint64_t *Sx = L.gsort.S;
-            const Cand *sorted = L.gsort.in;
-            if (tid == 0) sh.bcast_i = -1;
-            __syncthreads();
-            for (int j = tid; j < n; j += NT) {
-              const uint64_t se = P.cbase_m + S_excl(Sx, j), si = P.cbase_m + Sx[j];
-              bool hit = false;
-              if (P.qkind == Q_COUNT) hit = (P.cbase_c + j) == P.tcount;
-              else if (P.qkind == Q_POINT) hit = se <= P.tpoint && P.tpoint < si;
-              if (hit) sh.bcast_i = j;
-              if (P.qkind == Q_LASTLT && (double)se < P.thr) atomicMax(&sh.bcast_i, j);
-            }
-            __syncthreads();
-            if (tid == 0) {
-              const int j = sh.bcast_i;
-              if (j < 0) {
-                P.state = ST_FINISH;
-                sh.res.status |= MSTAR_STATUS_EMPTY;
-              } else {
-                const uint64_t ck = ckey(km, sorted[j].x, sorted[j].gid);
-                const uint64_t si = P.cbase_m + Sx[j];
-                P.level = 0;
-                P.lo = P.l1lo;
-                P.hi = P.l1hi;
-                P.shift = P.l1shift;
-                P.nbins = P.l1nbins;
-                P.base_c = 0;
-                P.base_m = 0;
-                if (P.stage == 0) {  // A boundary (top_k)
-                  P.WA = si;
-                  P.ckA = ck;
-                  if (MODE == 1 || r.K <= TAIL_CAP) {
-                    sh.cmd = Cmd{OP_COMPACT, 0, P.l1lo, ck, 0, 0};
-                    P.state = ST_AFTER_PREFIX;
-                  } else {
-                    P.stage = 1;
-                    if (r.topp) {
-                      P.thr = __dmul_rn((double)r.P, (double)P.WA);
-                      if (!(0.0 < P.thr)) {
-                        P.qkind = Q_COUNT;
-                        P.tcount = 0;
-                      } else {
-                        P.qkind = Q_LASTLT;
-                      }
-                    } else {
-                      P.WK = P.WA;
-                      P.ckK = P.ckA;
-                      P.stage = 2;
-                      P.qkind = Q_POINT;
-                      P.tpoint = draw_point(u, P.WK);
-                    }
-                    P.state = ST_LOC_BIN;
-                  }
-                } else if (P.stage == 1) {  // top-p boundary: last kept element
-                  P.WK = si;
-                  P.ckK = ck;
-                  P.stage = 2;
-                  P.qkind = Q_POINT;
-                  P.tpoint = draw_point(u, P.WK);
-                  P.state = ST_LOC_BIN;
-                } else {  // draw
-                  sh.res.token = sorted[j].gid;
-                  sh.res.WK = P.WK;
-                  sh.res.ckK = P.ckK;
-                  P.state = ST_FINISH;
-                }
-              }
-            }
-            __syncthreads();
-            if (P.state == ST_AFTER_PREFIX) break;
-            continue;
-          }
-          if (state == ST_FINISH) {
-            if (tid == 0) sh.cmd = Cmd{OP_DONE, 0, 0, 0, 0, 0};
-            break;
-          }
-        }
-        __syncthreads();
-      }
-      cluster.sync();  // command published
-      const Cmd cmd = cluster.map_shared_rank(&sh, 0)->cmd;
-      if (cmd.op == OP_DONE) break;
-      if (cmd.op == OP_HIST) {
-        uint32_t *hc = rank == 0 ? (cmd.target == TGT_L1 ? L.l1c : L.refc) : L.l1c;
-        uint64_t *hm = rank == 0 ? (cmd.target == TGT_L1 ? L.l1m : L.refm) : L.l1m;
-        if (rank != 0) {
-          for (int b = tid; b < NBIN; b += NT) {
-            hc[b] = 0;
-            hm[b] = 0;
-          }
-          __syncthreads();
-        }
-        for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount,
-                          [&](float x, uint32_t gid, uint64_t w) {
-                            const uint64_t ck = ckey(km, x, gid);
-                            if (ck < cmd.lo || ck > cmd.hi) return;
-                            const int b = (int)((ck - cmd.lo) >> cmd.shift);
-                            atomicAdd(&hc[b], 1u);
-                            atomicAdd((unsigned long long *)&hm[b], (unsigned long long)w);
-                          });
-        if (rank != 0) {
-          __syncthreads();
-          uint32_t *rc = cluster.map_shared_rank(cmd.target == TGT_L1 ? L.l1c : L.refc, 0);
-          uint64_t *rm = cluster.map_shared_rank(cmd.target == TGT_L1 ? L.l1m : L.refm, 0);
-          for (int b = tid; b < cmd.nbins; b += NT) {
-            if (hc[b]) {
-              atomicAdd(&rc[b], hc[b]);
-              atomicAdd((unsigned long long *)&rm[b], (unsigned long long)hm[b]);
-            }
-          }
-        }
-      } else {  // OP_COMPACT into the CTA-local list
-        if (tid == 0) sh.nloc = 0;
-        __syncthreads();
-        for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount,
-                          [&](float x, uint32_t gid, uint64_t w) {
-                            const uint64_t ck = ckey(km, x, gid);
-                            if (ck < cmd.lo || ck > cmd.hi) return;
-                            const uint32_t idx = atomicAdd(&sh.nloc, 1u);
-                            if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
-                          });
-      }
-      cluster.sync();  // round results complete
-    }
+    general_path<T, MODE>(ctx, sh);
   }
 
   // ---- leader: outputs and state updates
@@ -1731,43 +1966,9 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
   }
-
-  // ---- debug dense outputs (recomputed from global memory)
   if (debug) {
     cluster.sync();
-    const Result res = cluster.map_shared_rank(&sh, 0)->res;
-    const uint32_t kmm = okey(res.m);
-    const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)slot * p.allowed_words : nullptr;
-    auto emit = [&](int64_t e, float x) {
-      const int64_t o = (int64_t)row * p.V + e;
-      const uint32_t gid = (uint32_t)(e + gbase);
-      bool kept = false;
-      float prob = 0.0f;
-      if (!res.empty && x == x) {
-        if (res.greedy) {
-          kept = gid == res.token;
-          prob = kept ? 1.0f : 0.0f;
-        } else if (x > -INFINITY && x <= res.m && ckey(kmm, x, gid) <= res.ckK) {
-          kept = true;
-          prob = (float)__ddiv_rn((double)spec_w_from_e(spec_e(x, res.m)), (double)res.WK);
-        }
-      }
-      if (p.out_x) p.out_x[o] = x;
-      if (p.out_kept) p.out_kept[o] = kept ? 1 : 0;
-      if (p.out_probs) p.out_probs[o] = prob;
-    };
-    for (int64_t e = c0 + tid; e < c1; e += NT) {
-      const float v = Elem<T>::load(rowp, e);
-      const int64_t g = e + gbase;
-      const bool allowed = !aw || ((aw[g >> 5] >> (g & 31)) & 1u);
-      float x;
-      if (v != v) x = v;
-      else if (!allowed) x = -INFINITY;
-      else x = r.greedy ? v : __fmul_rn(v, r.invT);
-      emit(e, x);
-    }
-    __syncthreads();
-    for (int i = tid; i < nspec; i += NT) emit((int64_t)L.spec[i].gid - gbase, L.spec[i].x);
+    debug_dense<T>(ctx, sh);
   }
   if (!fast || debug) cluster.sync();  // keep shared memory alive until every remote access is done
 }
@@ -1803,8 +2004,12 @@ __global__ void __launch_bounds__(NT, 1)
   status &= ~(uint32_t)MSTAR_STATUS_EMPTY;
   if (tid == 0) {
     sh.nloc = 0;
+    sh.best = 0xFFFFFFFFu;
     sh.res.token = 0;
     sh.theta = 0.0f;
+    sh.u = p.uniforms ? p.uniforms[row]
+                      : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
+    tail_reset(sh);
   }
   const bool empty = !(m > -INFINITY);
   const bool one = r.greedy || r.K == 1;
@@ -1817,6 +2022,8 @@ __global__ void __launch_bounds__(NT, 1)
     const float theta = sh.theta;
     const uint32_t km = okey(m);
     uint32_t best = 0xFFFFFFFFu;
+    uint64_t kmn = ~0ull, kmx = 0ull;
+    uint32_t np = 0;
     for (int q = 0; q < tp_world; ++q) {
       const uint32_t *rec = recv + ((int64_t)q * p.B + row) * rec_words;
       const int n = (int)min(rec[1], (uint32_t)tp_cap);
@@ -1826,31 +2033,19 @@ __global__ void __launch_bounds__(NT, 1)
         if (one) {
           if (x == m) best = min(best, gid);
         } else if (x >= theta) {
-          const uint64_t w = weight_A(r, x, m);
-          if (w) {
-            const uint32_t idx = atomicAdd(&sh.nloc, 1u);
-            if (idx < (uint32_t)TAIL_CAP) {
-              ts.K[idx] = ckey(km, x, gid);
-              ts.W[idx] = w;
-            }
-          }
+          const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+          if (idx < (uint32_t)TAIL_CAP) tail_put(r, m, km, Cand{x, gid}, (int)idx, ts, kmn, kmx, np);
         }
       }
     }
     if (one) {
-      best = block_min_u32(best, sh);
-      if (tid == 0) sh.res.token = best;
-    } else {
+      if (best != 0xFFFFFFFFu) atomicMin(&sh.best, best);
       __syncthreads();
-      const int n = (int)min(sh.nloc, (uint32_t)TAIL_CAP);
-      if (tid < TW) {
-        tail_sort_small(n, km - okey(theta), ts, sh);
-        if (tid == 0) {
-          const float u = p.uniforms ? p.uniforms[row]
-                                     : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
-          tail_resolve(r, n, u, ts, sh.res);
-        }
-      }
+      if (tid == 0) sh.res.token = sh.best;
+    } else {
+      tail_gather_end(kmn, kmx, np, ts, sh);
+      tail_sort((int)min(sh.nloc, (uint32_t)TAIL_CAP), ts, sh);
+      tail_resolve(r, sh.u, ts, sh);
     }
   }
   __syncthreads();
