@@ -50,7 +50,7 @@ namespace cg = cooperative_groups;
 
 namespace mstar {
 
-constexpr int NT = 1024;            // threads per CTA
+constexpr int NT = 512;             // threads per CTA
 constexpr int NWARP = NT / 32;
 constexpr int TAIL_CAP = 2048;      // candidates the fast tail resolves
 constexpr int LCAP = TAIL_CAP;      // CTA-local candidate list (general path)
@@ -65,7 +65,9 @@ constexpr int CHUNK_BYTES = 32768;  // bulk-copy granule (one mbarrier each)
 constexpr int MAX_CHUNKS = 8;       // slice data <= 256 KB
 constexpr int MAX_ROUNDS = 96;      // bound on general-path rounds
 constexpr int BIAS_SMEM = 256;      // bias entries staged in shared memory
-constexpr int QCAP = 2048;          // vectors queued by the candidate scan before draining
+constexpr int QCAP = 2048;          // vectors queued by the first pass (all warps)
+constexpr int WQCAP = QCAP / (NT / 32);  // per-warp share of the queue
+constexpr int PU = 4;                    // vectors per thread per trip of the first pass
 constexpr int GQCAP = 1024;         // vectors queued per general-path round
 constexpr int GEN_BYTES = 12288 + 14336 + GCAP * 8 + GQCAP * 4;  // L1 | REF/sort | sort input | queue
 static_assert(NBIN * 12 <= 12288, "L1 / REF histograms");
@@ -74,7 +76,7 @@ static_assert(GBK <= NT && NBIN % NT == 0 && NBK % NT == 0 && TAIL_CAP % NT == 0
 constexpr int WORK_BYTES_MIN = GEN_BYTES;
 constexpr int LEAN_SCRATCH = 112 * 1024;  // fast-tail scratch (the leader's data region)
 static_assert(TAIL_CAP * 44 + NBK * 12 <= LEAN_SCRATCH, "fast tail scratch");
-static_assert(NBK % NT == 0 && NBK / NT <= 2, "tail bucket scan");
+static_assert(NBK % NT == 0, "tail bucket scan");
 constexpr unsigned kWaitLimit = 1u << 24;
 
 struct __align__(8) Cand {
@@ -170,6 +172,7 @@ struct CtaSh {
   uint32_t n_spec;
   uint32_t ht_fail;
   uint32_t qcount;
+  uint32_t wqn[NWARP];  // vectors each warp queued in the first pass
   float theta;
   float m;
   int fast;
@@ -193,6 +196,39 @@ __device__ __forceinline__ uint64_t u64max(uint64_t a, uint64_t b) { return a > 
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// First of `cnt` consecutive slots in a shared list for each lane of a full
+// warp (all 32 lanes call it together): one atomic per warp.
+__device__ __forceinline__ uint32_t warp_reserve(uint32_t *counter, uint32_t cnt) {
+  const int lane = threadIdx.x & 31;
+  uint32_t inc = cnt;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(~0u, inc, o);
+    if (lane >= o) inc += t;
+  }
+  const uint32_t tot = __shfl_sync(~0u, inc, 31);
+  uint32_t base = 0;
+  if (lane == 31 && tot) base = atomicAdd(counter, tot);
+  return __shfl_sync(~0u, base, 31) + inc - cnt;
+}
+
+// 4-byte asynchronous global -> shared copy (completes at cp_async_wait_all
+// of the issuing thread).
+__device__ __forceinline__ void cp_async4(void *dst, uintptr_t src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Whether the aligned 32-bit word holding element e of a row of V elements
+// lies inside the row (a 2-byte element at a word boundary as the row's last
+// element would pull in 2 bytes past it).
+template <typename T>
+__device__ __forceinline__ bool word_in_row(const uint8_t *rowp, int64_t e, int64_t V) {
+  if (sizeof(T) == 4) return true;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(rowp + e * 2);
+  return (a & 2u) != 0 || e + 1 < V;
 }
 
 // Split cluster barrier: a CTA may touch a peer's shared memory only once
@@ -286,6 +322,8 @@ struct Elem<float> {
   static __device__ __forceinline__ float smem_elem(const uint8_t *data, int64_t pos) {
     return reinterpret_cast<const float *>(data)[pos];
   }
+  // element e of the row from the aligned 32-bit word that holds it
+  static __device__ __forceinline__ float from_word(uint32_t w, const uint8_t *, int64_t) { return __uint_as_float(w); }
 };
 
 template <>
@@ -352,6 +390,11 @@ struct Elem<__nv_bfloat16> {
   }
   static __device__ __forceinline__ float smem_elem(const uint8_t *data, int64_t pos) {
     return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(data)[pos] << 16);
+  }
+  // element e of the row from the aligned 32-bit word that holds it
+  static __device__ __forceinline__ float from_word(uint32_t w, const uint8_t *rowp, int64_t e) {
+    const bool hi = (reinterpret_cast<uintptr_t>(rowp + e * 2) & 2u) != 0;
+    return __uint_as_float(hi ? (w & 0xFFFF0000u) : (w << 16));
   }
 };
 
@@ -904,7 +947,7 @@ __device__ void tail_sort(int n, const TailScr &s, CtaSh &sh) {
     s.P[i] = (b << 16) | pos;
   }
   __syncthreads();
-  {  // inclusive scans of counts and masses; NB / NT (<= 2) buckets per thread
+  {  // inclusive scans of counts and masses; NBK / NT buckets per thread
     constexpr int PER = NBK / NT;
     const int b0 = t * PER;
     uint32_t c = 0;
@@ -930,8 +973,8 @@ __device__ void tail_sort(int n, const TailScr &s, CtaSh &sh) {
       sh.red_u64[wid] = im;
     }
     __syncthreads();
-    uint32_t wc = sh.red_u32[lane];
-    uint64_t wm = sh.red_u64[lane];
+    uint32_t wc = lane < NWARP ? sh.red_u32[lane] : 0u;
+    uint64_t wm = lane < NWARP ? sh.red_u64[lane] : 0ull;
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t uc = __shfl_up_sync(~0u, wc, o);
       const uint64_t um = __shfl_up_sync(~0u, (unsigned long long)wm, o);
@@ -1034,6 +1077,144 @@ __device__ void tail_emit(const Row &r, uint32_t km, int tp_cap, uint32_t *rec, 
   }
   if (threadIdx.x == 0) sh.nemit = ne;
   __syncthreads();
+}
+
+// The whole tail on one warp, for at most 32 * E candidates (E per lane, in
+// registers; element i lives in lane i / E, slot i % E): keys and weights,
+// a bitonic sort, prefix sums with shuffles, then the queries (step) or the
+// record (TP shard).  The candidate lists are those of the fast path (list q
+// at lists + q * stride, cnt[q] entries placed at off[q]).
+template <int E>
+__device__ __forceinline__ uint64_t lane_pick(const uint64_t (&a)[E], int h) {
+  uint64_t v = a[0];
+#pragma unroll
+  for (int q = 1; q < E; ++q) v = h == q ? a[q] : v;
+  return v;
+}
+
+template <int E>
+__device__ void tail_warp(const Row &r, float m, uint32_t km, float u, int S, const uint32_t *cnt,
+                          const uint32_t *off, const Cand *lists, int stride, int n, int mode, int tp_cap,
+                          uint32_t *rec, CtaSh &sh) {
+  const int lane = threadIdx.x & 31;
+  uint64_t key[E], w[E];
+#pragma unroll
+  for (int h = 0; h < E; ++h) {
+    const int i = lane * E + h;
+    key[h] = ~0ull;
+    w[h] = 0ull;
+    if (i < n) {
+      for (int q = 0; q < S; ++q) {
+        const int o = (int)off[q];
+        if (i >= o && i < o + (int)cnt[q]) {
+          const Cand cd = lists[q * stride + (i - o)];
+          key[h] = ckey(km, cd.x, cd.gid);
+          w[h] = weight_A(r, cd.x, m);
+        }
+      }
+    }
+  }
+  for (int k = 2; k <= 32 * E; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j < E) {  // both elements in this lane
+#pragma unroll
+        for (int h = 0; h < E; ++h) {
+          if (h & j) continue;
+          const int h2 = h | j;
+          const bool asc = ((lane * E + h) & k) == 0;
+          if (asc ? (key[h2] < key[h]) : (key[h2] > key[h])) {
+            const uint64_t tk = key[h], tw = w[h];
+            key[h] = key[h2];
+            w[h] = w[h2];
+            key[h2] = tk;
+            w[h2] = tw;
+          }
+        }
+      } else {  // partner in lane ^ (j / E), same slot
+        const int lj = j / E;
+#pragma unroll
+        for (int h = 0; h < E; ++h) {
+          const uint64_t ok = __shfl_xor_sync(~0u, (unsigned long long)key[h], lj);
+          const uint64_t ow = __shfl_xor_sync(~0u, (unsigned long long)w[h], lj);
+          const int i = lane * E + h;
+          const bool keep_min = ((i & k) == 0) == ((i & j) == 0);
+          if (keep_min ? (ok < key[h]) : (ok > key[h])) {
+            key[h] = ok;
+            w[h] = ow;
+          }
+        }
+      }
+    }
+  }
+  // weight-0 candidates fail the predicate and sort behind every passing one
+  int np = 0;
+#pragma unroll
+  for (int h = 0; h < E; ++h) np += __popc(__ballot_sync(~0u, w[h] != 0ull));
+  uint64_t inc[E], exc[E];
+  uint64_t lt = 0;
+#pragma unroll
+  for (int h = 0; h < E; ++h) {
+    lt += w[h];
+    inc[h] = lt;
+  }
+  uint64_t li = lt;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t t = __shfl_up_sync(~0u, (unsigned long long)li, o);
+    if (lane >= o) li += t;
+  }
+#pragma unroll
+  for (int h = 0; h < E; ++h) {
+    inc[h] += li - lt;
+    exc[h] = inc[h] - w[h];
+  }
+  const int nA = r.topk ? min(np, r.K) : np;
+  if (mode == 1) {
+    if (nA <= tp_cap) {
+#pragma unroll
+      for (int h = 0; h < E; ++h) {
+        const int i = lane * E + h;
+        if (i < nA) {
+          rec[4 + 2 * i] = __float_as_uint(okey_inv(km - (uint32_t)(key[h] >> 32)));
+          rec[5 + 2 * i] = (uint32_t)(key[h] & 0xFFFFFFFFu);
+        }
+      }
+    }
+    if (lane == 0) sh.nemit = nA;
+    return;
+  }
+  if (nA <= 0) {  // no candidate carries weight: the leading one stands
+    const uint64_t k0 = __shfl_sync(~0u, (unsigned long long)key[0], 0);
+    if (lane == 0) {
+      sh.res.token = (uint32_t)(k0 & 0xFFFFFFFFu);
+      sh.res.WK = 0;
+      sh.res.ckK = k0;
+    }
+    return;
+  }
+  int nK = nA;
+  if (r.topp) {  // kept ranks: j == 0 or S_j < P * W_A (a prefix)
+    const uint64_t WA = __shfl_sync(~0u, (unsigned long long)lane_pick<E>(inc, (nA - 1) % E), (nA - 1) / E);
+    const double thr = __dmul_rn((double)r.P, (double)WA);
+    int c = 0;
+#pragma unroll
+    for (int h = 0; h < E; ++h) c += __popc(__ballot_sync(~0u, lane * E + h < nA && (double)exc[h] < thr));
+    nK = max(c, 1);
+  }
+  const uint64_t WK = __shfl_sync(~0u, (unsigned long long)lane_pick<E>(inc, (nK - 1) % E), (nK - 1) / E);
+  const uint64_t rr = draw_point(u, WK);
+  uint64_t tk = 0;
+#pragma unroll
+  for (int h = 0; h < E; ++h) {
+    const unsigned hit = __ballot_sync(~0u, lane * E + h < nK && exc[h] <= rr && rr < inc[h]);
+    const uint64_t t = __shfl_sync(~0u, (unsigned long long)key[h], hit ? __ffs(hit) - 1 : 0);
+    if (hit) tk = t;
+  }
+  const uint64_t ck = __shfl_sync(~0u, (unsigned long long)lane_pick<E>(key, (nK - 1) % E), (nK - 1) / E);
+  if (lane == 0) {
+    sh.res.token = (uint32_t)(tk & 0xFFFFFFFFu);
+    sh.res.WK = WK;
+    sh.res.ckK = ck;
+  }
 }
 
 // ------------------------------------------------------------ the kernel
@@ -1603,6 +1784,10 @@ __global__ void __launch_bounds__(NT, 1)
     // specials: history / seen bits / bias ids that fall in [c0, c1).  The
     // thread that creates a table entry sets the position's skip bit and
     // records whether it was already set (a disallowed position).
+    // The creator also takes the special's list entry and starts an
+    // asynchronous copy of the 32-bit word holding its logit into it, so
+    // the special can be finalized before the chunk holding it lands.
+    uint32_t *spec32 = reinterpret_cast<uint32_t *>(L.spec);
     auto add_special = [&](int64_t e, int cnt) {
       int h;
       const int created = ht_insert(L.ht, pl.ht_cap, (int)e, cnt, h);
@@ -1612,15 +1797,34 @@ __global__ void __launch_bounds__(NT, 1)
         const int64_t pos = e - c0al;
         const uint32_t bit = 1u << (pos & 31);
         if (atomicOr(&skip32[pos >> 5], bit) & bit) atomicOr(&L.ht[h].y, HT_MASKED);
+        cg::coalesced_group g = cg::coalesced_threads();
+        uint32_t cb = 0;
+        if (g.thread_rank() == 0) cb = atomicAdd(&sh.n_spec, (uint32_t)g.size());
+        const uint32_t ci = g.shfl(cb, 0) + g.thread_rank();
+        if ((int)ci < pl.spec_cap) {
+          spec32[2 * ci] = (uint32_t)h;
+          if (word_in_row<T>(rowp, e, p.V))
+            cp_async4(&spec32[2 * ci + 1], reinterpret_cast<uintptr_t>(rowp + e * es) & ~(uintptr_t)3);
+        } else {
+          sh.ht_fail = 1;
+        }
       }
     };
     if (has_hist) {
       const int32_t len = p.hist_len[slot];
       const int n = min(len, p.H);
       const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
-      for (int j = tid; j < n; j += NT) {
-        const int64_t e = (int64_t)h[j] - gbase;
-        if (e >= c0 && e < c1) add_special(e, 1);
+      // repeated ids are merged inside each warp first (one table update
+      // per distinct id per warp and step)
+      for (int j0 = 0; j0 < n; j0 += NT) {
+        const int j = j0 + tid;
+        int e = -1;
+        if (j < n) {
+          const int64_t g = (int64_t)h[j] - gbase;
+          if (g >= c0 && g < c1) e = (int)g;
+        }
+        const unsigned same = __match_any_sync(~0u, (unsigned)e);
+        if (e >= 0 && __ffs(same) - 1 == lane) add_special(e, __popc(same));
       }
     } else if (p.seen_bits) {
       const uint32_t *sw = p.seen_bits + (int64_t)slot * p.seen_words;
@@ -1646,20 +1850,22 @@ __global__ void __launch_bounds__(NT, 1)
         if (e >= c0 && e < c1) add_special(e, 0);
       }
     }
-    __syncthreads();  // bitmap and table complete
+    cp_async_commit();
+    __syncthreads();  // bitmap, table and special list entries complete
   }
   const Row r = sh.row;
   const Slice sl{data4, L.skip, nvec, pos0_gid};
   const bool one = r.greedy || r.K == 1;
 
-  // ---- pass A, chunk by chunk as the bulk copies land: masked raw max, and
-  // a queue of the vectors whose max reaches the running threshold
-  // thr(M) = M - |M| 2^-10 + lq T (1 + 2^-10), M a raw max seen so far and
-  // lq the lowest threshold offset the final value threshold can take.
+  // ---- pass A, block by block as the bulk copies land: masked raw max; a
+  // per-warp queue of the vectors whose max reaches the running threshold
+  // thr(M) = M - |M| 2^-10 + lq T (1 + 2^-10) (M a raw max seen so far, lq
+  // the lowest offset below the CTA max that this CTA's value threshold can
+  // take); the specials of each block as soon as its values are resident.
   float lq = 0.0f;
   if (!one) {
     lq = -33.0f;
-    if (r.minp) lq = fmaxf(lq, __fadd_rn(r.lnMp, -1.25f));
+    if (r.minp) lq = fmaxf(lq, __fadd_rn(r.lnMp, -0.25f));
   }
   const float lqr = one ? 0.0f : __fmul_rn(lq, __fmul_rn(r.T, 1.0009765625f));
   auto thr_of = [&](float M) -> float {
@@ -1667,20 +1873,18 @@ __global__ void __launch_bounds__(NT, 1)
     return __fadd_rn(__fmaf_rn(fabsf(M), -0x1p-10f, M), lqr);
   };
   Acc racc = Elem<T>::acc_init();
-  float runM = -INFINITY;
-  bool boot = true, qopen = true, timed_out = false;
+  float runM = -INFINITY, spec_max = -INFINITY;
+  bool boot = true, timed_out = false;
+  uint32_t wq = 0;  // vectors this warp queued (warp-uniform)
+  int *const wqueue = L.queue + (tid >> 5) * WQCAP;
   auto enqueue = [&](bool pass, int k) {
     const unsigned bal = __ballot_sync(~0u, pass);
-    if (bal && qopen) {
-      const int leader = __ffs(bal) - 1;
-      uint32_t base = 0;
-      if (lane == leader) base = atomicAdd(&sh.qcount, (uint32_t)__popc(bal));
-      base = __shfl_sync(~0u, base, leader);
+    if (bal) {
       if (pass) {
-        const uint32_t idx = base + (uint32_t)__popc(bal & ((1u << lane) - 1u));
-        if (idx < (uint32_t)QCAP) L.queue[idx] = k;
+        const uint32_t idx = wq + (uint32_t)__popc(bal & ((1u << lane) - 1u));
+        if (idx < (uint32_t)WQCAP) wqueue[idx] = k;
       }
-      qopen = base + (uint32_t)__popc(bal) <= (uint32_t)QCAP;
+      wq += (uint32_t)__popc(bal);
     }
   };
   auto process = [&](int kb, int ke) {  // vectors [kb, ke); uniform trip count
@@ -1690,39 +1894,88 @@ __global__ void __launch_bounds__(NT, 1)
       th = thr_of(runM);
     }
     float cmx = -INFINITY;
-    for (int base = kb; base < ke; base += 2 * NT) {
-      const int k0 = base + tid, k1 = k0 + NT;
-      float v0 = -INFINITY, v1 = -INFINITY;
-      if (k0 < ke) {
-        const Acc a = Elem<T>::vred(load_masked<T>(sl, k0));
-        racc = Elem<T>::acc_max(racc, a);
-        v0 = Elem<T>::acc_f(a);
+    for (int base = kb; base < ke; base += PU * NT) {
+      float v[PU];
+#pragma unroll
+      for (int u = 0; u < PU; ++u) {
+        const int k = base + u * NT + tid;
+        v[u] = -INFINITY;
+        if (k < ke) {
+          const Acc a = Elem<T>::vred(load_masked<T>(sl, k));
+          racc = Elem<T>::acc_max(racc, a);
+          v[u] = Elem<T>::acc_f(a);
+        }
       }
-      if (k1 < ke) {
-        const Acc a = Elem<T>::vred(load_masked<T>(sl, k1));
-        racc = Elem<T>::acc_max(racc, a);
-        v1 = Elem<T>::acc_f(a);
-      }
-      const float vm = fmaxf(v0, v1);
-      if (boot) {  // first block: the warp's own max sets the threshold
+      float vm = v[0];
+#pragma unroll
+      for (int u = 1; u < PU; ++u) vm = fmaxf(vm, v[u]);
+      if (boot) {  // first trip: the CTA max over it sets the threshold
         float w = vm;
         for (int o = 16; o; o >>= 1) w = fmaxf(w, __shfl_xor_sync(~0u, w, o));
-        th = thr_of(w);
-        runM = w;
         if (lane == 0 && w > -INFINITY) atomicMax(&sh.runmax, okey(w));
+        __syncthreads();  // uniform: every thread runs the same trips
+        runM = okey_inv(sh.runmax);
+        th = thr_of(runM);
         boot = false;
       }
       cmx = fmaxf(cmx, vm);
-      enqueue(v0 > -INFINITY && v0 >= th, k0);
-      enqueue(v1 > -INFINITY && v1 >= th, k1);
+#pragma unroll
+      for (int u = 0; u < PU; ++u) enqueue(v[u] > -INFINITY && v[u] >= th, base + u * NT + tid);
     }
     if (cmx > runM) atomicMax(&sh.runmax, okey(cmx));
+  };
+  // specials: bias (list order) -> penalties -> mask -> transform, for the
+  // table entries whose vector lies in [kb, ke); SB slots per thread at a
+  // time, appended with one atomic per warp (none when the warp has none)
+  float penR = 1.0f, penF = 0.0f, penP = 0.0f;
+  if (has_spec) {
+    penR = p.rep_pen ? p.rep_pen[slot] : 1.0f;
+    penF = p.freq_pen ? p.freq_pen[slot] : 0.0f;
+    penP = p.pres_pen ? p.pres_pen[slot] : 0.0f;
+  }
+  // Specials: bias (list order) -> penalties -> mask -> transform.  Their
+  // logits were fetched by asynchronous copies started when the table was
+  // built, so this runs after the first block without waiting for the
+  // chunks that hold them.  Entry i of the list holds (table slot, logit
+  // word) and becomes (x, id) in place.
+  auto finalize = [&]() {
+    cp_async_wait_all();
+    __syncthreads();  // every thread's copies have landed
+    const bool bias_smem = p.bias_ids && p.NB <= BIAS_SMEM;
+    const int32_t *bi = p.bias_ids ? p.bias_ids + (int64_t)slot * p.NB : nullptr;
+    const float *bv = p.bias_vals ? p.bias_vals + (int64_t)slot * p.NB : nullptr;
+    const int n = min((int)sh.n_spec, pl.spec_cap);
+    const uint32_t *spec32 = reinterpret_cast<const uint32_t *>(L.spec);
+    for (int i = tid; i < n; i += NT) {
+      const int2 ent = L.ht[spec32[2 * i]];
+      const int cnt = ent.y & ~HT_MASKED;
+      float v = word_in_row<T>(rowp, ent.x, p.V) ? Elem<T>::from_word(spec32[2 * i + 1], rowp, ent.x)
+                                                  : Elem<T>::load(rowp, ent.x);
+      if (bi) {
+        const int32_t gid = (int32_t)(ent.x + gbase);
+        for (int j = 0; j < p.NB; ++j) {
+          const int32_t id = bias_smem ? L.bias_id[j] : bi[j];
+          if (id == gid) v = __fadd_rn(v, bias_smem ? L.bias_val[j] : bv[j]);
+        }
+      }
+      if (cnt > 0) {
+        v = (v > 0.0f) ? __fdiv_rn(v, penR) : __fmul_rn(v, penR);
+        v = __fsub_rn(v, __fmul_rn(penF, (float)cnt));
+        v = __fsub_rn(v, penP);
+      }
+      float x;
+      if (v != v) x = v;
+      else if (ent.y & HT_MASKED) x = -INFINITY;
+      else x = xform(r, v);
+      L.spec[i] = Cand{x, (uint32_t)(ent.x + gbase)};
+      spec_max = fmaxf(spec_max, x);
+    }
   };
   {
     // blocks in order: bulk chunk 0 (it sets the threshold), the fringe
     // vectors (head, tail), then the remaining chunks as they land
     constexpr int CV = CHUNK_BYTES / 16;
-    const int nblk = nchunk + 2;
+    const int nblk = max(nchunk, 1) + 2;
     for (int bi = 0; bi < nblk; ++bi) {
       int kb, ke;
       if (bi == 1) {
@@ -1739,124 +1992,118 @@ __global__ void __launch_bounds__(NT, 1)
         ke = hv + min(nbv, (j + 1) * CV);
       }
       process(kb, ke);
+      if (has_spec && bi == 2) finalize();
     }
   }
   if (timed_out) atomicOr(&sh.status, MSTAR_STATUS_TIMEOUT);
-  const float rawmax = Elem<T>::acc_f(racc);
-  // finalize specials: bias (list order) -> penalties -> mask -> transform
-  float spec_max = -INFINITY;
-  if (has_spec) {
-    const float R = p.rep_pen ? p.rep_pen[slot] : 1.0f;
-    const float F = p.freq_pen ? p.freq_pen[slot] : 0.0f;
-    const float Pp = p.pres_pen ? p.pres_pen[slot] : 0.0f;
-    const bool bias_smem = p.bias_ids && p.NB <= BIAS_SMEM;
-    const int32_t *bi = p.bias_ids ? p.bias_ids + (int64_t)slot * p.NB : nullptr;
-    const float *bv = p.bias_vals ? p.bias_vals + (int64_t)slot * p.NB : nullptr;
-    for (int i = tid; i < pl.ht_cap; i += NT) {
-      const int2 ent = L.ht[i];
-      if (ent.x < 0) continue;
-      const int64_t e = ent.x;
-      const int cnt = ent.y & ~HT_MASKED;
-      float v = Elem<T>::smem_elem(L.data, e - c0al);
-      if (bi) {
-        const int32_t gid = (int32_t)(e + gbase);
-        for (int j = 0; j < p.NB; ++j) {
-          const int32_t id = bias_smem ? L.bias_id[j] : bi[j];
-          if (id == gid) v = __fadd_rn(v, bias_smem ? L.bias_val[j] : bv[j]);
-        }
-      }
-      if (cnt > 0) {
-        v = (v > 0.0f) ? __fdiv_rn(v, R) : __fmul_rn(v, R);
-        v = __fsub_rn(v, __fmul_rn(F, (float)cnt));
-        v = __fsub_rn(v, Pp);
-      }
-      float x;
-      if (v != v) x = v;
-      else if (ent.y & HT_MASKED) x = -INFINITY;
-      else x = xform(r, v);
-      const uint32_t idx = atomicAdd(&sh.n_spec, 1u);
-      if ((int)idx < pl.spec_cap) L.spec[idx] = Cand{x, (uint32_t)(e + gbase)};
-      else sh.ht_fail = 1;
-      spec_max = fmaxf(spec_max, x);
-    }
-  }
+  if (lane == 0) sh.wqn[tid >> 5] = wq;
   {
-    float cm = fmaxf(xform(r, rawmax), spec_max);
-    for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(~0u, cm, o));
-    if (lane == 0 && cm > -INFINITY) atomicMax(&sh.cmax, okey(cm));
+    float cmx = fmaxf(xform(r, Elem<T>::acc_f(racc)), spec_max);
+    for (int o = 16; o; o >>= 1) cmx = fmaxf(cmx, __shfl_xor_sync(~0u, cmx, o));
+    if (lane == 0 && cmx > -INFINITY) atomicMax(&sh.cmax, okey(cmx));
   }
-  __syncthreads();  // CTA max, queue, specials complete
-  if (tid == 0 && sh.ht_fail) sh.status |= MSTAR_STATUS_SPECIAL_OVERFLOW;
+  __syncthreads();  // CTA max, queues, specials complete
+  const float cm = okey_inv(sh.cmax);  // this CTA's max (transformed)
   const int nspec = min((int)sh.n_spec, pl.spec_cap);
-  cluster_wait();  // every CTA of the cluster runs
-  if (tid < S) cluster.map_shared_rank(&sh, tid)->maxes[rank] = okey_inv(sh.cmax);  // push to every CTA
-  cluster.sync();  // #1: maxima published
-
-  // ---- row max and value threshold (warp 0)
+  // ---- this CTA's value threshold, from its own max: every member of the
+  // row's A set (whose max m >= cm) has x >= theta(cm)
   if (tid < 32) {
-    float mm = lane < S ? sh.maxes[lane] : -INFINITY;
-    for (int o = 16; o; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(~0u, mm, o));
-    const float t = mm > -INFINITY ? choose_theta(r, mm) : INFINITY;
-    if (lane == 0) {
-      sh.m = mm;
-      sh.theta = t;
-    }
+    const float t = cm > -INFINITY ? choose_theta(r, cm) : INFINITY;
+    if (lane == 0) sh.theta = t;
   }
   __syncthreads();
-  const float m = sh.m;
-  const bool empty = !(m > -INFINITY);
-  const float theta = sh.theta;
-  const uint32_t km = okey(m);
+  const float theta_l = sh.theta;
   const int capq = TAIL_CAP / S;  // candidates each CTA may push to the leader
+  cluster_wait();                 // every CTA of the cluster runs: remote stores are safe
 
-  // ---- candidates: x >= theta (or x == m for greedy / top-1) from the
+  // ---- candidates: x >= theta(cm) (or x == cm for greedy / top-1) from the
   // queued vectors and the specials, pushed into the leader's region
-  if (!empty) {
-    const float tcut = one ? m : theta;
+  if (cm > -INFINITY) {
+    const float tcut = one ? cm : theta_l;
     // every queue threshold used was <= thr(CTA raw max): if a value below
-    // it can still reach tcut, or the queue overflowed, scan every vector
+    // it can still reach tcut, or a queue overflowed, scan every vector
     const float thq = thr_of(okey_inv(sh.runmax));
-    const bool rescan = sh.qcount > (uint32_t)QCAP || (thq > -INFINITY && !(xform(r, prev_float(thq)) < tcut));
+    const bool rescan = __any_sync(~0u, lane < NWARP && sh.wqn[lane] > (uint32_t)WQCAP) ||
+                        (thq > -INFINITY && !(xform(r, prev_float(thq)) < tcut));
     Cand *const lead = cluster.map_shared_rank(L.lcand, 0) + rank * capq;
     uint32_t best = 0xFFFFFFFFu;
-    auto take = [&](float x, uint32_t gid) {
-      if (one) {
-        if (x == m) best = min(best, gid);
-      } else if (x >= theta) {
-        const uint32_t idx = atomicAdd(&sh.nloc, 1u);
-        if (idx < (uint32_t)capq) lead[idx] = Cand{x, gid};
+    // one vector per lane per step (warp-uniform step count); the passing
+    // values are appended with one atomic per warp
+    auto scan_vec = [&](int k, bool valid) {
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      bool any = false;
+      if (valid) {
+        v = load_masked<T>(sl, k);
+        any = xform(r, Elem<T>::vmax(v)) >= tcut;
+      }
+      const uint32_t gid0 = (uint32_t)(pos0_gid + (int64_t)k * VEC);
+      uint32_t pm = 0;
+      if (any) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float x = xform(r, Elem<T>::get(v, j));
+          if (one) {
+            if (x == cm) best = min(best, gid0 + (uint32_t)j);
+          } else if (x >= theta_l) {
+            pm |= 1u << j;
+          }
+        }
+      }
+      if (one || !__any_sync(~0u, pm != 0u)) return;
+      uint32_t o = warp_reserve(&sh.nloc, (uint32_t)__popc(pm));
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        if (!((pm >> j) & 1u)) continue;
+        if (o < (uint32_t)capq) lead[o] = Cand{xform(r, Elem<T>::get(v, j)), gid0 + (uint32_t)j};
+        ++o;
       }
     };
-    auto scan_vec = [&](int k) {
-      const uint4 v = load_masked<T>(sl, k);
-      if (!(xform(r, Elem<T>::vmax(v)) >= tcut)) return;
-      const uint32_t gid0 = (uint32_t)(pos0_gid + (int64_t)k * VEC);
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) take(xform(r, Elem<T>::get(v, j)), gid0 + (uint32_t)j);
-    };
-    const int nscan = rescan ? nvec : (int)sh.qcount;
-    for (int i = tid; i < nscan; i += NT) scan_vec(rescan ? i : L.queue[i]);
-    for (int i = tid; i < nspec; i += NT) take(L.spec[i].x, L.spec[i].gid);
+    if (rescan) {
+      for (int k0 = 0; k0 < nvec; k0 += NT) scan_vec(k0 + tid, k0 + tid < nvec);
+    } else {  // each warp drains its own queue
+      const int nq = (int)min(wq, (uint32_t)WQCAP);
+      for (int i0 = 0; i0 < nq; i0 += 32) scan_vec(i0 + lane < nq ? wqueue[i0 + lane] : 0, i0 + lane < nq);
+    }
+    for (int i0 = 0; i0 < nspec; i0 += NT) {
+      const int i = i0 + tid;
+      const bool valid = i < nspec;
+      const Cand c = valid ? L.spec[i] : Cand{-INFINITY, 0u};
+      if (one) {
+        if (valid && c.x == cm) best = min(best, c.gid);
+        continue;
+      }
+      const bool pass = valid && c.x >= theta_l;
+      if (!__any_sync(~0u, pass)) continue;
+      const uint32_t o = warp_reserve(&sh.nloc, pass ? 1u : 0u);
+      if (pass && o < (uint32_t)capq) lead[o] = c;
+    }
     if (best != 0xFFFFFFFFu) atomicMin(&sh.best, best);
   }
   __syncthreads();
-  if (tid < S) {  // push this CTA's count / status / lowest id to every CTA
+  if (tid < S) {  // push this CTA's max, count, status and lowest id to every CTA
     CtaSh *peer = cluster.map_shared_rank(&sh, tid);
+    peer->maxes[rank] = cm;
     peer->gcnt[rank] = sh.nloc;
-    peer->gstat[rank] = sh.status;
+    peer->gstat[rank] = sh.status | (sh.ht_fail ? (uint32_t)MSTAR_STATUS_SPECIAL_OVERFLOW : 0u);
     peer->gmin[rank] = sh.best;
   }
-  cluster.sync();  // #2: candidates and counts delivered
+  cluster.sync();  // #1: candidates, maxima and counts delivered
 
-  // every CTA takes the same decision from the delivered counts
+  // every CTA takes the same decision from the delivered values
   const bool debug = MODE == 0 && (p.out_x || p.out_kept || p.out_probs);
+  float m;
   bool fast;
   {
+    float mq = lane < S ? sh.maxes[lane] : -INFINITY;
+    for (int o = 16; o; o >>= 1) mq = fmaxf(mq, __shfl_xor_sync(~0u, mq, o));
+    m = mq;
     const uint32_t cq = lane < S ? sh.gcnt[lane] : 0u;
     const bool ovf = __any_sync(~0u, cq > (uint32_t)capq);
-    fast = empty || one || (!ovf && !(p.flags & MSTAR_FLAG_FORCE_GENERAL));
+    fast = !(m > -INFINITY) || one || (!ovf && !(p.flags & MSTAR_FLAG_FORCE_GENERAL));
   }
+  const bool empty = !(m > -INFINITY);
   if (fast && rank != 0 && !debug) return;  // nothing of this CTA is read any more
+  const uint32_t km = okey(m);
   if (tid < 32) {
     const uint32_t cq = lane < S ? min(sh.gcnt[lane], (uint32_t)capq) : 0u;
     uint32_t inc = cq;
@@ -1865,13 +2112,16 @@ __global__ void __launch_bounds__(NT, 1)
       if (lane >= o) inc += v;
     }
     const uint32_t st = __reduce_or_sync(~0u, lane < S ? sh.gstat[lane] : 0u);
-    const uint32_t mg = __reduce_min_sync(~0u, lane < S ? sh.gmin[lane] : 0xFFFFFFFFu);
+    const uint32_t mg = __reduce_min_sync(~0u, (lane < S && sh.maxes[lane] == m) ? sh.gmin[lane] : 0xFFFFFFFFu);
+    // the general path needs the row's own value threshold
+    const float tg = (!fast && !empty) ? choose_theta(r, m) : INFINITY;
     if (lane < 16) sh.goff[lane] = inc - cq;
     if (lane == 31) sh.ncand = inc;
     if (lane == 0) {
+      sh.theta = tg;
       sh.min_all = mg;
       sh.res.m = m;
-      sh.res.theta = theta;
+      sh.res.theta = tg;
       sh.res.greedy = r.greedy;
       sh.res.empty = empty;
       sh.res.token = 0;
@@ -1881,6 +2131,7 @@ __global__ void __launch_bounds__(NT, 1)
     }
   }
   __syncthreads();
+  const float theta = sh.theta;
   uint32_t *rec = MODE == 1 ? tp_send + (int64_t)row * pl.rec_words : nullptr;
   RowCtx ctx;
   if (!fast || debug) {
@@ -1913,6 +2164,15 @@ __global__ void __launch_bounds__(NT, 1)
           sh.res.WK = 4294967296ull;
           sh.res.ckK = (uint64_t)sh.min_all;
           sh.nemit = -1;
+        }
+      } else if (sh.ncand <= 64u) {  // one warp, in registers
+        if (tid < 32) {
+          if (sh.ncand <= 32u)
+            tail_warp<1>(r, m, km, MODE == 0 ? sh.u : 0.0f, S, sh.gcnt, sh.goff, L.lcand, capq, (int)sh.ncand,
+                         MODE, pl.tp_cap, rec, sh);
+          else
+            tail_warp<2>(r, m, km, MODE == 0 ? sh.u : 0.0f, S, sh.gcnt, sh.goff, L.lcand, capq, (int)sh.ncand,
+                         MODE, pl.tp_cap, rec, sh);
         }
       } else {  // the candidates pushed into this CTA's region, gap-free by goff
         const int n = (int)sh.ncand;

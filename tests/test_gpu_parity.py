@@ -98,3 +98,32 @@ def test_seen_bits_update():
     for r, t in enumerate(out.cpu().numpy()):
         exp[r, t >> 5] |= np.uint32(1) << np.uint32(t & 31)
     np.testing.assert_array_equal(after, exp)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("cluster", [0, 3])
+def test_candidate_count_paths(oracle_lib, dtype, cluster):
+    """Rows whose candidate set has an exact size: N ids near the top, the
+    rest far below, min_p tiny.  The sizes straddle every tail variant (one
+    warp with one or two candidates per lane, the block tail, the general
+    path) and each row mixes top_k / top_p settings."""
+    from mstar_rs_b200.workloads import Batch, f32_to_bf16_bits
+
+    sizes = [1, 2, 31, 32, 33, 63, 64, 65, 200, 530, 2047, 2600]
+    V, B = 24000, len(sizes)
+    rng = np.random.default_rng(11 + cluster)
+    x = np.full((B, V), -60.0, np.float32) + rng.standard_normal((B, V)).astype(np.float32)
+    for r, n in enumerate(sizes):
+        ids = rng.choice(V, n, replace=False)
+        x[r, ids] = rng.uniform(0.0, 4.0, n).astype(np.float32)
+    logits = f32_to_bf16_bits(x) if dtype == "bf16" else x
+    case = Batch(logits=logits, dtype=dtype,
+                 temperature=np.full(B, 0.9, np.float32),
+                 top_k=np.array([0, 0, 20, 0, 50, 0, 0, 40, 0, 100, 0, 0], np.int32),
+                 top_p=np.array([1.0, 0.9, 1.0, 0.8, 0.95, 1.0, 0.5, 0.99, 0.9, 0.85, 1.0, 0.97], np.float32),
+                 min_p=np.full(B, 1e-6, np.float32),
+                 uniforms=rng.random(B, dtype=np.float32),
+                 name="candidate_counts")
+    o = oracle_lib.run(case, debug=True)
+    g = run_gpu(case, cluster_size=cluster)
+    assert_parity(g, o, case)
