@@ -147,6 +147,7 @@ struct Row {
   const void *rowp;
   int64_t V, gbase;  // gbase = vocab_offset
   float T, invT, Mp, lnMp, P;
+  float R, F, Pp;    // repetition / frequency / presence penalties
   int K;             // 0 = off
   bool greedy, topk, minp, topp;
 };
@@ -168,6 +169,8 @@ struct CtaSh {
   uint64_t kmin, kmax;  // tail: key range
   uint32_t npass;       // tail: candidates passing the value-A predicate
   uint32_t cnt_k;       // tail: ranks kept by top_p
+  uint32_t pf_n, pf_zero;  // top_k pre-selection: kept count, a zero offset
+  int pf_bstar;            // top_k pre-selection: last kept bucket
   float u;              // the row's uniform draw
   uint32_t n_spec;
   uint32_t ht_fail;
@@ -516,6 +519,9 @@ __device__ __forceinline__ void row_init(Row &r, const mstar_sampler_params_t &p
   r.lnMp = r.minp ? logf(r.Mp) : 0.0f;
   r.P = p.top_p ? p.top_p[slot] : 1.0f;
   r.topp = r.P < 1.0f;
+  r.R = p.rep_pen ? p.rep_pen[slot] : 1.0f;
+  r.F = p.freq_pen ? p.freq_pen[slot] : 0.0f;
+  r.Pp = p.pres_pen ? p.pres_pen[slot] : 0.0f;
 }
 
 // value-A predicate of x given the row max m (positive weight and min_p).
@@ -1079,137 +1085,211 @@ __device__ void tail_emit(const Row &r, uint32_t km, int tp_cap, uint32_t *rec, 
   __syncthreads();
 }
 
-// The whole tail on one warp, for at most 32 * E candidates (E per lane, in
-// registers; element i lives in lane i / E, slot i % E): keys and weights,
-// a bitonic sort, prefix sums with shuffles, then the queries (step) or the
-// record (TP shard).  The candidate lists are those of the fast path (list q
-// at lists + q * stride, cnt[q] entries placed at off[q]).
-template <int E>
-__device__ __forceinline__ uint64_t lane_pick(const uint64_t (&a)[E], int h) {
-  uint64_t v = a[0];
+// top_k pre-selection for a tail with more candidates than top_k: counts of
+// the order keys in PF_NB buckets over their range; every candidate in a
+// bucket at or below the one holding the K-th smallest key is kept (at least
+// K, including all of the K smallest) in one compacted list at s.RS.  The
+// kept candidates' first K are the row's first K, and whether they carry
+// weight is decided the same way, so the tail runs unchanged on the list.
+// Block-wide; ends with a barrier; leaves the tail state reset.
+constexpr int PF_NB = 256;
+__device__ void tail_topk_prefilter(const Row &r, uint32_t km, int S, const uint32_t *cnt, const uint32_t *off,
+                                    const Cand *lists, int stride, int n, const TailScr &s, CtaSh &sh) {
+  const int t = threadIdx.x, lane = t & 31;
+  uint64_t kmn = ~0ull, kmx = 0ull;
+  for (int q = 0; q < S; ++q) {
+    const int c = (int)cnt[q], o = (int)off[q];
+    for (int i = t; i < c; i += NT) {
+      const Cand cd = lists[q * stride + i];
+      const uint64_t k = ckey(km, cd.x, cd.gid);
+      s.RK[o + i] = k;
+      kmn = u64min(kmn, k);
+      kmx = u64max(kmx, k);
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    kmn = u64min(kmn, (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)kmn, o));
+    kmx = u64max(kmx, (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)kmx, o));
+  }
+  if (lane == 0 && kmn <= kmx) {
+    atomicMin((unsigned long long *)&sh.kmin, (unsigned long long)kmn);
+    atomicMax((unsigned long long *)&sh.kmax, (unsigned long long)kmx);
+  }
+  for (int b = t; b < PF_NB; b += NT) s.bc[b] = 0;
+  __syncthreads();
+  const uint64_t kmin = sh.kmin, range = sh.kmax - kmin;
+  const int bits = range ? 64 - __clzll((long long)range) : 0;
+  const int bsh = bits > 8 ? bits - 8 : 0;
+  static_assert(PF_NB == 256, "8-bit buckets");
+  for (int i = t; i < n; i += NT) atomicAdd(&s.bc[(uint32_t)((s.RK[i] - kmin) >> bsh)], 1u);
+  __syncthreads();
+  if (t < 32) {  // first bucket whose inclusive count reaches K
+    constexpr int PB = PF_NB / 32;
+    uint32_t c[PB], sum = 0;
 #pragma unroll
-  for (int q = 1; q < E; ++q) v = h == q ? a[q] : v;
-  return v;
+    for (int j = 0; j < PB; ++j) {
+      c[j] = s.bc[lane * PB + j];
+      sum += c[j];
+    }
+    uint32_t inc = sum;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(~0u, inc, o);
+      if (lane >= o) inc += v;
+    }
+    uint32_t run = inc - sum;
+    int hit = PF_NB;
+#pragma unroll
+    for (int j = 0; j < PB; ++j) {
+      run += c[j];
+      if (hit == PF_NB && run >= (uint32_t)r.K) hit = lane * PB + j;
+    }
+    hit = __reduce_min_sync(~0u, hit);
+    if (lane == 0) {
+      sh.pf_bstar = hit;
+      sh.pf_n = 0;
+      sh.pf_zero = 0;
+      tail_reset(sh);
+    }
+  }
+  __syncthreads();
+  const uint32_t bstar = (uint32_t)sh.pf_bstar;
+  Cand *out = reinterpret_cast<Cand *>(s.RS);
+  for (int q = 0; q < S; ++q) {  // warp-uniform trip counts: one reservation per warp and step
+    const int c = (int)cnt[q], o = (int)off[q];
+    for (int i0 = 0; i0 < c; i0 += NT) {
+      const int i = i0 + t;
+      const bool keep = i < c && (uint32_t)((s.RK[o + i] - kmin) >> bsh) <= bstar;
+      if (!__any_sync(~0u, keep)) continue;
+      const uint32_t w = warp_reserve(&sh.pf_n, keep ? 1u : 0u);
+      if (keep) out[w] = lists[q * stride + i];
+    }
+  }
+  __syncthreads();
+}
+
+// The whole tail on one warp, for at most 32 * E candidates (E = 1 or 2 per
+// lane, in registers: element i is slot i / 32 of lane i % 32): keys and
+// weights, a bitonic sort of each slot across the lanes and, for E = 2, a
+// bitonic merge of the two slots; prefix sums with shuffles; then the
+// queries (step) or the record (TP shard).  The candidate lists are those of
+// the fast path (list q at lists + q * stride, cnt[q] entries placed at
+// off[q]).  The two slots are named variables: indexed register arrays in
+// these unrolled loops compiled to far slower code.
+__device__ __forceinline__ void cas_lanes(uint64_t &key, uint64_t &w, int j, bool keep_min) {
+  const uint64_t ok = __shfl_xor_sync(~0u, (unsigned long long)key, j);
+  const uint64_t ow = __shfl_xor_sync(~0u, (unsigned long long)w, j);
+  const bool take = keep_min ? (ok < key) : (ok > key);
+  key = take ? ok : key;
+  w = take ? ow : w;
+}
+
+__device__ __forceinline__ void tail_warp_load(const Row &r, float m, uint32_t km, int S, const uint32_t *cnt,
+                                               const uint32_t *off, const Cand *lists, int stride, int n, int i,
+                                               uint64_t &key, uint64_t &w) {
+  key = ~0ull;
+  w = 0ull;
+  if (i >= n) return;
+  for (int q = 0; q < S; ++q) {
+    const int o = (int)off[q];
+    if (i >= o && i < o + (int)cnt[q]) {
+      const Cand cd = lists[q * stride + (i - o)];
+      key = ckey(km, cd.x, cd.gid);
+      w = weight_A(r, cd.x, m);
+    }
+  }
 }
 
 template <int E>
 __device__ void tail_warp(const Row &r, float m, uint32_t km, float u, int S, const uint32_t *cnt,
                           const uint32_t *off, const Cand *lists, int stride, int n, int mode, int tp_cap,
                           uint32_t *rec, CtaSh &sh) {
+  static_assert(E == 1 || E == 2, "one or two candidates per lane");
   const int lane = threadIdx.x & 31;
-  uint64_t key[E], w[E];
+  uint64_t k0, w0, k1 = ~0ull, w1 = 0ull;
+  tail_warp_load(r, m, km, S, cnt, off, lists, stride, n, lane, k0, w0);
+  if (E == 2) tail_warp_load(r, m, km, S, cnt, off, lists, stride, n, 32 + lane, k1, w1);
 #pragma unroll
-  for (int h = 0; h < E; ++h) {
-    const int i = lane * E + h;
-    key[h] = ~0ull;
-    w[h] = 0ull;
-    if (i < n) {
-      for (int q = 0; q < S; ++q) {
-        const int o = (int)off[q];
-        if (i >= o && i < o + (int)cnt[q]) {
-          const Cand cd = lists[q * stride + (i - o)];
-          key[h] = ckey(km, cd.x, cd.gid);
-          w[h] = weight_A(r, cd.x, m);
-        }
-      }
+  for (int k = 2; k <= 32; k <<= 1) {  // each slot ascending across the lanes
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const bool keep_min = ((lane & k) == 0) == ((lane & j) == 0);
+      cas_lanes(k0, w0, j, keep_min);
+      if (E == 2) cas_lanes(k1, w1, j, keep_min);
     }
   }
-  for (int k = 2; k <= 32 * E; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      if (j < E) {  // both elements in this lane
+  if (E == 2) {  // merge: slot 1 reversed, half-cleaner across the slots, then clean each slot
+    const uint64_t rk = __shfl_sync(~0u, (unsigned long long)k1, 31 - lane);
+    const uint64_t rw = __shfl_sync(~0u, (unsigned long long)w1, 31 - lane);
+    const bool lo = k0 < rk;
+    k1 = lo ? rk : k0;
+    w1 = lo ? rw : w0;
+    k0 = lo ? k0 : rk;
+    w0 = lo ? w0 : rw;
 #pragma unroll
-        for (int h = 0; h < E; ++h) {
-          if (h & j) continue;
-          const int h2 = h | j;
-          const bool asc = ((lane * E + h) & k) == 0;
-          if (asc ? (key[h2] < key[h]) : (key[h2] > key[h])) {
-            const uint64_t tk = key[h], tw = w[h];
-            key[h] = key[h2];
-            w[h] = w[h2];
-            key[h2] = tk;
-            w[h2] = tw;
-          }
-        }
-      } else {  // partner in lane ^ (j / E), same slot
-        const int lj = j / E;
-#pragma unroll
-        for (int h = 0; h < E; ++h) {
-          const uint64_t ok = __shfl_xor_sync(~0u, (unsigned long long)key[h], lj);
-          const uint64_t ow = __shfl_xor_sync(~0u, (unsigned long long)w[h], lj);
-          const int i = lane * E + h;
-          const bool keep_min = ((i & k) == 0) == ((i & j) == 0);
-          if (keep_min ? (ok < key[h]) : (ok > key[h])) {
-            key[h] = ok;
-            w[h] = ow;
-          }
-        }
-      }
+    for (int j = 16; j > 0; j >>= 1) {
+      const bool keep_min = (lane & j) == 0;
+      cas_lanes(k0, w0, j, keep_min);
+      cas_lanes(k1, w1, j, keep_min);
     }
   }
   // weight-0 candidates fail the predicate and sort behind every passing one
-  int np = 0;
-#pragma unroll
-  for (int h = 0; h < E; ++h) np += __popc(__ballot_sync(~0u, w[h] != 0ull));
-  uint64_t inc[E], exc[E];
-  uint64_t lt = 0;
-#pragma unroll
-  for (int h = 0; h < E; ++h) {
-    lt += w[h];
-    inc[h] = lt;
-  }
-  uint64_t li = lt;
+  const int np = __popc(__ballot_sync(~0u, w0 != 0ull)) + (E == 2 ? __popc(__ballot_sync(~0u, w1 != 0ull)) : 0);
+  uint64_t i0 = w0, i1 = w1;
   for (int o = 1; o < 32; o <<= 1) {
-    const uint64_t t = __shfl_up_sync(~0u, (unsigned long long)li, o);
-    if (lane >= o) li += t;
+    const uint64_t t0 = __shfl_up_sync(~0u, (unsigned long long)i0, o);
+    const uint64_t t1 = E == 2 ? (uint64_t)__shfl_up_sync(~0u, (unsigned long long)i1, o) : 0ull;
+    if (lane >= o) {
+      i0 += t0;
+      i1 += t1;
+    }
   }
-#pragma unroll
-  for (int h = 0; h < E; ++h) {
-    inc[h] += li - lt;
-    exc[h] = inc[h] - w[h];
-  }
+  if (E == 2) i1 += __shfl_sync(~0u, (unsigned long long)i0, 31);
+  const uint64_t e0 = i0 - w0, e1 = i1 - w1;  // exclusive prefixes
   const int nA = r.topk ? min(np, r.K) : np;
   if (mode == 1) {
     if (nA <= tp_cap) {
-#pragma unroll
-      for (int h = 0; h < E; ++h) {
-        const int i = lane * E + h;
-        if (i < nA) {
-          rec[4 + 2 * i] = __float_as_uint(okey_inv(km - (uint32_t)(key[h] >> 32)));
-          rec[5 + 2 * i] = (uint32_t)(key[h] & 0xFFFFFFFFu);
-        }
+      if (lane < nA) {
+        rec[4 + 2 * lane] = __float_as_uint(okey_inv(km - (uint32_t)(k0 >> 32)));
+        rec[5 + 2 * lane] = (uint32_t)(k0 & 0xFFFFFFFFu);
+      }
+      if (E == 2 && 32 + lane < nA) {
+        rec[4 + 2 * (32 + lane)] = __float_as_uint(okey_inv(km - (uint32_t)(k1 >> 32)));
+        rec[5 + 2 * (32 + lane)] = (uint32_t)(k1 & 0xFFFFFFFFu);
       }
     }
     if (lane == 0) sh.nemit = nA;
     return;
   }
   if (nA <= 0) {  // no candidate carries weight: the leading one stands
-    const uint64_t k0 = __shfl_sync(~0u, (unsigned long long)key[0], 0);
+    const uint64_t kl = __shfl_sync(~0u, (unsigned long long)k0, 0);
     if (lane == 0) {
-      sh.res.token = (uint32_t)(k0 & 0xFFFFFFFFu);
+      sh.res.token = (uint32_t)(kl & 0xFFFFFFFFu);
       sh.res.WK = 0;
-      sh.res.ckK = k0;
+      sh.res.ckK = kl;
     }
     return;
   }
+  // element i's inclusive prefix / key, gathered from its lane
+  auto inc_at = [&](int i) -> uint64_t {
+    const uint64_t v = __shfl_sync(~0u, (unsigned long long)(i >= 32 ? i1 : i0), i & 31);
+    return v;
+  };
+  auto key_at = [&](int i) -> uint64_t {
+    return __shfl_sync(~0u, (unsigned long long)(i >= 32 ? k1 : k0), i & 31);
+  };
   int nK = nA;
   if (r.topp) {  // kept ranks: j == 0 or S_j < P * W_A (a prefix)
-    const uint64_t WA = __shfl_sync(~0u, (unsigned long long)lane_pick<E>(inc, (nA - 1) % E), (nA - 1) / E);
-    const double thr = __dmul_rn((double)r.P, (double)WA);
-    int c = 0;
-#pragma unroll
-    for (int h = 0; h < E; ++h) c += __popc(__ballot_sync(~0u, lane * E + h < nA && (double)exc[h] < thr));
+    const double thr = __dmul_rn((double)r.P, (double)inc_at(nA - 1));
+    int c = __popc(__ballot_sync(~0u, lane < nA && (double)e0 < thr));
+    if (E == 2) c += __popc(__ballot_sync(~0u, 32 + lane < nA && (double)e1 < thr));
     nK = max(c, 1);
   }
-  const uint64_t WK = __shfl_sync(~0u, (unsigned long long)lane_pick<E>(inc, (nK - 1) % E), (nK - 1) / E);
+  const uint64_t WK = inc_at(nK - 1);
   const uint64_t rr = draw_point(u, WK);
-  uint64_t tk = 0;
-#pragma unroll
-  for (int h = 0; h < E; ++h) {
-    const unsigned hit = __ballot_sync(~0u, lane * E + h < nK && exc[h] <= rr && rr < inc[h]);
-    const uint64_t t = __shfl_sync(~0u, (unsigned long long)key[h], hit ? __ffs(hit) - 1 : 0);
-    if (hit) tk = t;
-  }
-  const uint64_t ck = __shfl_sync(~0u, (unsigned long long)lane_pick<E>(key, (nK - 1) % E), (nK - 1) / E);
+  const unsigned h0 = __ballot_sync(~0u, lane < nK && e0 <= rr && rr < i0);
+  const unsigned h1 = E == 2 ? __ballot_sync(~0u, 32 + lane < nK && e1 <= rr && rr < i1) : 0u;
+  const uint64_t tk = key_at(h0 ? __ffs(h0) - 1 : (h1 ? 32 + __ffs(h1) - 1 : 0));
+  const uint64_t ck = key_at(nK - 1);
   if (lane == 0) {
     sh.res.token = (uint32_t)(tk & 0xFFFFFFFFu);
     sh.res.WK = WK;
@@ -1654,32 +1734,6 @@ __global__ void __launch_bounds__(NT, 1)
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ CtaSh sh;
 
-  const int slot = p.slot_idx ? p.slot_idx[row] : row;
-  if (slot < 0) {  // padding row: uniform across the cluster
-    if (rank == 0 && tid == 0) {
-      if (MODE == 0) {
-        if (p.out_ids) p.out_ids[row] = p.vocab_offset;
-        if (p.out_ids32) p.out_ids32[row] = (int32_t)p.vocab_offset;
-        if (p.out_status) p.out_status[row] = 0;
-      } else {
-        uint32_t *rec = tp_send + (int64_t)row * pl.rec_words;
-        rec[0] = __float_as_uint(-INFINITY);
-        rec[1] = 0;
-        rec[2] = 0;
-        rec[3] = 0;
-      }
-    }
-    if (MODE == 0 && (p.out_x || p.out_kept || p.out_probs)) {
-      const int64_t c0 = min((int64_t)rank * pl.slice, (int64_t)p.V), c1 = min((int64_t)p.V, c0 + pl.slice);
-      for (int64_t i = c0 + tid; i < c1; i += NT) {
-        const int64_t o = (int64_t)row * p.V + i;
-        if (p.out_x) p.out_x[o] = -INFINITY;
-        if (p.out_kept) p.out_kept[o] = 0;
-        if (p.out_probs) p.out_probs[o] = 0.0f;
-      }
-    }
-    return;
-  }
   cluster_arrive_relaxed();  // matched by the wait before the first remote store
 
   const Layout L = make_layout(smem, pl);
@@ -1702,7 +1756,8 @@ __global__ void __launch_bounds__(NT, 1)
   const int nchunk = (int)((nbulk + CHUNK_BYTES - 1) / CHUNK_BYTES);
   uint4 *data4 = reinterpret_cast<uint4 *>(L.data);
 
-  // ---- issue the bulk copies first; stage the row's parameters
+  // ---- the bulk copies go out before anything else (they depend on nothing
+  // but the geometry)
   if (tid == 0) {
     for (int j = 0; j < nchunk; ++j) mbar_init(&sh.mbar[j], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1712,6 +1767,52 @@ __global__ void __launch_bounds__(NT, 1)
       bulk_g2s(L.data + (b0 - a_al) + (int64_t)j * CHUNK_BYTES,
                reinterpret_cast<const void *>(b0 + (uintptr_t)j * CHUNK_BYTES), bytes, &sh.mbar[j]);
     }
+  }
+  const int slot = p.slot_idx ? p.slot_idx[row] : row;
+  if (slot < 0) {  // padding row (uniform across the cluster): drain the copies, write the padding outputs
+    if (tid == 0) {
+      for (int j = 0; j < nchunk; ++j) mbar_wait(&sh.mbar[j], 0);
+      if (rank == 0) {
+        if (MODE == 0) {
+          if (p.out_ids) p.out_ids[row] = p.vocab_offset;
+          if (p.out_ids32) p.out_ids32[row] = (int32_t)p.vocab_offset;
+          if (p.out_status) p.out_status[row] = 0;
+        } else {
+          uint32_t *rec = tp_send + (int64_t)row * pl.rec_words;
+          rec[0] = __float_as_uint(-INFINITY);
+          rec[1] = 0;
+          rec[2] = 0;
+          rec[3] = 0;
+        }
+      }
+    }
+    if (MODE == 0 && (p.out_x || p.out_kept || p.out_probs)) {
+      for (int64_t i = c0 + tid; i < c1; i += NT) {
+        const int64_t o = (int64_t)row * p.V + i;
+        if (p.out_x) p.out_x[o] = -INFINITY;
+        if (p.out_kept) p.out_kept[o] = 0;
+        if (p.out_probs) p.out_probs[o] = 0.0f;
+      }
+    }
+    return;
+  }
+  // row parameters and the history words this thread inserts: loads issued
+  // now, used after the first barrier
+  constexpr int HP = 2;  // history words prefetched per thread
+  static_assert(HP == 2, "the insertion loop reads hpre[0] / hpre[1]");
+  const bool has_hist = p.hist_ids && p.hist_len;
+  int hpre[HP];
+  int hlen = 0;
+  if (has_hist) {
+    const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
+    hlen = min(p.hist_len[slot], p.H);
+#pragma unroll
+    for (int u = 0; u < HP; ++u) {
+      const int j = u * NT + tid;
+      hpre[u] = j < p.H ? h[j] : -1;
+    }
+  }
+  if (tid == 0) {
     sh.nloc = 0;
     sh.qcount = 0;
     sh.status = 0;
@@ -1731,7 +1832,6 @@ __global__ void __launch_bounds__(NT, 1)
 
   const int64_t gbase = p.vocab_offset;
   const int64_t pos0_gid = gbase + c0al;  // gid of data position 0
-  const bool has_hist = p.hist_ids && p.hist_len;
   const bool has_spec = has_hist || p.seen_bits || p.bias_ids;
 
   // ---- setup while the copies fly: the skip bitmap (disallowed and
@@ -1811,20 +1911,10 @@ __global__ void __launch_bounds__(NT, 1)
       }
     };
     if (has_hist) {
-      const int32_t len = p.hist_len[slot];
-      const int n = min(len, p.H);
       const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
-      // repeated ids are merged inside each warp first (one table update
-      // per distinct id per warp and step)
-      for (int j0 = 0; j0 < n; j0 += NT) {
-        const int j = j0 + tid;
-        int e = -1;
-        if (j < n) {
-          const int64_t g = (int64_t)h[j] - gbase;
-          if (g >= c0 && g < c1) e = (int)g;
-        }
-        const unsigned same = __match_any_sync(~0u, (unsigned)e);
-        if (e >= 0 && __ffs(same) - 1 == lane) add_special(e, __popc(same));
+      for (int j = tid, u = 0; j < hlen; j += NT, ++u) {
+        const int64_t g = (int64_t)(u < HP ? (u == 0 ? hpre[0] : hpre[1]) : h[j]) - gbase;
+        if (g >= c0 && g < c1) add_special(g, 1);
       }
     } else if (p.seen_bits) {
       const uint32_t *sw = p.seen_bits + (int64_t)slot * p.seen_words;
@@ -1927,12 +2017,7 @@ __global__ void __launch_bounds__(NT, 1)
   // specials: bias (list order) -> penalties -> mask -> transform, for the
   // table entries whose vector lies in [kb, ke); SB slots per thread at a
   // time, appended with one atomic per warp (none when the warp has none)
-  float penR = 1.0f, penF = 0.0f, penP = 0.0f;
-  if (has_spec) {
-    penR = p.rep_pen ? p.rep_pen[slot] : 1.0f;
-    penF = p.freq_pen ? p.freq_pen[slot] : 0.0f;
-    penP = p.pres_pen ? p.pres_pen[slot] : 0.0f;
-  }
+  const float penR = r.R, penF = r.F, penP = r.Pp;
   // Specials: bias (list order) -> penalties -> mask -> transform.  Their
   // logits were fetched by asynchronous copies started when the table was
   // built, so this runs after the first block without waiting for the
@@ -2165,28 +2250,43 @@ __global__ void __launch_bounds__(NT, 1)
           sh.res.ckK = (uint64_t)sh.min_all;
           sh.nemit = -1;
         }
-      } else if (sh.ncand <= 64u) {  // one warp, in registers
-        if (tid < 32) {
-          if (sh.ncand <= 32u)
-            tail_warp<1>(r, m, km, MODE == 0 ? sh.u : 0.0f, S, sh.gcnt, sh.goff, L.lcand, capq, (int)sh.ncand,
-                         MODE, pl.tp_cap, rec, sh);
-          else
-            tail_warp<2>(r, m, km, MODE == 0 ? sh.u : 0.0f, S, sh.gcnt, sh.goff, L.lcand, capq, (int)sh.ncand,
-                         MODE, pl.tp_cap, rec, sh);
-        }
-      } else {  // the candidates pushed into this CTA's region, gap-free by goff
-        const int n = (int)sh.ncand;
+      } else {
+        // candidate lists: the pushed ones (S lists, gap-free by goff), or
+        // one list kept by the top_k pre-selection
         const TailScr ts = tail_scratch(L.data);  // the leader's slice data is dead by now
-        uint64_t kmn = ~0ull, kmx = 0ull;
-        uint32_t np = 0;
-        for (int q = 0; q < S; ++q) {
-          const int cq = min((int)sh.gcnt[q], capq), o = (int)sh.goff[q];
-          for (int i = tid; i < cq; i += NT) tail_put(r, m, km, L.lcand[q * capq + i], o + i, ts, kmn, kmx, np);
+        const Cand *lists = L.lcand;
+        const uint32_t *lcnt = sh.gcnt, *loff = sh.goff;
+        int nl = S, stride = capq, n = (int)sh.ncand;
+        if (r.topk && r.K < n && n > 64) {
+          tail_topk_prefilter(r, km, S, sh.gcnt, sh.goff, L.lcand, capq, n, ts, sh);
+          lists = reinterpret_cast<const Cand *>(ts.RS);
+          lcnt = &sh.pf_n;
+          loff = &sh.pf_zero;
+          nl = 1;
+          stride = 0;
+          n = (int)sh.pf_n;
         }
-        tail_gather_end(kmn, kmx, np, ts, sh);
-        tail_sort(n, ts, sh);
-        if (MODE == 0) tail_resolve(r, sh.u, ts, sh);
-        else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
+        if (n <= 64) {  // one warp, in registers
+          if (tid < 32) {
+            if (n <= 32)
+              tail_warp<1>(r, m, km, MODE == 0 ? sh.u : 0.0f, nl, lcnt, loff, lists, stride, n, MODE, pl.tp_cap,
+                           rec, sh);
+            else
+              tail_warp<2>(r, m, km, MODE == 0 ? sh.u : 0.0f, nl, lcnt, loff, lists, stride, n, MODE, pl.tp_cap,
+                           rec, sh);
+          }
+        } else {
+          uint64_t kmn = ~0ull, kmx = 0ull;
+          uint32_t np = 0;
+          for (int q = 0; q < nl; ++q) {
+            const int cq = (int)min(lcnt[q], (uint32_t)(nl == 1 ? n : capq)), o = (int)loff[q];
+            for (int i = tid; i < cq; i += NT) tail_put(r, m, km, lists[q * stride + i], o + i, ts, kmn, kmx, np);
+          }
+          tail_gather_end(kmn, kmx, np, ts, sh);
+          tail_sort(n, ts, sh);
+          if (MODE == 0) tail_resolve(r, sh.u, ts, sh);
+          else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
+        }
       }
     }
   } else {
