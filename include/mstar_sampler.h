@@ -20,8 +20,7 @@
  *   mstar_sampler_tp_local  <- the vocab-parallel half of the TP sampler whose
  *   mstar_sampler_tp_merge     tp_group keeps Thinker ranks in agreement
  *                              (python/mstar_rs/models/qwen3_omni.py:401-404, :408, :431)
- *   mstar_sampler_smem_bytes / mstar_sampler_cluster_size: launch planning
- *                              behind SamplerBuffers.allocate
+ *   mstar_sampler_plan      <- launch planning behind SamplerBuffers.allocate
  *                              (orpheus.py:101-103, qwen3_omni.py:431, :987-989)
  */
 #ifndef MSTAR_SAMPLER_H_
