@@ -248,6 +248,7 @@ class CudaGraphableSampler:
         self.sbuf = sbuf
         self.n = n
         self.out = torch.zeros(n, dtype=torch.int64, device=sbuf.device)
+        self.slot_idx: torch.Tensor | None = None  # [n] int32; -1 marks a padding row
         self._rids: list = []
 
     def sample(self, rids, logits: torch.Tensor, apply_penalty: bool = True) -> torch.Tensor:
@@ -260,7 +261,7 @@ class CudaGraphableSampler:
             kw.update(rep_pen=None, pres_pen=None, freq_pen=None)
         kernel.sampler_step(logits, num_slots=sb.max_bs, **kw, offset=sb.offset_buf,
                             seen_bits=sb.seen_tokens.buf, seen_cap=sb.seen_cap, out_ids=self.out,
-                            flags=N.FLAG_ADVANCE_OFFSET | N.FLAG_UPDATE_SEEN)
+                            slot_idx=self.slot_idx, flags=N.FLAG_ADVANCE_OFFSET | N.FLAG_UPDATE_SEEN)
         return self.out
 
     def sync_seen_token_masks(self, masks) -> None:
@@ -335,3 +336,75 @@ class SamplerBuffers:
         for r, v in zip(rids, vals):
             if r in self._req_offset:
                 self._req_offset[r] = int(v)
+
+
+class SamplerGraphBuckets:
+    """One captured CUDA graph per bucket size over fixed buffers, the way
+    the reference's batched decode graphs pad a batch to the next bucket and
+    discard the pad rows (python/mstar_rs/batched_graph.py:26-80,
+    orpheus.py:322-366).  Pad rows carry slot -1: the kernel skips them (no
+    sampling work, no state update).
+
+    Usage: ``capture()`` once after ``SamplerBuffers.allocate``; then every
+    step ``sample(rids, logits)`` stages the rows (outside any graph),
+    replays the smallest bucket that holds them and returns the ids of the
+    real rows.  ``sync(rids, masks)`` copies seen bits and RNG offsets back."""
+
+    def __init__(self, sbuf: SamplerBuffers, buckets=(1, 2, 4, 8, 16, 32, 64), dtype=torch.bfloat16):
+        self.sbuf = sbuf
+        self.buckets = sorted(b for b in set(buckets) if 1 <= b <= sbuf.max_bs)
+        if not self.buckets:
+            raise ValueError("no bucket fits max_bs")
+        top = self.buckets[-1]
+        self.logits = torch.zeros(top, sbuf.vocab_size, dtype=dtype, device=sbuf.device)
+        self.slot_idx = torch.full((top,), -1, dtype=torch.int32, device=sbuf.device)
+        self._samplers = {}
+        self._graphs = {}
+        self._last = None
+
+    def capture(self) -> None:
+        sb = self.sbuf
+        saved_off = sb.offset_buf.clone()
+        saved_seen = sb.seen_tokens.buf.clone()
+        self.slot_idx.fill_(-1)  # capture with every row padded: no state changes
+        stream = torch.cuda.Stream(device=sb.device)
+        stream.wait_stream(torch.cuda.current_stream(sb.device))
+        for b in self.buckets:
+            s = CudaGraphableSampler(sb, b)
+            s.slot_idx = self.slot_idx[:b]
+            with torch.cuda.stream(stream):
+                s.sample(None, self.logits[:b])  # warm-up outside capture
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                s.sample(None, self.logits[:b])
+            self._samplers[b], self._graphs[b] = s, g
+        torch.cuda.current_stream(sb.device).wait_stream(stream)
+        torch.cuda.synchronize(sb.device)
+        sb.offset_buf.copy_(saved_off)
+        sb.seen_tokens.buf.copy_(saved_seen)
+
+    def bucket_for(self, n: int) -> int:
+        for b in self.buckets:
+            if b >= n:
+                return b
+        raise ValueError(f"batch {n} exceeds the largest bucket {self.buckets[-1]}")
+
+    def sample(self, rids, logits: torch.Tensor, masks=None) -> torch.Tensor:
+        n = len(rids)
+        b = self.bucket_for(n)
+        self.sbuf.gather_for_request_ids(rids, n, gather_seen_tokens=masks is not None)
+        if masks is not None:
+            self.sbuf.stage_seen_token_masks(rids, masks)
+        self.logits[:n].copy_(logits)
+        self.slot_idx[:n].copy_(torch.arange(n, dtype=torch.int32))
+        self.slot_idx[n:b].fill_(-1)
+        self._graphs[b].replay()
+        self._last = list(rids)
+        return self._samplers[b].out[:n]
+
+    def sync(self, rids, masks=None) -> None:
+        sb = self.sbuf
+        if masks is not None:
+            for j, m in enumerate(masks):
+                m.bits.copy_(sb.seen_tokens.buf[j])
+        sb._store_offsets(list(rids))

@@ -118,3 +118,38 @@ def test_graph_replay_matches_oracle(oracle_lib):
     sampler.sync_seen_token_masks(masks)
     for i in range(n):
         np.testing.assert_array_equal(masks[i].to_bool().cpu().numpy(), seen_host[i])
+
+
+def test_graph_buckets_match_oracle(oracle_lib):
+    """Batches of 3, 1 and 6 requests through buckets (1, 2, 4, 8): pad rows
+    are skipped, real rows match the oracle, RNG offsets advance per step."""
+    import torch
+
+    from mstar_rs_b200 import sampling
+
+    rng = np.random.default_rng(21)
+    V = 4099
+    sbuf = sampling.SamplerBuffers.allocate(8, "cuda", vocab_size=V)
+    cfg = _cfg_rows(rng, 8)
+    seeds = rng.integers(0, 2**62, 8).astype(np.uint64)
+    rids = [f"b{i}" for i in range(8)]
+    for i, r in enumerate(rids):
+        c = sampling.SamplingConfig(vocab_size=V, temperature=float(cfg["temperature"][i]),
+                                    top_k=int(cfg["top_k"][i]), top_p=float(cfg["top_p"][i]),
+                                    min_p=float(cfg["min_p"][i]))
+        c.set_seed(int(seeds[i]))
+        sbuf.register_request(r, c)
+    gb = sampling.SamplerGraphBuckets(sbuf, buckets=(1, 2, 4, 8), dtype=torch.float32)
+    gb.capture()
+    step = {r: 0 for r in rids}
+    for batch in ([0, 3, 5], [2], [1, 4, 6, 7, 0, 3]):
+        rb = [rids[i] for i in batch]
+        x = (rng.standard_normal((len(batch), V)) * 2).astype(np.float32)
+        tok = gb.sample(rb, torch.from_numpy(x).cuda()).cpu().numpy()
+        gb.sync(rb)
+        case = Batch(logits=x, temperature=cfg["temperature"][batch], top_k=cfg["top_k"][batch],
+                     top_p=cfg["top_p"][batch], min_p=cfg["min_p"][batch], seed=seeds[batch],
+                     offset=np.array([step[r] for r in rb], np.uint64))
+        np.testing.assert_array_equal(tok, oracle_lib.run(case)["ids"], err_msg=f"batch {batch}")
+        for r in rb:
+            step[r] += 1
