@@ -379,7 +379,7 @@ def run_e2e(args, case, d, dev, stream, world):
     lf = case.logits_f32()
     for i, h in enumerate(host):
         h.copy_(torch.from_numpy(np.roll(lf, 13 * i, axis=1)).to(dt))
-    engine = sampling.Sampler(device=dev)
+    engine = sampling.Sampler(device=dev, max_requests=max(256, B))
     rids = [f"r{i}" for i in range(B)]
     for i, rid in enumerate(rids):
         engine.add_request(rid)

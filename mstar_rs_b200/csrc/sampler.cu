@@ -224,6 +224,22 @@ __device__ __forceinline__ void cp_async4(void *dst, uintptr_t src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
+// 64-bit sums in shared (or cluster shared) memory kept as two 32-bit words
+// lo[i], hi[i]: 32-bit atomics are native, 64-bit atomic adds are
+// compare-and-swap loops that serialise badly under contention.
+__device__ __forceinline__ void add_u64_split(uint32_t *lo, uint32_t *hi, uint64_t v) {
+  const uint32_t vl = (uint32_t)v;
+  uint32_t vh = (uint32_t)(v >> 32);
+  if (vl) {
+    const uint32_t old = atomicAdd(lo, vl);
+    vh += (old + vl < old) ? 1u : 0u;  // carry out of the low word
+  }
+  if (vh) atomicAdd(hi, vh);
+}
+__device__ __forceinline__ uint64_t get_u64_split(const uint32_t *lo, const uint32_t *hi) {
+  return ((uint64_t)*hi << 32) | *lo;
+}
+
 // Whether the aligned 32-bit word holding element e of a row of V elements
 // lies inside the row (a 2-byte element at a word boundary as the row's last
 // element would pull in 2 bytes past it).
@@ -593,77 +609,39 @@ __device__ __forceinline__ uint4 load_masked(const Slice &sl, int k) {
   return b ? Elem<T>::mask_out(v, b) : v;
 }
 
-// Iterate the value-A elements this CTA holds (resident vectors and the
-// special list), applying the exact predicate; fn(x, gid, w).  Phase 1 streams
-// every vector and queues (warp-aggregated) the few whose transformed max
-// reaches theta; phase 2 drains the queue one vector per thread.  If the
-// queue overflows, phase 2 rescans everything directly.  Block-wide.
+// Iterate the value-A elements this CTA holds whose order key lies in
+// [lo, hi] (resident vectors and the special list); fn(x, gid, w).  A vector
+// is skipped after one compare when its max is below both theta and the
+// smallest value the key range admits; keys are tested before the weight is
+// computed, so a narrow range costs little more than the vector scan.
+// Block-wide (no barrier inside).
 template <typename T, typename F>
 __device__ __forceinline__ void for_each_value(const Slice &sl, const Cand *spec, int nspec, const Row &r, float m,
-                                               float theta, int *queue, int qcap, uint32_t *qcount, F &&fn) {
+                                               float theta, uint64_t lo, uint64_t hi, F &&fn) {
   constexpr int VEC = Elem<T>::VEC;
-  const int lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) *qcount = 0;
-  __syncthreads();
-  const int rounds = (sl.nvec + NT * 4 - 1) / (NT * 4);
-  for (int rd = 0; rd < rounds; ++rd) {
-    uint4 v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int k = rd * NT * 4 + u * NT + threadIdx.x;
-      if (k < sl.nvec) v[u] = load_masked<T>(sl, k);
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int k = rd * NT * 4 + u * NT + threadIdx.x;
-      bool pass = false;
-      if (k < sl.nvec) {
-        const float vm = Elem<T>::vmax(v[u]);
-        pass = (r.greedy ? vm : __fmul_rn(vm, r.invT)) >= theta;
-      }
-      const unsigned bal = __ballot_sync(~0u, pass);
-      if (bal) {
-        const int leader = __ffs(bal) - 1;
-        uint32_t base = 0;
-        if (lane == leader) base = atomicAdd(qcount, (uint32_t)__popc(bal));
-        base = __shfl_sync(~0u, base, leader);
-        if (pass) {
-          const uint32_t idx = base + (uint32_t)__popc(bal & ((1u << lane) - 1u));
-          if (idx < (uint32_t)qcap) queue[idx] = k;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  const uint32_t nq = *qcount;
-  auto scan = [&](int k) {
+  const uint32_t km = okey(m);
+  const uint32_t dhi = (uint32_t)(hi >> 32);
+  const float xlo = dhi >= km ? -INFINITY : okey_inv(km - dhi);  // keys <= hi have x >= xlo
+  const float tq = fmaxf(theta, xlo);
+  auto elem = [&](float x, uint32_t gid) {
+    if (!(x >= tq)) return;
+    const uint64_t ck = ckey(km, x, gid);
+    if (ck < lo || ck > hi) return;
+    const uint64_t w = weight_A(r, x, m);
+    if (w) fn(x, gid, w);
+  };
+  for (int k = threadIdx.x; k < sl.nvec; k += NT) {
     const uint4 v = load_masked<T>(sl, k);
+    const float vm = Elem<T>::vmax(v);
+    if (!((r.greedy ? vm : __fmul_rn(vm, r.invT)) >= tq)) continue;
     const uint32_t gid0 = (uint32_t)(sl.pos0_gid + (int64_t)k * VEC);
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
       const float raw = Elem<T>::get(v, j);
-      const float x = r.greedy ? raw : __fmul_rn(raw, r.invT);
-      if (x >= theta) {
-        const uint64_t w = weight_A(r, x, m);
-        if (w) fn(x, gid0 + (uint32_t)j, w);
-      }
-    }
-  };
-  if (nq <= (uint32_t)qcap) {
-    for (int i = threadIdx.x; i < (int)nq; i += NT) scan(queue[i]);
-  } else {
-    for (int k = threadIdx.x; k < sl.nvec; k += NT) {
-      const float vm = Elem<T>::vmax(load_masked<T>(sl, k));
-      if ((r.greedy ? vm : __fmul_rn(vm, r.invT)) >= theta) scan(k);
+      elem(r.greedy ? raw : __fmul_rn(raw, r.invT), gid0 + (uint32_t)j);
     }
   }
-  for (int i = threadIdx.x; i < nspec; i += NT) {
-    const Cand c = spec[i];
-    if (c.x >= theta) {
-      const uint64_t w = weight_A(r, c.x, m);
-      if (w) fn(c.x, c.gid, w);
-    }
-  }
+  for (int i = threadIdx.x; i < nspec; i += NT) elem(spec[i].x, spec[i].gid);
 }
 
 // ------------------------------------------------------------- fast tail
@@ -946,24 +924,27 @@ __device__ void tail_sort(int n, const TailScr &s, CtaSh &sh) {
   const uint64_t range = sh.kmax - kmin;
   const int bits = range ? 64 - __clzll((long long)range) : 0;
   const int bsh = bits > nbl ? bits - nbl : 0;
+  // bucket masses accumulate as split 32-bit words over the bm array's memory
+  uint32_t *mlo = reinterpret_cast<uint32_t *>(s.bm), *mhi = mlo + NBK;
   for (int i = t; i < n; i += NT) {
     const uint32_t b = (uint32_t)((s.K[i] - kmin) >> bsh);
     const uint32_t pos = atomicAdd(&s.bc[b], 1u);
-    atomicAdd((unsigned long long *)&s.bm[b], (unsigned long long)s.W[i]);
+    add_u64_split(&mlo[b], &mhi[b], s.W[i]);
     s.P[i] = (b << 16) | pos;
   }
   __syncthreads();
   {  // inclusive scans of counts and masses; NBK / NT buckets per thread
     constexpr int PER = NBK / NT;
     const int b0 = t * PER;
-    uint32_t c = 0;
-    uint64_t mm = 0;
+    uint32_t c = 0, cb[PER];
+    uint64_t mm = 0, mb[PER];
 #pragma unroll
-    for (int j = 0; j < PER; ++j)
-      if (b0 + j < NB) {
-        c += s.bc[b0 + j];
-        mm += s.bm[b0 + j];
-      }
+    for (int j = 0; j < PER; ++j) {
+      cb[j] = b0 + j < NB ? s.bc[b0 + j] : 0u;
+      mb[j] = b0 + j < NB ? get_u64_split(&mlo[b0 + j], &mhi[b0 + j]) : 0ull;
+      c += cb[j];
+      mm += mb[j];
+    }
     uint32_t ic = c;
     uint64_t im = mm;
     for (int o = 1; o < 32; o <<= 1) {
@@ -995,9 +976,9 @@ __device__ void tail_sort(int n, const TailScr &s, CtaSh &sh) {
     uint64_t om = (wid ? pm : 0ull) + im - mm;
 #pragma unroll
     for (int j = 0; j < PER; ++j)
-      if (b0 + j < NB) {
-        oc += s.bc[b0 + j];
-        om += s.bm[b0 + j];
+      if (b0 + j < NB) {  // every thread read its split words before the barrier above
+        oc += cb[j];
+        om += mb[j];
         s.bc[b0 + j] = oc;
         s.bm[b0 + j] = om;
       }
@@ -1371,10 +1352,11 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
           uint64_t *M = state == ST_AFTER_L1 ? L.l1m : L.refm;
           constexpr int PER = NBIN / NT;
           uint64_t lc[PER], lm[PER], sc = 0, sm = 0;
+          const uint32_t *Mlo = reinterpret_cast<const uint32_t *>(M), *Mhi = Mlo + NBIN;
 #pragma unroll
           for (int q = 0; q < PER; ++q) {
             lc[q] = C[tid * PER + q];
-            lm[q] = M[tid * PER + q];
+            lm[q] = get_u64_split(&Mlo[tid * PER + q], &Mhi[tid * PER + q]);
             sc += lc[q];
             sm += lm[q];
           }
@@ -1644,13 +1626,12 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
         }
         __syncthreads();
       }
-      for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount,
+      for_each_value<T>(sl, L.spec, nspec, r, m, theta, cmd.lo, cmd.hi,
                         [&](float x, uint32_t gid, uint64_t w) {
                           const uint64_t ck = ckey(km, x, gid);
-                          if (ck < cmd.lo || ck > cmd.hi) return;
                           const int b = (int)((ck - cmd.lo) >> cmd.shift);
                           atomicAdd(&hc[b], 1u);
-                          atomicAdd((unsigned long long *)&hm[b], (unsigned long long)w);
+                          add_u64_split(reinterpret_cast<uint32_t *>(hm) + b, reinterpret_cast<uint32_t *>(hm) + NBIN + b, w);
                         });
       if (rank != 0) {
         __syncthreads();
@@ -1659,17 +1640,17 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
         for (int b = tid; b < cmd.nbins; b += NT) {
           if (hc[b]) {
             atomicAdd(&rc[b], hc[b]);
-            atomicAdd((unsigned long long *)&rm[b], (unsigned long long)hm[b]);
+            const uint32_t *ml = reinterpret_cast<const uint32_t *>(hm);
+            add_u64_split(reinterpret_cast<uint32_t *>(rm) + b, reinterpret_cast<uint32_t *>(rm) + NBIN + b,
+                          get_u64_split(ml + b, ml + NBIN + b));
           }
         }
       }
     } else {  // OP_COMPACT into the CTA-local list
       if (tid == 0) sh.nloc = 0;
       __syncthreads();
-      for_each_value<T>(sl, L.spec, nspec, r, m, theta, L.gqueue, GQCAP, &sh.qcount,
-                        [&](float x, uint32_t gid, uint64_t w) {
-                          const uint64_t ck = ckey(km, x, gid);
-                          if (ck < cmd.lo || ck > cmd.hi) return;
+      for_each_value<T>(sl, L.spec, nspec, r, m, theta, cmd.lo, cmd.hi,
+                        [&](float x, uint32_t gid, uint64_t) {
                           const uint32_t idx = atomicAdd(&sh.nloc, 1u);
                           if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
                         });
@@ -2476,6 +2457,16 @@ static int max_smem_optin() {
   return v;
 }
 
+static int sm_count() {
+  static int v = -1;
+  if (v < 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) v = 148;
+  }
+  return v;
+}
+
 static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Plan &pl) {
   const int es = p->dtype == MSTAR_DTYPE_BF16 ? 2 : 4;
   const int spec_max = (p->hist_ids ? p->H : (p->seen_bits ? (p->seen_cap > 0 ? p->seen_cap : 2048) : 0)) +
@@ -2515,10 +2506,19 @@ static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Pl
     if (!need(p->cluster_size, pl)) return fail(MSTAR_ERR_UNSUPPORTED, "row does not fit the requested cluster size");
     return MSTAR_OK;
   }
-  for (int s = 1; s <= 16; ++s) {
+  // the smallest cluster the row fits, widened while the grid leaves SMs
+  // idle (small batches: each row's slice is then streamed by more SMs),
+  // up to the portable cluster size and keeping slices >= 8192 elements
+  int smin = 0;
+  for (int s = 1; s <= 16 && !smin; ++s)
+    if (need(s, pl)) smin = s;
+  if (!smin) return fail(MSTAR_ERR_UNSUPPORTED, "row too large for a 16-CTA cluster");
+  int target = std::min(8, std::max(1, sm_count() / std::max(1, p->B)));
+  target = (int)std::min<int64_t>(target, std::max<int64_t>(1, p->V / 8192));
+  for (int s = std::max(smin, target); s > smin; --s)
     if (need(s, pl)) return MSTAR_OK;
-  }
-  return fail(MSTAR_ERR_UNSUPPORTED, "row too large for a 16-CTA cluster");
+  need(smin, pl);
+  return MSTAR_OK;
 }
 
 template <typename T, int MODE>
