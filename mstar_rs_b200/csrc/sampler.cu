@@ -216,14 +216,6 @@ __device__ __forceinline__ uint32_t warp_reserve(uint32_t *counter, uint32_t cnt
   return __shfl_sync(~0u, base, 31) + inc - cnt;
 }
 
-// 4-byte asynchronous global -> shared copy (completes at cp_async_wait_all
-// of the issuing thread).
-__device__ __forceinline__ void cp_async4(void *dst, uintptr_t src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
 // 64-bit sums in shared (or cluster shared) memory kept as two 32-bit words
 // lo[i], hi[i]: 32-bit atomics are native, 64-bit atomic adds are
 // compare-and-swap loops that serialise badly under contention.
@@ -238,16 +230,6 @@ __device__ __forceinline__ void add_u64_split(uint32_t *lo, uint32_t *hi, uint64
 }
 __device__ __forceinline__ uint64_t get_u64_split(const uint32_t *lo, const uint32_t *hi) {
   return ((uint64_t)*hi << 32) | *lo;
-}
-
-// Whether the aligned 32-bit word holding element e of a row of V elements
-// lies inside the row (a 2-byte element at a word boundary as the row's last
-// element would pull in 2 bytes past it).
-template <typename T>
-__device__ __forceinline__ bool word_in_row(const uint8_t *rowp, int64_t e, int64_t V) {
-  if (sizeof(T) == 4) return true;
-  const uintptr_t a = reinterpret_cast<uintptr_t>(rowp + e * 2);
-  return (a & 2u) != 0 || e + 1 < V;
 }
 
 // Split cluster barrier: a CTA may touch a peer's shared memory only once
@@ -341,8 +323,6 @@ struct Elem<float> {
   static __device__ __forceinline__ float smem_elem(const uint8_t *data, int64_t pos) {
     return reinterpret_cast<const float *>(data)[pos];
   }
-  // element e of the row from the aligned 32-bit word that holds it
-  static __device__ __forceinline__ float from_word(uint32_t w, const uint8_t *, int64_t) { return __uint_as_float(w); }
 };
 
 template <>
@@ -409,11 +389,6 @@ struct Elem<__nv_bfloat16> {
   }
   static __device__ __forceinline__ float smem_elem(const uint8_t *data, int64_t pos) {
     return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(data)[pos] << 16);
-  }
-  // element e of the row from the aligned 32-bit word that holds it
-  static __device__ __forceinline__ float from_word(uint32_t w, const uint8_t *rowp, int64_t e) {
-    const bool hi = (reinterpret_cast<uintptr_t>(rowp + e * 2) & 2u) != 0;
-    return __uint_as_float(hi ? (w & 0xFFFF0000u) : (w << 16));
   }
 };
 
@@ -1010,6 +985,39 @@ __device__ void tail_sort(int n, const TailScr &s, CtaSh &sh) {
   for (int i = t; i < n; i += NT) {  // keys and weights into rank order
     s.RK[s.P[i]] = s.K[i];
     s.RW[s.P[i]] = s.W[i];
+  }
+  __syncthreads();
+}
+
+// Sort of a small gathered set (n <= RANK_MAX, distinct keys) by pairwise
+// counting: G = NT / slots threads per candidate each compare it with every
+// G-th key (interleaved, conflict-free reads) and sum the counts and the
+// weights of the smaller keys, which give its rank and its exclusive weight
+// prefix in one pass.  Same outputs as tail_sort (RK / RW / RS in rank
+// order).  Block-wide; ends with a barrier.
+constexpr int RANK_MAX = 128;
+__device__ void tail_rank_sort(int n, const TailScr &s) {
+  const int t = threadIdx.x;
+  const int G = n <= 64 ? NT / 64 : NT / 128;
+  const int e = t / G, part = t % G;
+  const uint64_t key = e < n ? s.K[e] : ~0ull;
+  uint32_t c = 0;
+  uint64_t before = 0;
+  for (int j = part; j < n; j += G) {
+    const uint64_t kj = s.K[j];
+    if (kj < key) {
+      ++c;
+      before += s.W[j];
+    }
+  }
+  for (int o = G >> 1; o; o >>= 1) {
+    c += __shfl_xor_sync(~0u, c, o);
+    before += (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)before, o);
+  }
+  if (part == 0 && e < n) {
+    s.RK[c] = key;
+    s.RW[c] = s.W[e];
+    s.RS[c] = before;
   }
   __syncthreads();
 }
@@ -1861,41 +1869,51 @@ __global__ void __launch_bounds__(NT, 1)
     }
   }
   __syncthreads();  // skip words written, table cleared
-  if (has_spec) {
-    // specials: history / seen bits / bias ids that fall in [c0, c1).  The
-    // thread that creates a table entry sets the position's skip bit and
-    // records whether it was already set (a disallowed position).
-    // The creator also takes the special's list entry and starts an
-    // asynchronous copy of the 32-bit word holding its logit into it, so
-    // the special can be finalized before the chunk holding it lands.
-    uint32_t *spec32 = reinterpret_cast<uint32_t *>(L.spec);
-    auto add_special = [&](int64_t e, int cnt) {
-      int h;
-      const int created = ht_insert(L.ht, pl.ht_cap, (int)e, cnt, h);
-      if (created < 0) {
-        sh.ht_fail = 1;
-      } else if (created) {
+  // Specials: history / seen bits / bias ids that fall in [c0, c1).  Each
+  // gets a skip bit (the first pass leaves it out), a hash-table entry (its
+  // count and flags) and a list entry; its final value is computed from the
+  // resident data after the last chunk.
+  //  - With an allowed mask the thread that creates a table entry sets the
+  //    position's skip bit and learns from the old bit whether the position
+  //    was disallowed; the table is complete before the first pass.
+  //  - Without one only the skip bits are set before the first pass (plain
+  //    ORs); the table is built after the first chunk, while later chunks
+  //    are still landing.
+  const bool mark_first = has_spec && !p.allowed_bits;
+  uint32_t *spec32 = reinterpret_cast<uint32_t *>(L.spec);
+  auto new_entry = [&](int h) {  // list entry of a created table entry
+    cg::coalesced_group g = cg::coalesced_threads();
+    uint32_t cb = 0;
+    if (g.thread_rank() == 0) cb = atomicAdd(&sh.n_spec, (uint32_t)g.size());
+    const uint32_t ci = g.shfl(cb, 0) + g.thread_rank();
+    if ((int)ci < pl.spec_cap) spec32[2 * ci] = (uint32_t)h;
+    else sh.ht_fail = 1;
+  };
+  auto add_special = [&](int64_t e, int cnt) {
+    int h;
+    const int created = ht_insert(L.ht, pl.ht_cap, (int)e, cnt, h);
+    if (created < 0) {
+      sh.ht_fail = 1;
+    } else if (created) {
+      if (!mark_first) {
         const int64_t pos = e - c0al;
         const uint32_t bit = 1u << (pos & 31);
         if (atomicOr(&skip32[pos >> 5], bit) & bit) atomicOr(&L.ht[h].y, HT_MASKED);
-        cg::coalesced_group g = cg::coalesced_threads();
-        uint32_t cb = 0;
-        if (g.thread_rank() == 0) cb = atomicAdd(&sh.n_spec, (uint32_t)g.size());
-        const uint32_t ci = g.shfl(cb, 0) + g.thread_rank();
-        if ((int)ci < pl.spec_cap) {
-          spec32[2 * ci] = (uint32_t)h;
-          if (word_in_row<T>(rowp, e, p.V))
-            cp_async4(&spec32[2 * ci + 1], reinterpret_cast<uintptr_t>(rowp + e * es) & ~(uintptr_t)3);
-        } else {
-          sh.ht_fail = 1;
-        }
       }
-    };
+      new_entry(h);
+    }
+  };
+  auto mark_special = [&](int64_t e, int) {
+    const int64_t pos = e - c0al;
+    atomicOr(&skip32[pos >> 5], 1u << (pos & 31));
+  };
+  // fn(e, count) for every special occurrence of this slice (e = position in the row)
+  auto for_each_special = [&](auto &&fn) {
     if (has_hist) {
       const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
       for (int j = tid, u = 0; j < hlen; j += NT, ++u) {
         const int64_t g = (int64_t)(u < HP ? (u == 0 ? hpre[0] : hpre[1]) : h[j]) - gbase;
-        if (g >= c0 && g < c1) add_special(g, 1);
+        if (g >= c0 && g < c1) fn(g, 1);
       }
     } else if (p.seen_bits) {
       const uint32_t *sw = p.seen_bits + (int64_t)slot * p.seen_words;
@@ -1907,7 +1925,7 @@ __global__ void __launch_bounds__(NT, 1)
             const int b = __ffs(bits) - 1;
             bits &= bits - 1;
             const int64_t g = (w << 5) + b;
-            if (g >= g0 && g < g1) add_special(g - gbase, 1);
+            if (g >= g0 && g < g1) fn(g - gbase, 1);
           }
         }
       }
@@ -1918,10 +1936,15 @@ __global__ void __launch_bounds__(NT, 1)
         const int32_t g = bi[j];
         if (g < 0) continue;
         const int64_t e = (int64_t)g - gbase;
-        if (e >= c0 && e < c1) add_special(e, 0);
+        if (e >= c0 && e < c1) fn(e, 0);
       }
     }
-    cp_async_commit();
+  };
+  if (mark_first) {
+    for_each_special(mark_special);
+    __syncthreads();  // skip bits of the specials in
+  } else if (has_spec) {
+    for_each_special(add_special);
     __syncthreads();  // bitmap, table and special list entries complete
   }
   const Row r = sh.row;
@@ -1932,7 +1955,7 @@ __global__ void __launch_bounds__(NT, 1)
   // per-warp queue of the vectors whose max reaches the running threshold
   // thr(M) = M - |M| 2^-10 + lq T (1 + 2^-10) (M a raw max seen so far, lq
   // the lowest offset below the CTA max that this CTA's value threshold can
-  // take); the specials of each block as soon as its values are resident.
+  // take); then the specials' final values.
   float lq = 0.0f;
   if (!one) {
     lq = -33.0f;
@@ -1966,20 +1989,17 @@ __global__ void __launch_bounds__(NT, 1)
     }
     float cmx = -INFINITY;
     for (int base = kb; base < ke; base += PU * NT) {
-      float v[PU];
+      Acc a[PU];
 #pragma unroll
       for (int u = 0; u < PU; ++u) {
         const int k = base + u * NT + tid;
-        v[u] = -INFINITY;
-        if (k < ke) {
-          const Acc a = Elem<T>::vred(load_masked<T>(sl, k));
-          racc = Elem<T>::acc_max(racc, a);
-          v[u] = Elem<T>::acc_f(a);
-        }
+        a[u] = k < ke ? Elem<T>::vred(load_masked<T>(sl, k)) : Elem<T>::acc_init();
       }
-      float vm = v[0];
+      Acc at = a[0];
 #pragma unroll
-      for (int u = 1; u < PU; ++u) vm = fmaxf(vm, v[u]);
+      for (int u = 1; u < PU; ++u) at = Elem<T>::acc_max(at, a[u]);
+      racc = Elem<T>::acc_max(racc, at);
+      const float vm = Elem<T>::acc_f(at);
       if (boot) {  // first trip: the CTA max over it sets the threshold
         float w = vm;
         for (int o = 16; o; o >>= 1) w = fmaxf(w, __shfl_xor_sync(~0u, w, o));
@@ -1990,23 +2010,23 @@ __global__ void __launch_bounds__(NT, 1)
         boot = false;
       }
       cmx = fmaxf(cmx, vm);
+      // one vote per trip; the per-vector queue appends only when a lane passes
+      if (__any_sync(~0u, vm > -INFINITY && vm >= th)) {
 #pragma unroll
-      for (int u = 0; u < PU; ++u) enqueue(v[u] > -INFINITY && v[u] >= th, base + u * NT + tid);
+        for (int u = 0; u < PU; ++u) {
+          const float vu = Elem<T>::acc_f(a[u]);
+          enqueue(vu > -INFINITY && vu >= th, base + u * NT + tid);
+        }
+      }
     }
     if (cmx > runM) atomicMax(&sh.runmax, okey(cmx));
   };
-  // specials: bias (list order) -> penalties -> mask -> transform, for the
-  // table entries whose vector lies in [kb, ke); SB slots per thread at a
-  // time, appended with one atomic per warp (none when the warp has none)
   const float penR = r.R, penF = r.F, penP = r.Pp;
-  // Specials: bias (list order) -> penalties -> mask -> transform.  Their
-  // logits were fetched by asynchronous copies started when the table was
-  // built, so this runs after the first block without waiting for the
-  // chunks that hold them.  Entry i of the list holds (table slot, logit
-  // word) and becomes (x, id) in place.
+  // Specials: bias (list order) -> penalties -> mask -> transform, after the
+  // last block, from the resident data.  Entry i of the list holds its table
+  // slot and becomes (x, id) in place.
   auto finalize = [&]() {
-    cp_async_wait_all();
-    __syncthreads();  // every thread's copies have landed
+    __syncthreads();  // table complete; every chunk landed (each thread waited on all)
     const bool bias_smem = p.bias_ids && p.NB <= BIAS_SMEM;
     const int32_t *bi = p.bias_ids ? p.bias_ids + (int64_t)slot * p.NB : nullptr;
     const float *bv = p.bias_vals ? p.bias_vals + (int64_t)slot * p.NB : nullptr;
@@ -2015,8 +2035,7 @@ __global__ void __launch_bounds__(NT, 1)
     for (int i = tid; i < n; i += NT) {
       const int2 ent = L.ht[spec32[2 * i]];
       const int cnt = ent.y & ~HT_MASKED;
-      float v = word_in_row<T>(rowp, ent.x, p.V) ? Elem<T>::from_word(spec32[2 * i + 1], rowp, ent.x)
-                                                  : Elem<T>::load(rowp, ent.x);
+      float v = Elem<T>::smem_elem(L.data, ent.x - c0al);
       if (bi) {
         const int32_t gid = (int32_t)(ent.x + gbase);
         for (int j = 0; j < p.NB; ++j) {
@@ -2057,10 +2076,11 @@ __global__ void __launch_bounds__(NT, 1)
         kb = hv + j * CV;
         ke = hv + min(nbv, (j + 1) * CV);
       }
+      if (mark_first && bi == 1) for_each_special(add_special);  // the table, after the first chunk
       process(kb, ke);
-      if (has_spec && bi == 2) finalize();
     }
   }
+  if (has_spec) finalize();
   if (timed_out) atomicOr(&sh.status, MSTAR_STATUS_TIMEOUT);
   if (lane == 0) sh.wqn[tid >> 5] = wq;
   {
@@ -2238,7 +2258,7 @@ __global__ void __launch_bounds__(NT, 1)
         const Cand *lists = L.lcand;
         const uint32_t *lcnt = sh.gcnt, *loff = sh.goff;
         int nl = S, stride = capq, n = (int)sh.ncand;
-        if (r.topk && r.K < n && n > 64) {
+        if (r.topk && r.K < n && n > RANK_MAX) {
           tail_topk_prefilter(r, km, S, sh.gcnt, sh.goff, L.lcand, capq, n, ts, sh);
           lists = reinterpret_cast<const Cand *>(ts.RS);
           lcnt = &sh.pf_n;
@@ -2247,27 +2267,23 @@ __global__ void __launch_bounds__(NT, 1)
           stride = 0;
           n = (int)sh.pf_n;
         }
-        if (n <= 64) {  // one warp, in registers
-          if (tid < 32) {
-            if (n <= 32)
-              tail_warp<1>(r, m, km, MODE == 0 ? sh.u : 0.0f, nl, lcnt, loff, lists, stride, n, MODE, pl.tp_cap,
-                           rec, sh);
-            else
-              tail_warp<2>(r, m, km, MODE == 0 ? sh.u : 0.0f, nl, lcnt, loff, lists, stride, n, MODE, pl.tp_cap,
-                           rec, sh);
-          }
+        uint64_t kmn = ~0ull, kmx = 0ull;
+        uint32_t np = 0;
+        for (int q = 0; q < nl; ++q) {
+          const int cq = (int)min(lcnt[q], (uint32_t)(nl == 1 ? n : capq)), o = (int)loff[q];
+          for (int i = tid; i < cq; i += NT) tail_put(r, m, km, lists[q * stride + i], o + i, ts, kmn, kmx, np);
+        }
+        if (n <= RANK_MAX) {
+          np = __reduce_add_sync(~0u, np);
+          if (lane == 0 && np) atomicAdd(&sh.npass, np);
+          __syncthreads();  // keys, weights and the pass count complete
+          tail_rank_sort(n, ts);
         } else {
-          uint64_t kmn = ~0ull, kmx = 0ull;
-          uint32_t np = 0;
-          for (int q = 0; q < nl; ++q) {
-            const int cq = (int)min(lcnt[q], (uint32_t)(nl == 1 ? n : capq)), o = (int)loff[q];
-            for (int i = tid; i < cq; i += NT) tail_put(r, m, km, lists[q * stride + i], o + i, ts, kmn, kmx, np);
-          }
           tail_gather_end(kmn, kmx, np, ts, sh);
           tail_sort(n, ts, sh);
-          if (MODE == 0) tail_resolve(r, sh.u, ts, sh);
-          else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
         }
+        if (MODE == 0) tail_resolve(r, sh.u, ts, sh);
+        else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
       }
     }
   } else {
