@@ -68,10 +68,11 @@ constexpr int BIAS_SMEM = 256;      // bias entries staged in shared memory
 constexpr int QCAP = 2048;          // vectors queued by the first pass (all warps)
 constexpr int WQCAP = QCAP / (NT / 32);  // per-warp share of the queue
 constexpr int PU = 4;                    // vectors per thread per trip of the first pass
-constexpr int GQCAP = 1024;         // vectors queued per general-path round
-constexpr int GEN_BYTES = 12288 + 14336 + GCAP * 8 + GQCAP * 4;  // L1 | REF/sort | sort input | queue
-static_assert(NBIN * 12 <= 12288, "L1 / REF histograms");
-static_assert(GCAP * 20 + GBK * 8 <= 14336, "general sort scratch");
+constexpr int HIST_BYTES = NBIN * 16;  // per histogram: counts + three 11-bit mass parts
+constexpr int GEN_BYTES = 2 * HIST_BYTES + GCAP * 8;  // L1 | REF (aliased by the sort scratch) | sort input
+static_assert(NBIN * 8 <= NBIN * 12, "64-bit mass prefixes fit over the part arrays");
+static_assert(GCAP * 20 + GBK * 8 <= HIST_BYTES, "general sort scratch");
+static_assert((NT / 32) * 256 * 4 <= HIST_BYTES && (NT / 32) * 256 <= LCAP * 2, "general-path warp lists");
 static_assert(GBK <= NT && NBIN % NT == 0 && NBK % NT == 0 && TAIL_CAP % NT == 0, "per-thread splits");
 constexpr int WORK_BYTES_MIN = GEN_BYTES;
 constexpr int LEAN_SCRATCH = 112 * 1024;  // fast-tail scratch (the leader's data region)
@@ -585,38 +586,92 @@ __device__ __forceinline__ uint4 load_masked(const Slice &sl, int k) {
 }
 
 // Iterate the value-A elements this CTA holds whose order key lies in
-// [lo, hi] (resident vectors and the special list); fn(x, gid, w).  A vector
-// is skipped after one compare when its max is below both theta and the
-// smallest value the key range admits; keys are tested before the weight is
-// computed, so a narrow range costs little more than the vector scan.
-// Block-wide (no barrier inside).
-template <typename T, typename F>
+// [lo, hi] (resident vectors and the special list), calling
+// fn(x, gid, w, valid) with all 32 lanes of each warp, valid = the lane holds
+// such an element (w its weight, > 0).  Each warp alternates a compact scan,
+// which lists the vectors that may hold an element in range (their max
+// reaches the range; unless DENSE, also one element inside its value
+// bounds) in its own list (wq, QW entries), and an evaluation of the listed
+// vectors 32 at a time, each lane evaluating its vector's elements together
+// without branches so their exponentials overlap.  Keeping the two loops
+// apart keeps the scan loop small.  Block-wide, warp-synchronous; no barrier.
+constexpr int QW = 256;  // per-warp list entries (vector indices)
+template <typename T, bool DENSE, typename F>
 __device__ __forceinline__ void for_each_value(const Slice &sl, const Cand *spec, int nspec, const Row &r, float m,
-                                               float theta, uint64_t lo, uint64_t hi, F &&fn) {
+                                               float theta, uint64_t lo, uint64_t hi, int *wq, F &&fn) {
   constexpr int VEC = Elem<T>::VEC;
+  constexpr int SU = 4;  // vectors per lane per scan trip (independent loads in flight)
+  const int lane = threadIdx.x & 31;
   const uint32_t km = okey(m);
   const uint32_t dhi = (uint32_t)(hi >> 32);
   const float xlo = dhi >= km ? -INFINITY : okey_inv(km - dhi);  // keys <= hi have x >= xlo
   const float tq = fmaxf(theta, xlo);
-  auto elem = [&](float x, uint32_t gid) {
-    if (!(x >= tq)) return;
+  const uint32_t dlo = (uint32_t)(lo >> 32);
+  const float xhi = dlo == 0 ? INFINITY : okey_inv(km - dlo);  // keys >= lo have x <= xhi
+  auto in_range = [&](float x, uint32_t gid) {
+    if (!(x >= tq && x <= xhi)) return false;
     const uint64_t ck = ckey(km, x, gid);
-    if (ck < lo || ck > hi) return;
-    const uint64_t w = weight_A(r, x, m);
-    if (w) fn(x, gid, w);
+    return ck >= lo && ck <= hi;
   };
-  for (int k = threadIdx.x; k < sl.nvec; k += NT) {
-    const uint4 v = load_masked<T>(sl, k);
-    const float vm = Elem<T>::vmax(v);
-    if (!((r.greedy ? vm : __fmul_rn(vm, r.invT)) >= tq)) continue;
-    const uint32_t gid0 = (uint32_t)(sl.pos0_gid + (int64_t)k * VEC);
+  int kb = threadIdx.x & ~31;
+  while (kb < sl.nvec) {  // warp-uniform
+    int qn = 0;
+    for (; kb < sl.nvec && qn <= QW - SU * 32; kb += SU * NT) {
+      bool pv[SU];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      const float raw = Elem<T>::get(v, j);
-      elem(r.greedy ? raw : __fmul_rn(raw, r.invT), gid0 + (uint32_t)j);
+      for (int u = 0; u < SU; ++u) {
+        const int k = kb + u * NT + lane;
+        pv[u] = false;
+        if (k < sl.nvec) {
+          const uint4 v = load_masked<T>(sl, k);
+          if (DENSE) {
+            const float vm = Elem<T>::vmax(v);
+            pv[u] = (r.greedy ? vm : __fmul_rn(vm, r.invT)) >= tq;
+          } else {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) {
+              const float raw = Elem<T>::get(v, j);
+              const float x = r.greedy ? raw : __fmul_rn(raw, r.invT);
+              pv[u] |= x >= tq && x <= xhi;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < SU; ++u) {
+        const unsigned bal = __ballot_sync(~0u, pv[u]);
+        if (pv[u]) wq[qn + __popc(bal & ((1u << lane) - 1u))] = kb + u * NT + lane;
+        qn += __popc(bal);
+      }
     }
+    __syncwarp();
+    for (int i = 0; i < qn; i += 32) {
+      const bool have = i + lane < qn;
+      const int k = have ? wq[i + lane] : 0;
+      const uint4 v = have ? load_masked<T>(sl, k) : make_uint4(0, 0, 0, 0);
+      const uint32_t gid0 = (uint32_t)(sl.pos0_gid + (int64_t)k * VEC);
+      float x[VEC];
+      uint64_t w[VEC];
+      bool in[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float raw = Elem<T>::get(v, j);
+        x[j] = r.greedy ? raw : __fmul_rn(raw, r.invT);
+        in[j] = have && in_range(x[j], gid0 + (uint32_t)j);
+        w[j] = weight_A(r, x[j], m);
+      }
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) fn(x[j], gid0 + (uint32_t)j, w[j], in[j] && w[j] != 0);
+    }
+    __syncwarp();
   }
-  for (int i = threadIdx.x; i < nspec; i += NT) elem(spec[i].x, spec[i].gid);
+  for (int ib = threadIdx.x & ~31; ib < nspec; ib += NT) {
+    const int i = ib + lane;
+    const Cand c = i < nspec ? spec[i] : Cand{-INFINITY, 0u};
+    const bool in = i < nspec && in_range(c.x, c.gid);
+    const uint64_t w = weight_A(r, c.x, m);
+    fn(c.x, c.gid, w, in && w != 0);
+  }
 }
 
 // ------------------------------------------------------------- fast tail
@@ -709,12 +764,14 @@ struct Layout {
   int32_t *bias_id;
   float *bias_val;
   uint8_t *work;
-  uint32_t *l1c;
+  // general-path histograms: counts, then the masses as three 11-bit parts
+  // (REDs only; part sums stay below 2^32 for rows of up to 2^21 ids), which
+  // the planner turns into 64-bit inclusive prefixes stored over the parts
+  uint32_t *l1c, *l1p;
   uint64_t *l1m;
-  uint32_t *refc;
+  uint32_t *refc, *refp;
   uint64_t *refm;
   SortScratch gsort;
-  int *gqueue;
 };
 
 __device__ __forceinline__ Layout make_layout(uint8_t *smem, const Plan &pl) {
@@ -732,16 +789,18 @@ __device__ __forceinline__ Layout make_layout(uint8_t *smem, const Plan &pl) {
   // over the hash table and the first scan's queue, dead by then
   uint8_t *g = L.work + pl.map_bytes;
   L.l1c = reinterpret_cast<uint32_t *>(g);
-  L.l1m = reinterpret_cast<uint64_t *>(g + 4096);
-  L.refc = reinterpret_cast<uint32_t *>(g + 12288);  // NBIN counts + NBIN masses
-  L.refm = reinterpret_cast<uint64_t *>(g + 16384);
-  L.gsort.mid = reinterpret_cast<Cand *>(g + 12288);  // aliases REF (14 KB)
-  L.gsort.tmp = reinterpret_cast<uint32_t *>(g + 12288 + GCAP * 8);
-  L.gsort.S = reinterpret_cast<uint64_t *>(g + 12288 + GCAP * 12);
-  L.gsort.bcnt = reinterpret_cast<uint32_t *>(g + 12288 + GCAP * 20);
-  L.gsort.boff = reinterpret_cast<uint32_t *>(g + 12288 + GCAP * 20 + GBK * 4);
-  L.gsort.in = reinterpret_cast<Cand *>(g + 12288 + 14336);
-  L.gqueue = reinterpret_cast<int *>(g + 12288 + 14336 + GCAP * 8);  // general-path scan queue
+  L.l1p = reinterpret_cast<uint32_t *>(g + NBIN * 4);
+  L.l1m = reinterpret_cast<uint64_t *>(g + NBIN * 4);
+  uint8_t *gr = g + HIST_BYTES;
+  L.refc = reinterpret_cast<uint32_t *>(gr);
+  L.refp = reinterpret_cast<uint32_t *>(gr + NBIN * 4);
+  L.refm = reinterpret_cast<uint64_t *>(gr + NBIN * 4);
+  L.gsort.mid = reinterpret_cast<Cand *>(gr);  // aliases REF
+  L.gsort.tmp = reinterpret_cast<uint32_t *>(gr + GCAP * 8);
+  L.gsort.S = reinterpret_cast<uint64_t *>(gr + GCAP * 12);
+  L.gsort.bcnt = reinterpret_cast<uint32_t *>(gr + GCAP * 20);
+  L.gsort.boff = reinterpret_cast<uint32_t *>(gr + GCAP * 20 + GBK * 4);
+  L.gsort.in = reinterpret_cast<Cand *>(g + 2 * HIST_BYTES);
   return L;
 }
 
@@ -1059,6 +1118,37 @@ __device__ void tail_resolve(const Row &r, float u, const TailScr &s, CtaSh &sh)
   __syncthreads();
 }
 
+// tail_resolve for at most RANK_MAX rank-ordered candidates, by one full
+// warp with ballots and reductions (no block barrier).
+__device__ void tail_resolve_warp(const Row &r, float u, const TailScr &s, CtaSh &sh) {
+  const int lane = threadIdx.x & 31;
+  const int np = (int)sh.npass;
+  const int nA = r.topk ? min(np, r.K) : np;
+  if (nA <= 0) {  // no candidate carries weight: the leading one stands
+    if (lane == 0) {
+      sh.res.token = (uint32_t)(s.RK[0] & 0xFFFFFFFFu);
+      sh.res.WK = 0;
+      sh.res.ckK = s.RK[0];
+    }
+    return;
+  }
+  int nK = nA;
+  if (r.topp) {  // kept ranks: j == 0 or S_j < P * W_A (a prefix)
+    const double thr = __dmul_rn((double)r.P, (double)(s.RS[nA - 1] + s.RW[nA - 1]));
+    uint32_t c = 0;
+    for (int j = lane; j < nA; j += 32) c += (double)s.RS[j] < thr;
+    nK = max((int)__reduce_add_sync(~0u, c), 1);
+  }
+  const uint64_t WK = s.RS[nK - 1] + s.RW[nK - 1];
+  const uint64_t rr = draw_point(u, WK);
+  for (int j = lane; j < nK; j += 32)
+    if (s.RS[j] <= rr && rr < s.RS[j] + s.RW[j]) sh.res.token = (uint32_t)(s.RK[j] & 0xFFFFFFFFu);
+  if (lane == 0) {
+    sh.res.WK = WK;
+    sh.res.ckK = s.RK[nK - 1];
+  }
+}
+
 // TP shard record: the A set in order (top_k-limited) as (x bits, id)
 // pairs.  Block-wide; ends with a barrier.
 __device__ void tail_emit(const Row &r, uint32_t km, int tp_cap, uint32_t *rec, const TailScr &s, CtaSh &sh) {
@@ -1156,136 +1246,6 @@ __device__ void tail_topk_prefilter(const Row &r, uint32_t km, int S, const uint
   __syncthreads();
 }
 
-// The whole tail on one warp, for at most 32 * E candidates (E = 1 or 2 per
-// lane, in registers: element i is slot i / 32 of lane i % 32): keys and
-// weights, a bitonic sort of each slot across the lanes and, for E = 2, a
-// bitonic merge of the two slots; prefix sums with shuffles; then the
-// queries (step) or the record (TP shard).  The candidate lists are those of
-// the fast path (list q at lists + q * stride, cnt[q] entries placed at
-// off[q]).  The two slots are named variables: indexed register arrays in
-// these unrolled loops compiled to far slower code.
-__device__ __forceinline__ void cas_lanes(uint64_t &key, uint64_t &w, int j, bool keep_min) {
-  const uint64_t ok = __shfl_xor_sync(~0u, (unsigned long long)key, j);
-  const uint64_t ow = __shfl_xor_sync(~0u, (unsigned long long)w, j);
-  const bool take = keep_min ? (ok < key) : (ok > key);
-  key = take ? ok : key;
-  w = take ? ow : w;
-}
-
-__device__ __forceinline__ void tail_warp_load(const Row &r, float m, uint32_t km, int S, const uint32_t *cnt,
-                                               const uint32_t *off, const Cand *lists, int stride, int n, int i,
-                                               uint64_t &key, uint64_t &w) {
-  key = ~0ull;
-  w = 0ull;
-  if (i >= n) return;
-  for (int q = 0; q < S; ++q) {
-    const int o = (int)off[q];
-    if (i >= o && i < o + (int)cnt[q]) {
-      const Cand cd = lists[q * stride + (i - o)];
-      key = ckey(km, cd.x, cd.gid);
-      w = weight_A(r, cd.x, m);
-    }
-  }
-}
-
-template <int E>
-__device__ void tail_warp(const Row &r, float m, uint32_t km, float u, int S, const uint32_t *cnt,
-                          const uint32_t *off, const Cand *lists, int stride, int n, int mode, int tp_cap,
-                          uint32_t *rec, CtaSh &sh) {
-  static_assert(E == 1 || E == 2, "one or two candidates per lane");
-  const int lane = threadIdx.x & 31;
-  uint64_t k0, w0, k1 = ~0ull, w1 = 0ull;
-  tail_warp_load(r, m, km, S, cnt, off, lists, stride, n, lane, k0, w0);
-  if (E == 2) tail_warp_load(r, m, km, S, cnt, off, lists, stride, n, 32 + lane, k1, w1);
-#pragma unroll
-  for (int k = 2; k <= 32; k <<= 1) {  // each slot ascending across the lanes
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      const bool keep_min = ((lane & k) == 0) == ((lane & j) == 0);
-      cas_lanes(k0, w0, j, keep_min);
-      if (E == 2) cas_lanes(k1, w1, j, keep_min);
-    }
-  }
-  if (E == 2) {  // merge: slot 1 reversed, half-cleaner across the slots, then clean each slot
-    const uint64_t rk = __shfl_sync(~0u, (unsigned long long)k1, 31 - lane);
-    const uint64_t rw = __shfl_sync(~0u, (unsigned long long)w1, 31 - lane);
-    const bool lo = k0 < rk;
-    k1 = lo ? rk : k0;
-    w1 = lo ? rw : w0;
-    k0 = lo ? k0 : rk;
-    w0 = lo ? w0 : rw;
-#pragma unroll
-    for (int j = 16; j > 0; j >>= 1) {
-      const bool keep_min = (lane & j) == 0;
-      cas_lanes(k0, w0, j, keep_min);
-      cas_lanes(k1, w1, j, keep_min);
-    }
-  }
-  // weight-0 candidates fail the predicate and sort behind every passing one
-  const int np = __popc(__ballot_sync(~0u, w0 != 0ull)) + (E == 2 ? __popc(__ballot_sync(~0u, w1 != 0ull)) : 0);
-  uint64_t i0 = w0, i1 = w1;
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint64_t t0 = __shfl_up_sync(~0u, (unsigned long long)i0, o);
-    const uint64_t t1 = E == 2 ? (uint64_t)__shfl_up_sync(~0u, (unsigned long long)i1, o) : 0ull;
-    if (lane >= o) {
-      i0 += t0;
-      i1 += t1;
-    }
-  }
-  if (E == 2) i1 += __shfl_sync(~0u, (unsigned long long)i0, 31);
-  const uint64_t e0 = i0 - w0, e1 = i1 - w1;  // exclusive prefixes
-  const int nA = r.topk ? min(np, r.K) : np;
-  if (mode == 1) {
-    if (nA <= tp_cap) {
-      if (lane < nA) {
-        rec[4 + 2 * lane] = __float_as_uint(okey_inv(km - (uint32_t)(k0 >> 32)));
-        rec[5 + 2 * lane] = (uint32_t)(k0 & 0xFFFFFFFFu);
-      }
-      if (E == 2 && 32 + lane < nA) {
-        rec[4 + 2 * (32 + lane)] = __float_as_uint(okey_inv(km - (uint32_t)(k1 >> 32)));
-        rec[5 + 2 * (32 + lane)] = (uint32_t)(k1 & 0xFFFFFFFFu);
-      }
-    }
-    if (lane == 0) sh.nemit = nA;
-    return;
-  }
-  if (nA <= 0) {  // no candidate carries weight: the leading one stands
-    const uint64_t kl = __shfl_sync(~0u, (unsigned long long)k0, 0);
-    if (lane == 0) {
-      sh.res.token = (uint32_t)(kl & 0xFFFFFFFFu);
-      sh.res.WK = 0;
-      sh.res.ckK = kl;
-    }
-    return;
-  }
-  // element i's inclusive prefix / key, gathered from its lane
-  auto inc_at = [&](int i) -> uint64_t {
-    const uint64_t v = __shfl_sync(~0u, (unsigned long long)(i >= 32 ? i1 : i0), i & 31);
-    return v;
-  };
-  auto key_at = [&](int i) -> uint64_t {
-    return __shfl_sync(~0u, (unsigned long long)(i >= 32 ? k1 : k0), i & 31);
-  };
-  int nK = nA;
-  if (r.topp) {  // kept ranks: j == 0 or S_j < P * W_A (a prefix)
-    const double thr = __dmul_rn((double)r.P, (double)inc_at(nA - 1));
-    int c = __popc(__ballot_sync(~0u, lane < nA && (double)e0 < thr));
-    if (E == 2) c += __popc(__ballot_sync(~0u, 32 + lane < nA && (double)e1 < thr));
-    nK = max(c, 1);
-  }
-  const uint64_t WK = inc_at(nK - 1);
-  const uint64_t rr = draw_point(u, WK);
-  const unsigned h0 = __ballot_sync(~0u, lane < nK && e0 <= rr && rr < i0);
-  const unsigned h1 = E == 2 ? __ballot_sync(~0u, 32 + lane < nK && e1 <= rr && rr < i1) : 0u;
-  const uint64_t tk = key_at(h0 ? __ffs(h0) - 1 : (h1 ? 32 + __ffs(h1) - 1 : 0));
-  const uint64_t ck = key_at(nK - 1);
-  if (lane == 0) {
-    sh.res.token = (uint32_t)(tk & 0xFFFFFFFFu);
-    sh.res.WK = WK;
-    sh.res.ckK = ck;
-  }
-}
-
 // ------------------------------------------------------------ the kernel
 
 // What the out-of-line paths (general rounds, dense debug outputs) share
@@ -1325,6 +1285,8 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
   const int nspec = c.nspec;
   uint32_t *rec = c.rec;
   Planner &P = sh.pl;
+  // this CTA's values above its own threshold (counted by the first pass)
+  const bool dense_l1 = sh.nloc > (uint32_t)(sl.nvec * (Elem<T>::VEC / 4));
   if (rank == 0 && tid == 0) {
     memset(&P, 0, sizeof(P));
     P.state = ST_START;
@@ -1349,22 +1311,20 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
             sh.cmd = Cmd{OP_HIST, TGT_L1, P.l1lo, P.l1hi, P.l1shift, P.l1nbins};
             P.state = ST_AFTER_L1;
           }
-          for (int b = tid; b < NBIN; b += NT) {
-            L.l1c[b] = 0;
-            L.l1m[b] = 0;
-          }
+          for (int b = tid; b < NBIN * 4; b += NT) L.l1c[b] = 0;  // counts and parts
           break;
         }
         if (state == ST_AFTER_L1 || state == ST_LOC_AFTER_REF) {
           uint32_t *C = state == ST_AFTER_L1 ? L.l1c : L.refc;
           uint64_t *M = state == ST_AFTER_L1 ? L.l1m : L.refm;
+          const uint32_t *Mp = state == ST_AFTER_L1 ? L.l1p : L.refp;
           constexpr int PER = NBIN / NT;
           uint64_t lc[PER], lm[PER], sc = 0, sm = 0;
-          const uint32_t *Mlo = reinterpret_cast<const uint32_t *>(M), *Mhi = Mlo + NBIN;
 #pragma unroll
-          for (int q = 0; q < PER; ++q) {
-            lc[q] = C[tid * PER + q];
-            lm[q] = get_u64_split(&Mlo[tid * PER + q], &Mhi[tid * PER + q]);
+          for (int q = 0; q < PER; ++q) {  // read before the scan's barriers; M is written over the parts
+            const int b = tid * PER + q;
+            lc[q] = C[b];
+            lm[q] = (uint64_t)Mp[b] + ((uint64_t)Mp[NBIN + b] << 11) + ((uint64_t)Mp[2 * NBIN + b] << 22);
             sc += lc[q];
             sm += lm[q];
           }
@@ -1377,8 +1337,15 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
             C[tid * PER + q] = (uint32_t)oc;
             M[tid * PER + q] = om;
           }
+          if (tid == 0) sh.bcast_i = -1;
           __syncthreads();
           if (state == ST_AFTER_L1) {
+            if (r.topk && tc > (uint64_t)r.K) {  // the L1 bin holding the K-th key (prefixes are monotone)
+              const uint32_t km1 = (uint32_t)(r.K - 1);
+              for (int b = tid; b < P.l1nbins; b += NT)
+                if (C[b] > km1 && (b == 0 || C[b - 1] <= km1)) sh.bcast_i = b;
+              __syncthreads();
+            }
             if (tid == 0) {
               P.N = tc;
               P.Wv = tm;
@@ -1390,14 +1357,7 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
               P.base_c = 0;
               P.base_m = 0;
               const bool needA = r.topk && P.N > (uint64_t)r.K;
-              int b_end = P.nbins - 1;
-              if (needA) {
-                for (int b = 0; b < P.nbins; ++b)
-                  if ((uint64_t)L.l1c[b] > (uint64_t)(r.K - 1)) {
-                    b_end = b;
-                    break;
-                  }
-              }
+              const int b_end = needA && sh.bcast_i >= 0 ? sh.bcast_i : P.nbins - 1;
               const uint64_t pre = L.l1c[b_end];
               if (pre <= (uint64_t)TAIL_CAP) {
                 const uint64_t bhi = u64min(P.l1hi, P.l1lo + (((uint64_t)b_end + 1) << P.l1shift) - 1);
@@ -1487,10 +1447,7 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
           }
           __syncthreads();
           if (P.state == ST_LOC_AFTER_REF) {
-            for (int b = tid; b < NBIN; b += NT) {
-              L.refc[b] = 0;
-              L.refm[b] = 0;
-            }
+            for (int b = tid; b < NBIN * 4; b += NT) L.refc[b] = 0;  // counts and parts
           }
           if (P.state == ST_FINISH) continue;
           break;
@@ -1626,41 +1583,50 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
     if (cmd.op == OP_DONE) break;
     if (cmd.op == OP_HIST) {
       uint32_t *hc = rank == 0 ? (cmd.target == TGT_L1 ? L.l1c : L.refc) : L.l1c;
-      uint64_t *hm = rank == 0 ? (cmd.target == TGT_L1 ? L.l1m : L.refm) : L.l1m;
+      uint32_t *hp = hc + NBIN;  // the three mass parts follow the counts
       if (rank != 0) {
-        for (int b = tid; b < NBIN; b += NT) {
-          hc[b] = 0;
-          hm[b] = 0;
-        }
+        for (int b = tid; b < NBIN * 4; b += NT) hc[b] = 0;
         __syncthreads();
       }
-      for_each_value<T>(sl, L.spec, nspec, r, m, theta, cmd.lo, cmd.hi,
-                        [&](float x, uint32_t gid, uint64_t w) {
-                          const uint64_t ck = ckey(km, x, gid);
-                          const int b = (int)((ck - cmd.lo) >> cmd.shift);
-                          atomicAdd(&hc[b], 1u);
-                          add_u64_split(reinterpret_cast<uint32_t *>(hm) + b, reinterpret_cast<uint32_t *>(hm) + NBIN + b, w);
-                        });
+      auto add = [&](float x, uint32_t gid, uint64_t w, bool valid) {
+        if (!valid) return;
+        const uint64_t ck = ckey(km, x, gid);
+        const int b = (int)((ck - cmd.lo) >> cmd.shift);
+        atomicAdd(&hc[b], 1u);
+        const uint32_t p0 = (uint32_t)w & 0x7FFu, p1 = (uint32_t)(w >> 11) & 0x7FFu, p2 = (uint32_t)(w >> 22);
+        if (p0) atomicAdd(&hp[b], p0);
+        if (p1) atomicAdd(&hp[NBIN + b], p1);
+        if (p2) atomicAdd(&hp[2 * NBIN + b], p2);
+      };
+      // the first histogram spans the whole A range: dense when the first
+      // pass found most of this CTA's values above its threshold; the warp
+      // lists sit in the CTA-local candidate list, unused by histogram rounds
+      int *wq = reinterpret_cast<int *>(L.lcand) + (tid >> 5) * QW;
+      if (cmd.target == TGT_L1 && dense_l1)
+        for_each_value<T, true>(sl, L.spec, nspec, r, m, theta, cmd.lo, cmd.hi, wq, add);
+      else
+        for_each_value<T, false>(sl, L.spec, nspec, r, m, theta, cmd.lo, cmd.hi, wq, add);
       if (rank != 0) {
         __syncthreads();
         uint32_t *rc = cluster.map_shared_rank(cmd.target == TGT_L1 ? L.l1c : L.refc, 0);
-        uint64_t *rm = cluster.map_shared_rank(cmd.target == TGT_L1 ? L.l1m : L.refm, 0);
         for (int b = tid; b < cmd.nbins; b += NT) {
           if (hc[b]) {
             atomicAdd(&rc[b], hc[b]);
-            const uint32_t *ml = reinterpret_cast<const uint32_t *>(hm);
-            add_u64_split(reinterpret_cast<uint32_t *>(rm) + b, reinterpret_cast<uint32_t *>(rm) + NBIN + b,
-                          get_u64_split(ml + b, ml + NBIN + b));
+#pragma unroll
+            for (int q = 1; q <= 3; ++q)
+              if (hc[q * NBIN + b]) atomicAdd(&rc[q * NBIN + b], hc[q * NBIN + b]);
           }
         }
       }
     } else {  // OP_COMPACT into the CTA-local list
       if (tid == 0) sh.nloc = 0;
       __syncthreads();
-      for_each_value<T>(sl, L.spec, nspec, r, m, theta, cmd.lo, cmd.hi,
-                        [&](float x, uint32_t gid, uint64_t) {
-                          const uint32_t idx = atomicAdd(&sh.nloc, 1u);
-                          if (idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
+      // the warp lists sit in the REF histogram's area, dead once a bin is being compacted
+      for_each_value<T, false>(sl, L.spec, nspec, r, m, theta, cmd.lo, cmd.hi,
+                               reinterpret_cast<int *>(L.refc) + (tid >> 5) * QW,
+                        [&](float x, uint32_t gid, uint64_t, bool valid) {
+                          const uint32_t idx = warp_reserve(&sh.nloc, valid ? 1u : 0u);
+                          if (valid && idx < (uint32_t)LCAP) L.lcand[idx] = Cand{x, gid};
                         });
     }
     cluster.sync();  // round results complete
@@ -2269,21 +2235,27 @@ __global__ void __launch_bounds__(NT, 1)
         }
         uint64_t kmn = ~0ull, kmx = 0ull;
         uint32_t np = 0;
-        for (int q = 0; q < nl; ++q) {
-          const int cq = (int)min(lcnt[q], (uint32_t)(nl == 1 ? n : capq)), o = (int)loff[q];
-          for (int i = tid; i < cq; i += NT) tail_put(r, m, km, lists[q * stride + i], o + i, ts, kmn, kmx, np);
+        for (int i = tid; i < n; i += NT) {  // one candidate per thread; the lists lie gap-free at loff
+          int q = 0;
+          while (q + 1 < nl && i >= (int)loff[q + 1]) ++q;
+          tail_put(r, m, km, lists[q * stride + (i - (int)loff[q])], i, ts, kmn, kmx, np);
         }
         if (n <= RANK_MAX) {
           np = __reduce_add_sync(~0u, np);
           if (lane == 0 && np) atomicAdd(&sh.npass, np);
           __syncthreads();  // keys, weights and the pass count complete
           tail_rank_sort(n, ts);
+          if (MODE == 0) {
+            if (tid < 32) tail_resolve_warp(r, sh.u, ts, sh);
+          } else {
+            tail_emit(r, km, pl.tp_cap, rec, ts, sh);
+          }
         } else {
           tail_gather_end(kmn, kmx, np, ts, sh);
           tail_sort(n, ts, sh);
+          if (MODE == 0) tail_resolve(r, sh.u, ts, sh);
+          else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
         }
-        if (MODE == 0) tail_resolve(r, sh.u, ts, sh);
-        else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
       }
     }
   } else {
@@ -2400,9 +2372,19 @@ __global__ void __launch_bounds__(NT, 1)
       __syncthreads();
       if (tid == 0) sh.res.token = sh.best;
     } else {
-      tail_gather_end(kmn, kmx, np, ts, sh);
-      tail_sort((int)min(sh.nloc, (uint32_t)TAIL_CAP), ts, sh);
-      tail_resolve(r, sh.u, ts, sh);
+      __syncthreads();  // every candidate counted
+      const int n = (int)min(sh.nloc, (uint32_t)TAIL_CAP);
+      if (n <= RANK_MAX) {
+        np = __reduce_add_sync(~0u, np);
+        if ((tid & 31) == 0 && np) atomicAdd(&sh.npass, np);
+        __syncthreads();  // keys, weights and the pass count complete
+        tail_rank_sort(n, ts);
+        if (tid < 32) tail_resolve_warp(r, sh.u, ts, sh);
+      } else {
+        tail_gather_end(kmn, kmx, np, ts, sh);
+        tail_sort(n, ts, sh);
+        tail_resolve(r, sh.u, ts, sh);
+      }
     }
   }
   __syncthreads();
@@ -2437,7 +2419,8 @@ static int validate(const mstar_sampler_params_t *p) {
   if (p->dtype != MSTAR_DTYPE_F32 && p->dtype != MSTAR_DTYPE_BF16)
     return fail(MSTAR_ERR_INVALID, "dtype must be MSTAR_DTYPE_F32 or MSTAR_DTYPE_BF16");
   if (p->B < 1 || p->B > 65535) return fail(MSTAR_ERR_INVALID, "B must be in [1, 65535]");
-  if (p->V < 1 || p->V > (1 << 22)) return fail(MSTAR_ERR_INVALID, "V must be in [1, 4194304]");
+  // (general-path histogram mass parts are exact for rows of up to 2^21 ids)
+  if (p->V < 1 || p->V > (1 << 21)) return fail(MSTAR_ERR_INVALID, "V must be in [1, 2097152]");
   if (p->ld < p->V) return fail(MSTAR_ERR_INVALID, "ld must be >= V");
   if (p->vocab_offset < 0 || p->vocab_offset + p->V > 0x7FFFFFFFLL)
     return fail(MSTAR_ERR_INVALID, "vocab_offset out of range");
