@@ -72,12 +72,14 @@ constexpr int HIST_BYTES = NBIN * 16;  // per histogram: counts + three 11-bit m
 constexpr int GEN_BYTES = 2 * HIST_BYTES + GCAP * 8;  // L1 | REF (aliased by the sort scratch) | sort input
 static_assert(NBIN * 8 <= NBIN * 12, "64-bit mass prefixes fit over the part arrays");
 static_assert(GCAP * 20 + GBK * 8 <= HIST_BYTES, "general sort scratch");
+static_assert(GBK * 8 >= 256 * 8 && GCAP >= 256, "small general sort: weights over the bucket arrays");
 static_assert((NT / 32) * 256 * 4 <= HIST_BYTES && (NT / 32) * 256 <= LCAP * 2, "general-path warp lists");
 static_assert(GBK <= NT && NBIN % NT == 0 && NBK % NT == 0 && TAIL_CAP % NT == 0, "per-thread splits");
 constexpr int WORK_BYTES_MIN = GEN_BYTES;
 constexpr int LEAN_SCRATCH = 112 * 1024;  // fast-tail scratch (the leader's data region)
 static_assert(TAIL_CAP * 44 + NBK * 12 <= LEAN_SCRATCH, "fast tail scratch");
 static_assert(NBK % NT == 0, "tail bucket scan");
+static_assert(NT == 512, "the rank sort splits 512 threads into 64 / 128 / 256 slots");
 constexpr unsigned kWaitLimit = 1u << 24;
 
 struct __align__(8) Cand {
@@ -750,6 +752,48 @@ __device__ void tail_sort_scan(Cand *in, int n, float m, const SortScratch &s, C
   __syncthreads();
 }
 
+// tail_sort_scan for n <= RANK_MAX by pairwise counting (G = NT / slots
+// threads per element, as in tail_rank_sort): every element's rank and the
+// sum of the weights of the smaller keys in one pass.  Block-wide; ends with
+// a barrier.
+__device__ void tail_sort_scan_small(Cand *in, int n, float m, const SortScratch &s) {
+  const uint32_t km = okey(m);
+  const int t = threadIdx.x;
+  const int G = n <= 64 ? NT / 64 : n <= 128 ? NT / 128 : NT / 256;
+  const int e = t / G, part = t % G;
+  uint64_t *K = reinterpret_cast<uint64_t *>(s.mid);   // [GCAP] keys
+  uint64_t *W = reinterpret_cast<uint64_t *>(s.bcnt);  // [GBK] weights (bcnt and boff together)
+  Cand c{0.0f, 0u};
+  uint64_t key = ~0ull, w = 0;
+  if (e < n) {
+    c = in[e];
+    key = ckey(km, c.x, c.gid);
+    w = spec_w_from_e(spec_e(c.x, m));
+    if (part == 0) {
+      K[e] = key;
+      W[e] = w;
+    }
+  }
+  __syncthreads();  // keys and weights in; every element read from `in`
+  uint32_t rk = 0;
+  uint64_t before = 0;
+  for (int j = part; j < n; j += G) {
+    if (K[j] < key) {
+      ++rk;
+      before += W[j];
+    }
+  }
+  for (int o = G >> 1; o; o >>= 1) {
+    rk += __shfl_xor_sync(~0u, rk, o);
+    before += (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)before, o);
+  }
+  if (part == 0 && e < n) {
+    in[rk] = c;
+    s.S[rk] = before + w;
+  }
+  __syncthreads();
+}
+
 __device__ __forceinline__ uint64_t S_excl(const uint64_t *S, int j) { return j ? S[j - 1] : 0; }
 
 // ------------------------------------------------------- kernel sections
@@ -1049,15 +1093,16 @@ __device__ void tail_sort(int n, const TailScr &s, CtaSh &sh) {
 }
 
 // Sort of a small gathered set (n <= RANK_MAX, distinct keys) by pairwise
-// counting: G = NT / slots threads per candidate each compare it with every
+// counting: G = NT / slots threads per candidate (8, 4 or 2 for up to 64, 128
+// or 256 candidates) each compare it with every
 // G-th key (interleaved, conflict-free reads) and sum the counts and the
 // weights of the smaller keys, which give its rank and its exclusive weight
 // prefix in one pass.  Same outputs as tail_sort (RK / RW / RS in rank
 // order).  Block-wide; ends with a barrier.
-constexpr int RANK_MAX = 128;
+constexpr int RANK_MAX = 256;
 __device__ void tail_rank_sort(int n, const TailScr &s) {
   const int t = threadIdx.x;
-  const int G = n <= 64 ? NT / 64 : NT / 128;
+  const int G = n <= 64 ? NT / 64 : n <= 128 ? NT / 128 : NT / 256;
   const int e = t / G, part = t % G;
   const uint64_t key = e < n ? s.K[e] : ~0ull;
   uint32_t c = 0;
@@ -1162,6 +1207,31 @@ __device__ void tail_emit(const Row &r, uint32_t km, int tp_cap, uint32_t *rec, 
   }
   if (threadIdx.x == 0) sh.nemit = ne;
   __syncthreads();
+}
+
+// Sort the n gathered candidates (tail_put, every thread's kmn / kmx / np)
+// and resolve them (MODE 0: res.token / WK / ckK) or emit the shard record
+// (MODE 1).  Block-wide; a small set is resolved by warp 0 alone, so callers
+// read sh.res after a barrier.
+template <int MODE>
+__device__ void tail_finish(const Row &r, float u, uint32_t km, int n, uint64_t kmn, uint64_t kmx, uint32_t np,
+                            int tp_cap, uint32_t *rec, const TailScr &ts, CtaSh &sh) {
+  if (n <= RANK_MAX) {
+    np = __reduce_add_sync(~0u, np);
+    if ((threadIdx.x & 31) == 0 && np) atomicAdd(&sh.npass, np);
+    __syncthreads();  // keys, weights and the pass count complete
+    tail_rank_sort(n, ts);
+    if (MODE == 0) {
+      if (threadIdx.x < 32) tail_resolve_warp(r, u, ts, sh);
+    } else {
+      tail_emit(r, km, tp_cap, rec, ts, sh);
+    }
+  } else {
+    tail_gather_end(kmn, kmx, np, ts, sh);
+    tail_sort(n, ts, sh);
+    if (MODE == 0) tail_resolve(r, u, ts, sh);
+    else tail_emit(r, km, tp_cap, rec, ts, sh);
+  }
 }
 
 // top_k pre-selection for a tail with more candidates than top_k: counts of
@@ -1473,32 +1543,39 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
             const TailScr ts = tail_scratch(L.data);  // the leader's slice data is dead by now
             uint64_t kmn = ~0ull, kmx = 0ull;
             uint32_t np = 0;
-            for (int q = 0; q < S; ++q) {
-              const int o = (int)sh.goff[q], cq = min((int)sh.gcnt[q], n - o);
+            for (int i = tid; i < n; i += NT) {  // one candidate per thread; the lists lie gap-free at goff
+              int q = 0;
+              while (q + 1 < S && i >= (int)sh.goff[q + 1]) ++q;
               const Cand *list = cluster.map_shared_rank(L.lcand, q);
-              for (int i = tid; i < cq; i += NT) tail_put(r, m, km, list[i], o + i, ts, kmn, kmx, np);
+              tail_put(r, m, km, list[i - (int)sh.goff[q]], i, ts, kmn, kmx, np);
             }
-            tail_gather_end(kmn, kmx, np, ts, sh);
-            tail_sort(n, ts, sh);
-            if (MODE == 0) tail_resolve(r, u, ts, sh);
-            else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
+            tail_finish<MODE>(r, u, km, n, kmn, kmx, np, pl.tp_cap, rec, ts, sh);
           }
           if (tid == 0) P.state = ST_FINISH;
           __syncthreads();
           continue;
         }
         if (state == ST_LOC_AFTER_COMPACT) {
-          int n = 0;
-          for (int q = 0; q < S; ++q) {  // gather every CTA's list (DSMEM)
-            const int c = (int)min(cluster.map_shared_rank(&sh, q)->nloc, (uint32_t)LCAP);
-            const Cand *src = cluster.map_shared_rank(L.lcand, q);
-            for (int i = tid; i < c; i += NT)
-              if (n + i < GCAP) L.gsort.in[n + i] = src[i];
-            n += c;
+          if (tid < 32) {  // per-CTA counts of the compacted bin
+            const uint32_t c = lane < S ? min(cluster.map_shared_rank(&sh, lane)->nloc, (uint32_t)LCAP) : 0u;
+            uint32_t inc = c;
+            for (int o = 1; o < 32; o <<= 1) {
+              const uint32_t v = __shfl_up_sync(~0u, inc, o);
+              if (lane >= o) inc += v;
+            }
+            if (lane < 16) sh.goff[lane] = inc - c;
+            if (lane == 31) sh.ncand = min(inc, (uint32_t)GCAP);
           }
-          n = min(n, GCAP);
           __syncthreads();
-          tail_sort_scan(L.gsort.in, n, m, L.gsort, sh);
+          const int n = (int)sh.ncand;
+          for (int i = tid; i < n; i += NT) {  // every CTA's list (DSMEM), one element per thread
+            int q = 0;
+            while (q + 1 < S && i >= (int)sh.goff[q + 1]) ++q;
+            L.gsort.in[i] = cluster.map_shared_rank(L.lcand, q)[i - (int)sh.goff[q]];
+          }
+          __syncthreads();
+          if (n <= RANK_MAX) tail_sort_scan_small(L.gsort.in, n, m, L.gsort);
+          else tail_sort_scan(L.gsort.in, n, m, L.gsort, sh);
           const uint64_t *Sx = L.gsort.S;
           const Cand *sorted = L.gsort.in;
           if (tid == 0) sh.bcast_i = -1;
@@ -2240,22 +2317,7 @@ __global__ void __launch_bounds__(NT, 1)
           while (q + 1 < nl && i >= (int)loff[q + 1]) ++q;
           tail_put(r, m, km, lists[q * stride + (i - (int)loff[q])], i, ts, kmn, kmx, np);
         }
-        if (n <= RANK_MAX) {
-          np = __reduce_add_sync(~0u, np);
-          if (lane == 0 && np) atomicAdd(&sh.npass, np);
-          __syncthreads();  // keys, weights and the pass count complete
-          tail_rank_sort(n, ts);
-          if (MODE == 0) {
-            if (tid < 32) tail_resolve_warp(r, sh.u, ts, sh);
-          } else {
-            tail_emit(r, km, pl.tp_cap, rec, ts, sh);
-          }
-        } else {
-          tail_gather_end(kmn, kmx, np, ts, sh);
-          tail_sort(n, ts, sh);
-          if (MODE == 0) tail_resolve(r, sh.u, ts, sh);
-          else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
-        }
+        tail_finish<MODE>(r, MODE == 0 ? sh.u : 0.0f, km, n, kmn, kmx, np, pl.tp_cap, rec, ts, sh);
       }
     }
   } else {
@@ -2373,18 +2435,7 @@ __global__ void __launch_bounds__(NT, 1)
       if (tid == 0) sh.res.token = sh.best;
     } else {
       __syncthreads();  // every candidate counted
-      const int n = (int)min(sh.nloc, (uint32_t)TAIL_CAP);
-      if (n <= RANK_MAX) {
-        np = __reduce_add_sync(~0u, np);
-        if ((tid & 31) == 0 && np) atomicAdd(&sh.npass, np);
-        __syncthreads();  // keys, weights and the pass count complete
-        tail_rank_sort(n, ts);
-        if (tid < 32) tail_resolve_warp(r, sh.u, ts, sh);
-      } else {
-        tail_gather_end(kmn, kmx, np, ts, sh);
-        tail_sort(n, ts, sh);
-        tail_resolve(r, sh.u, ts, sh);
-      }
+      tail_finish<0>(r, sh.u, km, (int)min(sh.nloc, (uint32_t)TAIL_CAP), kmn, kmx, np, 0, nullptr, ts, sh);
     }
   }
   __syncthreads();
