@@ -1767,6 +1767,10 @@ __global__ void __launch_bounds__(NT, 1)
   __shared__ CtaSh sh;
 
   cluster_arrive_relaxed();  // matched by the wait before the first remote store
+  // Programmatic dependent launch: the next grid of the stream may place its
+  // blocks as SMs free up; they wait (griddepcontrol.wait below) until this
+  // grid has finished and its writes are visible.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const Layout L = make_layout(smem, pl);
   constexpr int es = (int)sizeof(T);
@@ -1787,6 +1791,10 @@ __global__ void __launch_bounds__(NT, 1)
   const int nvec = (int)((a_c1 - a_al + 15) / 16);  // all vectors of the slice
   const int nchunk = (int)((nbulk + CHUNK_BYTES - 1) / CHUNK_BYTES);
   uint4 *data4 = reinterpret_cast<uint4 *>(L.data);
+
+  // no global memory is read before the previous grid of the stream (which
+  // may have written the logits or the per-slot state) has completed
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- the bulk copies go out before anything else (they depend on nothing
   // but the geometry)
@@ -2586,13 +2594,17 @@ static int launch_T(const mstar_sampler_params_t *p, const Plan &pl, uint32_t *s
   cfg.blockDim = dim3(NT, 1, 1);
   cfg.dynamicSmemBytes = pl.smem_bytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = pl.S;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // blocks may be placed while the previous kernel of the stream finishes;
+  // the kernel waits for it (griddepcontrol.wait) before reading its inputs
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kern, *p, pl, send);
   if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
   return MSTAR_OK;
