@@ -1337,6 +1337,32 @@ struct RowCtx {
 
 __device__ __forceinline__ float xform(const Row &r, float v) { return r.greedy ? v : __fmul_rn(v, r.invT); }
 
+// Value bins of the general path's first histogram: bin b holds the values x
+// with E(b+1) < x <= E(b), E(b) = m - b * w (binary32 operations, so every CTA
+// and the planner agree on every bin), w = (m - theta) / NBIN.  Bins uniform
+// in value keep the bins near the row max (where the mass is) narrow; bins
+// of the order key itself would give almost all of them to values near zero.
+// The bins are monotone in the order key, so each is a key range.
+struct VBins {
+  float m, w, iw;  // row max, bin width, an approximate 1 / w (first guess only)
+};
+__device__ __forceinline__ float vb_edge(const VBins &v, int b) { return __fsub_rn(v.m, __fmul_rn((float)b, v.w)); }
+__device__ __forceinline__ int vb_bin(const VBins &v, float x) {
+  const float g = __fmul_rn(__fsub_rn(v.m, x), v.iw);
+  int b = g >= (float)(NBIN - 1) ? NBIN - 1 : (g > 0.0f ? (int)g : 0);
+  while (b > 0 && x > vb_edge(v, b)) --b;
+  while (b < NBIN - 1 && !(x > vb_edge(v, b + 1))) ++b;
+  return b;
+}
+// Order-key range [lo, hi] of value bin b (clipped to the A range's keys <= kmax).
+__device__ __forceinline__ void vb_range(const VBins &v, uint32_t km, int b, uint64_t kmax, uint64_t &lo,
+                                         uint64_t &hi) {
+  lo = b == 0 ? 0ull : (uint64_t)(km - okey(vb_edge(v, b))) << 32;
+  hi = b == NBIN - 1 ? kmax : ((uint64_t)(km - okey(vb_edge(v, b + 1))) << 32) - 1ull;
+  hi = u64min(hi, kmax);
+  lo = u64min(lo, kmax + 1);
+}
+
 // General path: leader-driven rounds of histogram (count + mass) and
 // compaction over the still-resident slices until every boundary (top_k,
 // top_p, the draw) is pinned to a bin small enough to sort.  Executed by
@@ -1357,6 +1383,12 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
   Planner &P = sh.pl;
   // this CTA's values above its own threshold (counted by the first pass)
   const bool dense_l1 = sh.nloc > (uint32_t)(sl.nvec * (Elem<T>::VEC / 4));
+  VBins vb;
+  vb.m = m;
+  vb.w = __fmul_rn(__fsub_rn(m, theta), 1.0f / NBIN);
+  vb.iw = 1.0f / vb.w;
+  // value bins unless the width is not a positive finite number
+  const bool vbins = vb.w > 0.0f && vb.w < INFINITY && vb.iw < INFINITY;
   if (rank == 0 && tid == 0) {
     memset(&P, 0, sizeof(P));
     P.state = ST_START;
@@ -1375,9 +1407,14 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
             const uint32_t DA = km - okey(theta);
             P.l1lo = 0;
             P.l1hi = ((uint64_t)DA << 32) | 0xFFFFFFFFull;
-            const int bits = 64 - __clzll((long long)(P.l1hi - P.l1lo));
-            P.l1shift = bits > NBIN_LOG2 ? bits - NBIN_LOG2 : 0;
-            P.l1nbins = (int)((P.l1hi - P.l1lo) >> P.l1shift) + 1;
+            if (vbins) {  // value bins (shift -1 marks them)
+              P.l1shift = -1;
+              P.l1nbins = NBIN;
+            } else {
+              const int bits = 64 - __clzll((long long)(P.l1hi - P.l1lo));
+              P.l1shift = bits > NBIN_LOG2 ? bits - NBIN_LOG2 : 0;
+              P.l1nbins = (int)((P.l1hi - P.l1lo) >> P.l1shift) + 1;
+            }
             sh.cmd = Cmd{OP_HIST, TGT_L1, P.l1lo, P.l1hi, P.l1shift, P.l1nbins};
             P.state = ST_AFTER_L1;
           }
@@ -1430,7 +1467,9 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
               const int b_end = needA && sh.bcast_i >= 0 ? sh.bcast_i : P.nbins - 1;
               const uint64_t pre = L.l1c[b_end];
               if (pre <= (uint64_t)TAIL_CAP) {
-                const uint64_t bhi = u64min(P.l1hi, P.l1lo + (((uint64_t)b_end + 1) << P.l1shift) - 1);
+                uint64_t blo, bhi;
+                if (P.l1shift < 0) vb_range(vb, km, b_end, P.l1hi, blo, bhi);
+                else bhi = u64min(P.l1hi, P.l1lo + (((uint64_t)b_end + 1) << P.l1shift) - 1);
                 sh.cmd = Cmd{OP_COMPACT, 0, P.l1lo, bhi, 0, 0};
                 P.state = ST_AFTER_PREFIX;
               } else if (needA) {
@@ -1494,12 +1533,17 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
               P.state = ST_FINISH;
               sh.res.status |= MSTAR_STATUS_EMPTY;
             } else {
-              const uint64_t blo = P.lo + ((uint64_t)b << P.shift);
-              const uint64_t bhi = u64min(P.hi, blo + (1ull << P.shift) - 1);
+              uint64_t blo, bhi;
+              if (P.shift < 0) {
+                vb_range(vb, km, b, P.hi, blo, bhi);
+              } else {
+                blo = P.lo + ((uint64_t)b << P.shift);
+                bhi = u64min(P.hi, blo + (1ull << P.shift) - 1);
+              }
               const uint64_t cnt = (uint64_t)C[b] - (b ? C[b - 1] : 0);
               P.cbase_c = P.base_c + (b ? C[b - 1] : 0);
               P.cbase_m = P.base_m + (b ? M[b - 1] : 0);
-              if (cnt <= (uint64_t)GCAP || P.shift == 0) {
+              if (cnt <= (uint64_t)GCAP || P.shift == 0 || blo >= bhi) {
                 sh.cmd = Cmd{OP_COMPACT, 0, blo, bhi, 0, 0};
                 P.state = ST_LOC_AFTER_COMPACT;
               } else {
@@ -1668,7 +1712,7 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
       auto add = [&](float x, uint32_t gid, uint64_t w, bool valid) {
         if (!valid) return;
         const uint64_t ck = ckey(km, x, gid);
-        const int b = (int)((ck - cmd.lo) >> cmd.shift);
+        const int b = cmd.shift < 0 ? vb_bin(vb, x) : (int)((ck - cmd.lo) >> cmd.shift);
         atomicAdd(&hc[b], 1u);
         const uint32_t p0 = (uint32_t)w & 0x7FFu, p1 = (uint32_t)(w >> 11) & 0x7FFu, p2 = (uint32_t)(w >> 22);
         if (p0) atomicAdd(&hp[b], p0);
