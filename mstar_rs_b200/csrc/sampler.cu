@@ -1587,13 +1587,66 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
             const TailScr ts = tail_scratch(L.data);  // the leader's slice data is dead by now
             uint64_t kmn = ~0ull, kmx = 0ull;
             uint32_t np = 0;
-            for (int i = tid; i < n; i += NT) {  // one candidate per thread; the lists lie gap-free at goff
-              int q = 0;
-              while (q + 1 < S && i >= (int)sh.goff[q + 1]) ++q;
-              const Cand *list = cluster.map_shared_rank(L.lcand, q);
-              tail_put(r, m, km, list[i - (int)sh.goff[q]], i, ts, kmn, kmx, np);
+            if (P.l1shift < 0 && n > 64) {
+              // Placed by value bin: the first histogram's prefix counts give
+              // every bin's slot range in rank order (the compacted prefix is
+              // exactly bins 0..b_end), so one pass places each candidate in
+              // its bin and a pass over each (narrow) bin ranks it there.
+              uint32_t *fill = L.refc;  // per-bin fill counters (the REF histogram is idle here)
+              const uint32_t *C = L.l1c;
+              for (int b = tid; b < NBIN; b += NT) fill[b] = 0;
+              __syncthreads();
+              for (int i = tid; i < n; i += NT) {
+                int q = 0;
+                while (q + 1 < S && i >= (int)sh.goff[q + 1]) ++q;
+                const Cand cd = cluster.map_shared_rank(L.lcand, q)[i - (int)sh.goff[q]];
+                const int b = vb_bin(vb, cd.x);
+                const uint32_t pos = (b ? C[b - 1] : 0u) + atomicAdd(&fill[b], 1u);
+                if (pos < (uint32_t)n) {
+                  const uint64_t w = weight_A(r, cd.x, m);
+                  ts.K[pos] = ckey(km, cd.x, cd.gid);
+                  ts.W[pos] = w;
+                  ts.P[pos] = (uint32_t)b;
+                  np += w != 0;
+                }
+              }
+              np = __reduce_add_sync(~0u, np);
+              if (lane == 0 && np) atomicAdd(&sh.npass, np);
+              __syncthreads();
+              for (int pos = tid; pos < n; pos += NT) {  // rank inside the bin
+                const int b = (int)ts.P[pos];
+                const uint32_t st = b ? C[b - 1] : 0u, en = min(C[b], (uint32_t)n);
+                const uint64_t key = ts.K[pos];
+                uint32_t rk = 0;
+                for (uint32_t j = st; j < en; ++j) rk += ts.K[j] < key;
+                ts.RK[st + rk] = key;
+                ts.RW[st + rk] = ts.W[pos];
+              }
+              __syncthreads();
+              {  // exclusive prefix of the weights in rank order
+                const int seg = (n + NT - 1) / NT;
+                const int a0 = min(n, tid * seg), a1 = min(n, a0 + seg);
+                uint64_t loc = 0;
+                for (int j = a0; j < a1; ++j) loc += ts.RW[j];
+                uint64_t tot;
+                uint64_t run = block_exscan_u64(loc, tot, sh);
+                for (int j = a0; j < a1; ++j) {
+                  ts.RS[j] = run;
+                  run += ts.RW[j];
+                }
+              }
+              __syncthreads();
+              if (MODE == 0) tail_resolve(r, u, ts, sh);
+              else tail_emit(r, km, pl.tp_cap, rec, ts, sh);
+            } else {
+              for (int i = tid; i < n; i += NT) {  // one candidate per thread; the lists lie gap-free at goff
+                int q = 0;
+                while (q + 1 < S && i >= (int)sh.goff[q + 1]) ++q;
+                const Cand *list = cluster.map_shared_rank(L.lcand, q);
+                tail_put(r, m, km, list[i - (int)sh.goff[q]], i, ts, kmn, kmx, np);
+              }
+              tail_finish<MODE>(r, u, km, n, kmn, kmx, np, pl.tp_cap, rec, ts, sh);
             }
-            tail_finish<MODE>(r, u, km, n, kmn, kmx, np, pl.tp_cap, rec, ts, sh);
           }
           if (tid == 0) P.state = ST_FINISH;
           __syncthreads();
