@@ -2173,14 +2173,13 @@ __global__ void __launch_bounds__(NT, 1)
   // Specials: bias (list order) -> penalties -> mask -> transform, after the
   // last block, from the resident data.  Entry i of the list holds its table
   // slot and becomes (x, id) in place.
-  auto finalize = [&]() {
-    __syncthreads();  // table complete; every chunk landed (each thread waited on all)
+  auto finalize = [&](int t0, int stride) {  // entries t0, t0 + stride, ...
     const bool bias_smem = p.bias_ids && p.NB <= BIAS_SMEM;
     const int32_t *bi = p.bias_ids ? p.bias_ids + (int64_t)slot * p.NB : nullptr;
     const float *bv = p.bias_vals ? p.bias_vals + (int64_t)slot * p.NB : nullptr;
     const int n = min((int)sh.n_spec, pl.spec_cap);
     const uint32_t *spec32 = reinterpret_cast<const uint32_t *>(L.spec);
-    for (int i = tid; i < n; i += NT) {
+    for (int i = t0; i < n; i += stride) {
       const int2 ent = L.ht[spec32[2 * i]];
       const int cnt = ent.y & ~HT_MASKED;
       float v = Elem<T>::smem_elem(L.data, ent.x - c0al);
@@ -2228,24 +2227,38 @@ __global__ void __launch_bounds__(NT, 1)
       process(kb, ke);
     }
   }
-  if (has_spec) finalize();
   if (timed_out) atomicOr(&sh.status, MSTAR_STATUS_TIMEOUT);
   if (lane == 0) sh.wqn[tid >> 5] = wq;
-  {
-    float cmx = fmaxf(xform(r, Elem<T>::acc_f(racc)), spec_max);
+  {  // this CTA's max over its non-special values
+    float cmx = xform(r, Elem<T>::acc_f(racc));
     for (int o = 16; o; o >>= 1) cmx = fmaxf(cmx, __shfl_xor_sync(~0u, cmx, o));
     if (lane == 0 && cmx > -INFINITY) atomicMax(&sh.cmax, okey(cmx));
   }
-  __syncthreads();  // CTA max, queues, specials complete
-  const float cm = okey_inv(sh.cmax);  // this CTA's max (transformed)
-  const int nspec = min((int)sh.n_spec, pl.spec_cap);
-  // ---- this CTA's value threshold, from its own max: every member of the
-  // row's A set (whose max m >= cm) has x >= theta(cm)
+  __syncthreads();  // non-special max and queues complete; specials' table built, every chunk landed
+  // ---- this CTA's value threshold theta(cm), cm its max: every member of
+  // the row's A set (whose max m >= cm) has x >= theta(cm).  Warp 0 computes
+  // it from the non-special max while the other warps finalize the specials;
+  // it is redone only when a special holds the CTA max.
+  const float cm_ns = okey_inv(sh.cmax);
   if (tid < 32) {
-    const float t = cm > -INFINITY ? choose_theta(r, cm) : INFINITY;
+    const float t = cm_ns > -INFINITY ? choose_theta(r, cm_ns) : INFINITY;
     if (lane == 0) sh.theta = t;
+  } else if (has_spec) {
+    finalize(tid - 32, NT - 32);
+    float smx = spec_max;
+    for (int o = 16; o; o >>= 1) smx = fmaxf(smx, __shfl_xor_sync(~0u, smx, o));
+    if (lane == 0 && smx > -INFINITY) atomicMax(&sh.cmax, okey(smx));
   }
-  __syncthreads();
+  __syncthreads();  // specials final, CTA max complete
+  const float cm = okey_inv(sh.cmax);  // this CTA's max (transformed)
+  if (cm != cm_ns) {  // uniform: a special holds the CTA max
+    if (tid < 32) {
+      const float t = choose_theta(r, cm);
+      if (lane == 0) sh.theta = t;
+    }
+    __syncthreads();
+  }
+  const int nspec = min((int)sh.n_spec, pl.spec_cap);
   const float theta_l = sh.theta;
   const int capq = TAIL_CAP / S;  // candidates each CTA may push to the leader
   cluster_wait();                 // every CTA of the cluster runs: remote stores are safe
