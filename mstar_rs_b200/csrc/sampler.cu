@@ -777,11 +777,12 @@ __device__ void tail_sort_scan_small(Cand *in, int n, float m, const SortScratch
   __syncthreads();  // keys and weights in; every element read from `in`
   uint32_t rk = 0;
   uint64_t before = 0;
-  for (int j = part; j < n; j += G) {
-    if (K[j] < key) {
-      ++rk;
-      before += W[j];
-    }
+#pragma unroll 4
+  for (int j = part; j < n; j += G) {  // branch-free: loads of later j overlap
+    const bool lt = K[j] < key;
+    const uint64_t wj = W[j];
+    rk += lt ? 1u : 0u;
+    before += lt ? wj : 0ull;
   }
   for (int o = G >> 1; o; o >>= 1) {
     rk += __shfl_xor_sync(~0u, rk, o);
@@ -1107,12 +1108,12 @@ __device__ void tail_rank_sort(int n, const TailScr &s) {
   const uint64_t key = e < n ? s.K[e] : ~0ull;
   uint32_t c = 0;
   uint64_t before = 0;
-  for (int j = part; j < n; j += G) {
-    const uint64_t kj = s.K[j];
-    if (kj < key) {
-      ++c;
-      before += s.W[j];
-    }
+#pragma unroll 4
+  for (int j = part; j < n; j += G) {  // branch-free: loads of later j overlap
+    const bool lt = s.K[j] < key;
+    const uint64_t wj = s.W[j];
+    c += lt ? 1u : 0u;
+    before += lt ? wj : 0ull;
   }
   for (int o = G >> 1; o; o >>= 1) {
     c += __shfl_xor_sync(~0u, c, o);

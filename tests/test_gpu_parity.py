@@ -127,3 +127,30 @@ def test_candidate_count_paths(oracle_lib, dtype, cluster):
     o = oracle_lib.run(case, debug=True)
     g = run_gpu(case, cluster_size=cluster)
     assert_parity(g, o, case)
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_general_value_bins(oracle_lib, seed):
+    """General-path rows whose first histogram decides everything: top_k
+    prefixes that fit the tail (placed by value bin, then ranked inside each
+    bin), heavy exact ties (quantised logits: whole bins of equal values),
+    and a flat row (every value in one bin: refined by id)."""
+    from mstar_rs_b200 import _native as N
+    from mstar_rs_b200.workloads import bucket_sweep
+
+    case = bucket_sweep(6, seed=seed, V=40000)
+    case.uniforms = np.random.default_rng(seed).random(case.B).astype(np.float32)
+    case.seed = None
+    case.offset = None
+    case.top_k[:] = [120, 700, 1500, 1024, 65, 300]
+    if seed % 2:
+        x = case.logits_f32()
+        x = (np.round(x * 1.0) / 1.0).astype(np.float32)  # integer logits: many exact ties
+        x[5, :] = 1.5  # a flat row
+        case.logits = x
+    o = oracle_lib.run(case, debug=True)
+    for cl in (0, 4):
+        g = run_gpu(case, cluster_size=cl)
+        assert_parity(g, o, case)
+        g = run_gpu(case, cluster_size=cl, flags=N.FLAG_FORCE_GENERAL)
+        assert_parity(g, o, case)
