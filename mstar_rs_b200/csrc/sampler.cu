@@ -79,6 +79,7 @@ constexpr int WORK_BYTES_MIN = GEN_BYTES;
 constexpr int LEAN_SCRATCH = 112 * 1024;  // fast-tail scratch (the leader's data region)
 static_assert(TAIL_CAP * 44 + NBK * 12 <= LEAN_SCRATCH, "fast tail scratch");
 static_assert(NBK % NT == 0, "tail bucket scan");
+static_assert(NBK >= 2 * 256 && NBK >= NT, "value-bucket tail: counts and starts over the bucket counts, weights over the masses");
 static_assert(NT == 512, "the rank sort splits 512 threads into 64 / 128 / 256 slots");
 constexpr unsigned kWaitLimit = 1u << 24;
 
@@ -172,8 +173,6 @@ struct CtaSh {
   uint64_t kmin, kmax;  // tail: key range
   uint32_t npass;       // tail: candidates passing the value-A predicate
   uint32_t cnt_k;       // tail: ranks kept by top_p
-  uint32_t pf_n, pf_zero;  // top_k pre-selection: kept count, a zero offset
-  int pf_bstar;            // top_k pre-selection: last kept bucket
   float u;              // the row's uniform draw
   uint32_t n_spec;
   uint32_t ht_fail;
@@ -752,7 +751,7 @@ __device__ void tail_sort_scan(Cand *in, int n, float m, const SortScratch &s, C
   __syncthreads();
 }
 
-// tail_sort_scan for n <= RANK_MAX by pairwise counting (G = NT / slots
+// tail_sort_scan for n <= 256 by pairwise counting (G = NT / slots
 // threads per element, as in tail_rank_sort): every element's rank and the
 // sum of the weights of the smaller keys in one pass.  Block-wide; ends with
 // a barrier.
@@ -1093,14 +1092,13 @@ __device__ void tail_sort(int n, const TailScr &s, CtaSh &sh) {
   __syncthreads();
 }
 
-// Sort of a small gathered set (n <= RANK_MAX, distinct keys) by pairwise
+// Sort of a small gathered set (n <= 256, distinct keys) by pairwise
 // counting: G = NT / slots threads per candidate (8, 4 or 2 for up to 64, 128
 // or 256 candidates) each compare it with every
 // G-th key (interleaved, conflict-free reads) and sum the counts and the
 // weights of the smaller keys, which give its rank and its exclusive weight
 // prefix in one pass.  Same outputs as tail_sort (RK / RW / RS in rank
 // order).  Block-wide; ends with a barrier.
-constexpr int RANK_MAX = 256;
 __device__ void tail_rank_sort(int n, const TailScr &s) {
   const int t = threadIdx.x;
   const int G = n <= 64 ? NT / 64 : n <= 128 ? NT / 128 : NT / 256;
@@ -1164,7 +1162,7 @@ __device__ void tail_resolve(const Row &r, float u, const TailScr &s, CtaSh &sh)
   __syncthreads();
 }
 
-// tail_resolve for at most RANK_MAX rank-ordered candidates, by one full
+// tail_resolve for at most NT rank-ordered candidates, by one full
 // warp with ballots and reductions (no block barrier).
 __device__ void tail_resolve_warp(const Row &r, float u, const TailScr &s, CtaSh &sh) {
   const int lane = threadIdx.x & 31;
@@ -1210,6 +1208,111 @@ __device__ void tail_emit(const Row &r, uint32_t km, int tp_cap, uint32_t *rec, 
   __syncthreads();
 }
 
+// Sort of a larger gathered set (RANK_SMALL < n <= TAIL_CAP) by value
+// bucket: 255 buckets uniform in x over the A range below the row max (with
+// a margin, so the last bucket holds only values outside A, weight 0, left
+// unranked), one counting pass, a warp scan of the counts, a scatter into
+// bucket order and a rank inside each bucket; then the exclusive weight
+// prefix.  Same outputs as tail_sort (RK / RW / RS in rank order).  Returns
+// false, having sorted nothing, when a bucket of A holds more than
+// BUCKET_MAX candidates (runs of exact ties: the caller then sorts by order
+// key, whose buckets split ties by id).  Block-wide; ends with a barrier.
+constexpr int RANK_SMALL = 128;
+constexpr uint32_t BUCKET_MAX = 64;
+__device__ bool tail_bucket_sort(const Row &r, uint32_t km, int n, const TailScr &s, CtaSh &sh) {
+  const int t = threadIdx.x, lane = t & 31;
+  const float m = okey_inv(km);
+  const float span = fmaxf(r.minp ? fminf(23.5f, __fadd_rn(-r.lnMp, 0.25f)) : 23.5f, 1e-3f);
+  const float sc = 256.0f / span;
+  auto bucket_of = [&](uint64_t key) {  // monotone in the key
+    const float x = okey_inv(km - (uint32_t)(key >> 32));
+    const float g = __fmul_rn(__fsub_rn(m, x), sc);
+    return g >= 255.0f ? 255u : (g > 0.0f ? (uint32_t)g : 0u);
+  };
+  uint32_t *cnt = s.bc, *start = s.bc + 256;
+  uint64_t *BK = s.RS, *BW = s.bm;  // bucket order (RS is written last)
+  if (t < 256) cnt[t] = 0u;
+  __syncthreads();
+  for (int i = t; i < n; i += NT) {
+    const uint32_t b = bucket_of(s.K[i]);
+    s.P[i] = (b << 16) | atomicAdd(&cnt[b], 1u);
+  }
+  __syncthreads();
+  if (t < 32) {  // exclusive scan of the counts, 8 buckets per lane
+    uint32_t c[8], tot = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      c[q] = cnt[lane * 8 + q];
+      tot += c[q];
+    }
+    uint32_t inc = tot;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(~0u, inc, o);
+      if (lane >= o) inc += v;
+    }
+    uint32_t run = inc - tot, big = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      start[lane * 8 + q] = run;
+      run += c[q];
+      big |= (lane * 8 + q < 255 && c[q] > BUCKET_MAX) ? 1u : 0u;
+    }
+    big = __reduce_or_sync(~0u, big);
+    if (lane == 0) sh.bcast_i = (int)big;
+  }
+  __syncthreads();
+  if (sh.bcast_i) return false;  // uniform
+  // with top_k only the first K ranks are read: buckets starting at or past
+  // rank K are neither placed nor ranked
+  const uint32_t lim = r.topk ? (uint32_t)r.K : 0xFFFFFFFFu;
+  for (int i = t; i < n; i += NT) {
+    const uint32_t pb = s.P[i];
+    if (start[pb >> 16] >= lim) continue;
+    const uint32_t dst = start[pb >> 16] + (pb & 0xFFFFu);
+    BK[dst] = s.K[i];
+    BW[dst] = s.W[i];
+  }
+  __syncthreads();
+  // placed positions: [0, end of the last bucket that starts before lim)
+  uint32_t placed = (uint32_t)n;
+  if (lim < (uint32_t)n) {
+    int lo = 0, hi = 255;  // the last bucket whose start is < lim (starts are non-decreasing)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (start[mid] < lim) lo = mid;
+      else hi = mid - 1;
+    }
+    placed = start[lo] + cnt[lo];
+  }
+  for (int q = t; q < (int)placed; q += NT) {  // rank inside the bucket
+    const uint64_t key = BK[q];
+    const uint32_t b = bucket_of(key);
+    const uint32_t st = start[b], en = st + cnt[b];
+    uint32_t rk = (uint32_t)q - st;  // outside A: any order
+    if (b < 255u) {
+      rk = 0;
+      for (uint32_t j = st; j < en; ++j) rk += BK[j] < key ? 1u : 0u;
+    }
+    s.RK[st + rk] = key;
+    s.RW[st + rk] = BW[q];
+  }
+  __syncthreads();
+  {  // exclusive prefix of the weights in rank order, a segment per thread
+    const int seg = (n + NT - 1) / NT;
+    const int a0 = min(n, t * seg), a1 = min(n, a0 + seg);
+    uint64_t loc = 0;
+    for (int j = a0; j < a1; ++j) loc += s.RW[j];
+    uint64_t tot;
+    uint64_t run = block_exscan_u64(loc, tot, sh);
+    for (int j = a0; j < a1; ++j) {
+      s.RS[j] = run;
+      run += s.RW[j];
+    }
+  }
+  __syncthreads();
+  return true;
+}
+
 // Sort the n gathered candidates (tail_put, every thread's kmn / kmx / np)
 // and resolve them (MODE 0: res.token / WK / ckK) or emit the shard record
 // (MODE 1).  Block-wide; a small set is resolved by warp 0 alone, so callers
@@ -1217,105 +1320,27 @@ __device__ void tail_emit(const Row &r, uint32_t km, int tp_cap, uint32_t *rec, 
 template <int MODE>
 __device__ void tail_finish(const Row &r, float u, uint32_t km, int n, uint64_t kmn, uint64_t kmx, uint32_t np,
                             int tp_cap, uint32_t *rec, const TailScr &ts, CtaSh &sh) {
-  if (n <= RANK_MAX) {
-    np = __reduce_add_sync(~0u, np);
-    if ((threadIdx.x & 31) == 0 && np) atomicAdd(&sh.npass, np);
-    __syncthreads();  // keys, weights and the pass count complete
-    tail_rank_sort(n, ts);
-    if (MODE == 0) {
+  np = __reduce_add_sync(~0u, np);
+  if ((threadIdx.x & 31) == 0 && np) atomicAdd(&sh.npass, np);
+  __syncthreads();  // keys, weights and the pass count complete
+  bool sorted = true;
+  if (n <= RANK_SMALL) tail_rank_sort(n, ts);
+  else sorted = tail_bucket_sort(r, km, n, ts, sh);
+  if (!sorted) {  // long runs of ties: buckets of the order key (the pass count is in already)
+    tail_gather_end(kmn, kmx, 0u, ts, sh);
+    tail_sort(n, ts, sh);
+  }
+  if (MODE == 0) {
+    if (n <= NT) {
       if (threadIdx.x < 32) tail_resolve_warp(r, u, ts, sh);
     } else {
-      tail_emit(r, km, tp_cap, rec, ts, sh);
+      tail_resolve(r, u, ts, sh);
     }
   } else {
-    tail_gather_end(kmn, kmx, np, ts, sh);
-    tail_sort(n, ts, sh);
-    if (MODE == 0) tail_resolve(r, u, ts, sh);
-    else tail_emit(r, km, tp_cap, rec, ts, sh);
+    tail_emit(r, km, tp_cap, rec, ts, sh);
   }
 }
 
-// top_k pre-selection for a tail with more candidates than top_k: counts of
-// the order keys in PF_NB buckets over their range; every candidate in a
-// bucket at or below the one holding the K-th smallest key is kept (at least
-// K, including all of the K smallest) in one compacted list at s.RS.  The
-// kept candidates' first K are the row's first K, and whether they carry
-// weight is decided the same way, so the tail runs unchanged on the list.
-// Block-wide; ends with a barrier; leaves the tail state reset.
-constexpr int PF_NB = 256;
-__device__ void tail_topk_prefilter(const Row &r, uint32_t km, int S, const uint32_t *cnt, const uint32_t *off,
-                                    const Cand *lists, int stride, int n, const TailScr &s, CtaSh &sh) {
-  const int t = threadIdx.x, lane = t & 31;
-  uint64_t kmn = ~0ull, kmx = 0ull;
-  for (int q = 0; q < S; ++q) {
-    const int c = (int)cnt[q], o = (int)off[q];
-    for (int i = t; i < c; i += NT) {
-      const Cand cd = lists[q * stride + i];
-      const uint64_t k = ckey(km, cd.x, cd.gid);
-      s.RK[o + i] = k;
-      kmn = u64min(kmn, k);
-      kmx = u64max(kmx, k);
-    }
-  }
-  for (int o = 16; o; o >>= 1) {
-    kmn = u64min(kmn, (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)kmn, o));
-    kmx = u64max(kmx, (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)kmx, o));
-  }
-  if (lane == 0 && kmn <= kmx) {
-    atomicMin((unsigned long long *)&sh.kmin, (unsigned long long)kmn);
-    atomicMax((unsigned long long *)&sh.kmax, (unsigned long long)kmx);
-  }
-  for (int b = t; b < PF_NB; b += NT) s.bc[b] = 0;
-  __syncthreads();
-  const uint64_t kmin = sh.kmin, range = sh.kmax - kmin;
-  const int bits = range ? 64 - __clzll((long long)range) : 0;
-  const int bsh = bits > 8 ? bits - 8 : 0;
-  static_assert(PF_NB == 256, "8-bit buckets");
-  for (int i = t; i < n; i += NT) atomicAdd(&s.bc[(uint32_t)((s.RK[i] - kmin) >> bsh)], 1u);
-  __syncthreads();
-  if (t < 32) {  // first bucket whose inclusive count reaches K
-    constexpr int PB = PF_NB / 32;
-    uint32_t c[PB], sum = 0;
-#pragma unroll
-    for (int j = 0; j < PB; ++j) {
-      c[j] = s.bc[lane * PB + j];
-      sum += c[j];
-    }
-    uint32_t inc = sum;
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t v = __shfl_up_sync(~0u, inc, o);
-      if (lane >= o) inc += v;
-    }
-    uint32_t run = inc - sum;
-    int hit = PF_NB;
-#pragma unroll
-    for (int j = 0; j < PB; ++j) {
-      run += c[j];
-      if (hit == PF_NB && run >= (uint32_t)r.K) hit = lane * PB + j;
-    }
-    hit = __reduce_min_sync(~0u, hit);
-    if (lane == 0) {
-      sh.pf_bstar = hit;
-      sh.pf_n = 0;
-      sh.pf_zero = 0;
-      tail_reset(sh);
-    }
-  }
-  __syncthreads();
-  const uint32_t bstar = (uint32_t)sh.pf_bstar;
-  Cand *out = reinterpret_cast<Cand *>(s.RS);
-  for (int q = 0; q < S; ++q) {  // warp-uniform trip counts: one reservation per warp and step
-    const int c = (int)cnt[q], o = (int)off[q];
-    for (int i0 = 0; i0 < c; i0 += NT) {
-      const int i = i0 + t;
-      const bool keep = i < c && (uint32_t)((s.RK[o + i] - kmin) >> bsh) <= bstar;
-      if (!__any_sync(~0u, keep)) continue;
-      const uint32_t w = warp_reserve(&sh.pf_n, keep ? 1u : 0u);
-      if (keep) out[w] = lists[q * stride + i];
-    }
-  }
-  __syncthreads();
-}
 
 // ------------------------------------------------------------ the kernel
 
@@ -1672,7 +1697,7 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
             L.gsort.in[i] = cluster.map_shared_rank(L.lcand, q)[i - (int)sh.goff[q]];
           }
           __syncthreads();
-          if (n <= RANK_MAX) tail_sort_scan_small(L.gsort.in, n, m, L.gsort);
+          if (n <= 128) tail_sort_scan_small(L.gsort.in, n, m, L.gsort);
           else tail_sort_scan(L.gsort.in, n, m, L.gsort, sh);
           const uint64_t *Sx = L.gsort.S;
           const Cand *sorted = L.gsort.in;
@@ -2414,27 +2439,16 @@ __global__ void __launch_bounds__(NT, 1)
           sh.nemit = -1;
         }
       } else {
-        // candidate lists: the pushed ones (S lists, gap-free by goff), or
-        // one list kept by the top_k pre-selection
+        // the S pushed candidate lists (list q at lcand + q * capq, its
+        // entries numbered from goff[q] in the gathered order)
         const TailScr ts = tail_scratch(L.data);  // the leader's slice data is dead by now
-        const Cand *lists = L.lcand;
-        const uint32_t *lcnt = sh.gcnt, *loff = sh.goff;
-        int nl = S, stride = capq, n = (int)sh.ncand;
-        if (r.topk && r.K < n && n > RANK_MAX) {
-          tail_topk_prefilter(r, km, S, sh.gcnt, sh.goff, L.lcand, capq, n, ts, sh);
-          lists = reinterpret_cast<const Cand *>(ts.RS);
-          lcnt = &sh.pf_n;
-          loff = &sh.pf_zero;
-          nl = 1;
-          stride = 0;
-          n = (int)sh.pf_n;
-        }
+        const int n = (int)sh.ncand;
         uint64_t kmn = ~0ull, kmx = 0ull;
         uint32_t np = 0;
-        for (int i = tid; i < n; i += NT) {  // one candidate per thread; the lists lie gap-free at loff
+        for (int i = tid; i < n; i += NT) {  // one candidate per thread
           int q = 0;
-          while (q + 1 < nl && i >= (int)loff[q + 1]) ++q;
-          tail_put(r, m, km, lists[q * stride + (i - (int)loff[q])], i, ts, kmn, kmx, np);
+          while (q + 1 < S && i >= (int)sh.goff[q + 1]) ++q;
+          tail_put(r, m, km, L.lcand[q * capq + (i - (int)sh.goff[q])], i, ts, kmn, kmx, np);
         }
         tail_finish<MODE>(r, MODE == 0 ? sh.u : 0.0f, km, n, kmn, kmx, np, pl.tp_cap, rec, ts, sh);
       }
