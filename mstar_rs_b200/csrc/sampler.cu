@@ -1987,6 +1987,7 @@ __global__ void __launch_bounds__(NT, 1)
     sh.cmax = okey(-INFINITY);
     sh.best = 0xFFFFFFFFu;
     tail_reset(sh);
+  } else if (tid == 64) {  // row parameters: loads issued while thread 0 still issues the bulk copies
     row_init(sh.row, p, row, slot, p.V);
   } else if (MODE == 0 && tid == 32) {
     sh.u = p.uniforms ? p.uniforms[row]
