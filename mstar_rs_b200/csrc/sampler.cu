@@ -609,8 +609,11 @@ __device__ __forceinline__ void for_each_value(const Slice &sl, const Cand *spec
   const float tq = fmaxf(theta, xlo);
   const uint32_t dlo = (uint32_t)(lo >> 32);
   const float xhi = dlo == 0 ? INFINITY : okey_inv(km - dlo);  // keys >= lo have x <= xhi
+  // the whole A range (keys 0 .. (km - okey(theta)) << 32 | ~0): x >= theta says it all
+  const bool whole = lo == 0 && (hi >> 32) == (uint64_t)(km - okey(theta)) && (uint32_t)hi == 0xFFFFFFFFu;
   auto in_range = [&](float x, uint32_t gid) {
     if (!(x >= tq && x <= xhi)) return false;
+    if (whole) return true;
     const uint64_t ck = ckey(km, x, gid);
     return ck >= lo && ck <= hi;
   };
@@ -1790,8 +1793,7 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
       }
       auto add = [&](float x, uint32_t gid, uint64_t w, bool valid) {
         if (!valid) return;
-        const uint64_t ck = ckey(km, x, gid);
-        const int b = cmd.shift < 0 ? vb_bin(vb, x) : (int)((ck - cmd.lo) >> cmd.shift);
+        const int b = cmd.shift < 0 ? vb_bin(vb, x) : (int)((ckey(km, x, gid) - cmd.lo) >> cmd.shift);
         atomicAdd(&hc[b], 1u);
         const uint32_t p0 = (uint32_t)w & 0x7FFu, p1 = (uint32_t)(w >> 11) & 0x7FFu, p2 = (uint32_t)(w >> 22);
         if (p0) atomicAdd(&hp[b], p0);
