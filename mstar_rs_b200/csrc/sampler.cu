@@ -166,6 +166,7 @@ struct CtaSh {
   uint32_t gstat[16];  // per-CTA status bits, pushed
   uint32_t gmin[16];   // per-CTA lowest id at the max (greedy / top-1), pushed
   uint32_t nloc;       // CTA-local candidate count
+  uint32_t scanned;    // vectors a full candidate scan covered before it stopped (0: no full scan)
   uint32_t runmax;     // okey of the raw running max the queue threshold follows
   uint32_t cmax;       // okey of the CTA max (transformed)
   uint32_t best;       // lowest id at the max (greedy / top-1)
@@ -1411,7 +1412,8 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
   uint32_t *rec = c.rec;
   Planner &P = sh.pl;
   // this CTA's values above its own threshold (counted by the first pass)
-  const bool dense_l1 = sh.nloc > (uint32_t)(sl.nvec * (Elem<T>::VEC / 4));
+  const uint32_t seen = sh.scanned ? sh.scanned * (uint32_t)Elem<T>::VEC : (uint32_t)sl.nvec * Elem<T>::VEC;
+  const bool dense_l1 = sh.nloc * 4u > seen;
   VBins vb;
   vb.m = m;
   vb.w = __fmul_rn(__fsub_rn(m, theta), 1.0f / NBIN);
@@ -1979,6 +1981,7 @@ __global__ void __launch_bounds__(NT, 1)
   }
   if (tid == 0) {
     sh.nloc = 0;
+    sh.scanned = 0;
     sh.qcount = 0;
     sh.status = 0;
     sh.n_spec = 0;
@@ -2335,7 +2338,16 @@ __global__ void __launch_bounds__(NT, 1)
       }
     };
     if (rescan) {
-      for (int k0 = 0; k0 < nvec; k0 += NT) scan_vec(k0 + tid, k0 + tid < nvec);
+      // once this CTA holds more candidates than it may push, the row takes
+      // the general path (which scans again): the warp stops, and the share
+      // of the slice it covered stays on record for that path's density
+      int k0 = 0;
+      for (; k0 < nvec; k0 += NT) {
+        const uint32_t held = __shfl_sync(~0u, *reinterpret_cast<volatile uint32_t *>(&sh.nloc), 0);
+        if (held > (uint32_t)capq) break;  // warp-uniform
+        scan_vec(k0 + tid, k0 + tid < nvec);
+      }
+      if (lane == 0) atomicAdd(&sh.scanned, (uint32_t)min(k0, nvec) / NWARP + 1u);
     } else {  // each warp drains its own queue
       const int nq = (int)min(wq, (uint32_t)WQCAP);
       for (int i0 = 0; i0 < nq; i0 += 32) scan_vec(i0 + lane < nq ? wqueue[i0 + lane] : 0, i0 + lane < nq);
