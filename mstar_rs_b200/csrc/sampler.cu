@@ -38,6 +38,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -2665,6 +2666,49 @@ static int sm_count() {
   return v;
 }
 
+template <typename T, int MODE>
+__global__ void sampler_kernel(const mstar_sampler_params_t p, const Plan pl, uint32_t *tp_send);
+
+// CTAs of the step kernel that can be resident at once with clusters of S
+// CTAs and smem bytes of dynamic shared memory each (clusters are placed
+// whole, inside one GPC, so the width decides how many SMs a wave can use);
+// 0 if the runtime cannot say.  Cached per configuration.
+static int resident_ctas(int dtype, int mode, int S, int smem) {
+  static std::mutex mu;
+  static int keys[64][4], vals[64], used = 0;
+  std::lock_guard<std::mutex> g(mu);
+  for (int i = 0; i < used; ++i)
+    if (keys[i][0] == dtype && keys[i][1] == mode && keys[i][2] == S && keys[i][3] == smem) return vals[i];
+  const void *fn = dtype == MSTAR_DTYPE_BF16
+                       ? (mode ? (const void *)sampler_kernel<__nv_bfloat16, 1> : (const void *)sampler_kernel<__nv_bfloat16, 0>)
+                       : (mode ? (const void *)sampler_kernel<float, 1> : (const void *)sampler_kernel<float, 0>);
+  int v = 0;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S, 1, 1);
+    cfg.blockDim = dim3(NT, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) == cudaSuccess) v = clusters * S;
+  }
+  cudaGetLastError();  // a refused query leaves no error behind
+  if (used < 64) {
+    keys[used][0] = dtype;
+    keys[used][1] = mode;
+    keys[used][2] = S;
+    keys[used][3] = smem;
+    vals[used++] = v;
+  }
+  return v;
+}
+
 static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Plan &pl) {
   const int es = p->dtype == MSTAR_DTYPE_BF16 ? 2 : 4;
   const int spec_max = (p->hist_ids ? p->H : (p->seen_bits ? (p->seen_cap > 0 ? p->seen_cap : 2048) : 0)) +
@@ -2711,6 +2755,23 @@ static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Pl
   for (int s = 1; s <= 16 && !smin; ++s)
     if (need(s, pl)) smin = s;
   if (!smin) return fail(MSTAR_ERR_UNSUPPORTED, "row too large for a 16-CTA cluster");
+  if ((int64_t)p->B * smin > (int64_t)sm_count() && smin < 8) {
+    // more than one wave: the portable width that keeps the most CTAs
+    // resident (ties: the narrower); e.g. clusters of 7 leave a fifth of
+    // the SMs idle where clusters of 8 do not
+    int best = smin, best_ctas = resident_ctas(p->dtype, mode, smin, pl.smem_bytes);
+    for (int s = smin + 1; s <= 8 && best_ctas > 0; ++s) {
+      Plan q;
+      if (!need(s, q)) continue;
+      const int c = resident_ctas(p->dtype, mode, s, q.smem_bytes);
+      if (c > best_ctas) {
+        best = s;
+        best_ctas = c;
+      }
+    }
+    need(best, pl);
+    return MSTAR_OK;
+  }
   int target = std::min(8, std::max(1, sm_count() / std::max(1, p->B)));
   target = (int)std::min<int64_t>(target, std::max<int64_t>(1, p->V / 8192));
   for (int s = std::max(smin, target); s > smin; --s)
