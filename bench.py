@@ -46,7 +46,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="qwen_mixed",
-                    choices=["qwen_mixed", "orpheus_single", "bucket", "constrained"])
+                    choices=["qwen_mixed", "orpheus_single", "bucket", "constrained", "tp"])
     ap.add_argument("--bucket", type=int, default=128)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cluster", type=int, default=0)
@@ -64,6 +64,8 @@ def make_case(args, rank):
         return W.orpheus_single(seed=args.seed + rank)
     if args.workload == "bucket":
         return W.bucket_sweep(args.bucket, seed=args.seed + rank)
+    if args.workload == "tp":  # the reference arm samples the whole row (vocab sharding is ours)
+        return W.tp_full(W.tp_sharded(1, seed=args.seed))
     return W.constrained(seed=args.seed + rank)
 
 
@@ -448,12 +450,78 @@ def run_e2e(args, case, d, dev, stream, world):
             "steps": n, "api": "mstar_rs_b200.sampling.Sampler.sample (eager)"}
 
 
+def run_tp(args, world, rank, local):
+    """Vocab-parallel sampling (B=128, V=152064 bf16 split evenly over the
+    ranks): each step is this rank's shard records, an NCCL all-gather of the
+    records and the merge that gives every rank the same ids.  Strong scaling:
+    the rows and the vocabulary are fixed, the ranks share the vocabulary."""
+    import torch
+
+    from mstar_rs_b200 import tp as TP
+    from mstar_rs_b200 import workloads as W
+
+    dev = torch.device("cuda", local)
+    shard = W.tp_sharded(world, seed=args.seed)[rank]
+    d = W.to_device(shard, device=dev)
+    base = d.pop("logits")
+    off = int(d.pop("vocab_offset", shard.vocab_offset) or 0)
+    V_global = shard.V * world
+    step_bytes = base.numel() * base.element_size()
+    nbuf = max(2, -(-2 * L2_BYTES // step_bytes))
+    bufs = [base] + [torch.roll(base, shifts=997 * i, dims=1).contiguous() for i in range(1, nbuf)]
+    B = shard.B
+    gather = None if world > 1 else (lambda recv, send: recv.copy_(send))
+    smp = TP.VocabParallelSampler(B, V_global, world, rank, dev, tp_cap=64, gather=gather)
+    out = torch.zeros(B, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        smp.sample(bufs[i % nbuf], off, out, **d)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    K = args.steps
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(K):
+        step(i)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        dist.barrier()
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": METRIC, "value": B * K / (ms / 1e3), "unit": "rows/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"tp{world}_b{B}_v{V_global}_bf16", "B": B, "V": V_global, "logits_dtype": "bf16",
+                   "history": int(shard.hist_ids.shape[1]), "parallelism": f"tp{world}",
+                   "launch": "eager: shard records, all-gather, merge per step",
+                   "l2": f"{nbuf} rotating shard buffers ({nbuf * step_bytes / 2**20:.0f} MiB > 2x L2)"},
+        "gpu_launches": 2 * K,
+    }), flush=True)
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.workload == "tp":
+            run_tp(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:
