@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define MSTAR_SAMPLER_ABI_VERSION 1
+#define MSTAR_SAMPLER_ABI_VERSION 2
 
 /* logits dtypes */
 #define MSTAR_DTYPE_F32 0
@@ -50,6 +50,7 @@ extern "C" {
 #define MSTAR_STATUS_SPECIAL_OVERFLOW 0x4u /* more penalised/biased ids than the table holds */
 #define MSTAR_STATUS_TP_OVERFLOW 0x8u  /* TP: a shard's candidate set exceeded tp_cap */
 #define MSTAR_STATUS_TIMEOUT 0x10u     /* a bounded wait on a bulk copy gave up */
+#define MSTAR_STATUS_STOP 0x20u        /* the sampled id is one of the slot's stop ids */
 
 /* return codes */
 #define MSTAR_OK 0
@@ -118,6 +119,17 @@ typedef struct mstar_sampler_params {
 
   uint32_t flags;
   int32_t cluster_size;      /* CTAs per row; 0 = automatic */
+
+  /* stop tokens (replaces the host-side `token == stop_token_id` test after
+   * every step, python/mstar_rs/models/orpheus.py:428-432, :518-519):
+   * stop_ids [num_slots, NS] global ids, id < 0 marks an unused entry, or
+   * NULL.  A row whose sampled id is one of its slot's stop ids gets
+   * MSTAR_STATUS_STOP in out_status and, when stop_flags [num_slots] is
+   * non-NULL, stop_flags[slot] = 1 (set only; the caller clears it). */
+  const int32_t *stop_ids;
+  int32_t NS;
+  int32_t pad1;
+  int32_t *stop_flags;
 } mstar_sampler_params_t;
 
 /* Library ABI version (MSTAR_SAMPLER_ABI_VERSION). */

@@ -12,7 +12,7 @@ import threading
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "_lib", "libmstar_sampler.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 DTYPE_F32, DTYPE_BF16 = 0, 1
 FLAG_UPDATE_HISTORY = 0x1
 FLAG_UPDATE_SEEN = 0x2
@@ -23,6 +23,7 @@ STATUS_GENERAL = 0x2
 STATUS_SPECIAL_OVERFLOW = 0x4
 STATUS_TP_OVERFLOW = 0x8
 STATUS_TIMEOUT = 0x10
+STATUS_STOP = 0x20
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
 
 P = ctypes.c_void_p
@@ -45,6 +46,7 @@ class Params(ctypes.Structure):
         ("out_ids", P), ("out_ids32", P), ("out_status", P),
         ("out_x", P), ("out_kept", P), ("out_probs", P),
         ("flags", U32), ("cluster_size", I32),
+        ("stop_ids", P), ("NS", I32), ("pad1", I32), ("stop_flags", P),
     ]
 
 

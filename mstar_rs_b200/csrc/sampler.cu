@@ -899,6 +899,15 @@ __device__ __forceinline__ uint32_t allowed32(const uint32_t *aw, int64_t nwords
 // State updates + scalar outputs for one row (called by one thread).
 __device__ __forceinline__ void write_row_outputs(const mstar_sampler_params_t &p, int row, int slot, uint32_t token,
                                                   uint32_t status) {
+  if (p.stop_ids) {
+    const int32_t *st = p.stop_ids + (int64_t)slot * p.NS;
+    bool hit = false;
+    for (int i = 0; i < p.NS; ++i) hit |= st[i] >= 0 && (uint32_t)st[i] == token;
+    if (hit) {
+      status |= MSTAR_STATUS_STOP;
+      if (p.stop_flags) p.stop_flags[slot] = 1;
+    }
+  }
   if (p.out_ids) p.out_ids[row] = (int64_t)token;
   if (p.out_ids32) p.out_ids32[row] = (int32_t)token;
   if (p.out_status) p.out_status[row] = (int32_t)status;
@@ -2643,6 +2652,8 @@ static int validate(const mstar_sampler_params_t *p) {
     return fail(MSTAR_ERR_INVALID, "UPDATE_HISTORY needs hist_ids");
   if ((p->flags & MSTAR_FLAG_UPDATE_SEEN) && !p->seen_bits)
     return fail(MSTAR_ERR_INVALID, "UPDATE_SEEN needs seen_bits");
+  if (p->stop_ids && p->NS < 1) return fail(MSTAR_ERR_INVALID, "NS must be >= 1 with stop_ids");
+  if (p->stop_flags && !p->stop_ids) return fail(MSTAR_ERR_INVALID, "stop_flags needs stop_ids");
   return MSTAR_OK;
 }
 

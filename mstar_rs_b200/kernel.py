@@ -43,7 +43,7 @@ def build_params(logits: torch.Tensor, *, slot_idx=None, num_slots=None, tempera
                  hist_len=None, seen_bits=None, seen_cap=0, bias_ids=None, bias_vals=None,
                  allowed_bits=None, uniforms=None, seed=None, offset=None, out_ids=None, out_ids32=None,
                  out_status=None, out_x=None, out_kept=None, out_probs=None, flags=0, cluster_size=0,
-                 vocab_offset=0) -> N.Params:
+                 vocab_offset=0, stop_ids=None, stop_flags=None) -> N.Params:
     if logits.dim() != 2:
         raise ValueError("logits must be [B, V]")
     if logits.dtype not in _DT:
@@ -74,6 +74,10 @@ def build_params(logits: torch.Tensor, *, slot_idx=None, num_slots=None, tempera
     _need(bias_ids, "bias_ids", torch.int32, dev, ns, 2)
     _need(bias_vals, "bias_vals", torch.float32, dev, ns, 2)
     _need(allowed_bits, "allowed_bits", torch.int32, dev, ns, 2)
+    _need(stop_ids, "stop_ids", torch.int32, dev, ns, 2)
+    _need(stop_flags, "stop_flags", torch.int32, dev, ns)
+    if stop_flags is not None and stop_ids is None:
+        raise ValueError("stop_flags needs stop_ids")
     _need(uniforms, "uniforms", torch.float32, dev, B)
     _need(out_ids, "out_ids", torch.int64, dev, B)
     _need(out_ids32, "out_ids32", torch.int32, dev, B)
@@ -107,6 +111,9 @@ def build_params(logits: torch.Tensor, *, slot_idx=None, num_slots=None, tempera
     p.out_x, p.out_kept, p.out_probs = _ptr(out_x), _ptr(out_kept), _ptr(out_probs)
     p.flags = flags
     p.cluster_size = cluster_size
+    p.stop_ids = _ptr(stop_ids)
+    p.NS = 0 if stop_ids is None else stop_ids.shape[1]
+    p.stop_flags = _ptr(stop_flags)
     return p
 
 

@@ -19,6 +19,12 @@ semantics those engines rely on:
       sync_seen_token_masks(masks)  orpheus.py:350, :426; qwen3_omni.py:518
   SeenTokenMask.new(rid, V, device) / add_tokens(tok)   orpheus.py:187, :500
 
+One addition: `SamplingConfig.stop_token_ids` (ignored under `ignore_eos`)
+lets the kernel flag the rows that sampled a stop token, so an engine reads
+one small flag vector per step (`Sampler.stopped`, `SamplerBuffers.stopped`)
+instead of reading every sampled id back to compare it with the stop id
+(orpheus.py:428-432, :518-519).
+
 Every sampling call runs the sm_100a kernel through the C ABI; nothing here
 computes a token on the host.  Greedy is temperature 0 (or top_k 1).  The
 in-graph sampler advances the per-row RNG offset and the seen-token bits on
@@ -50,6 +56,7 @@ class SamplingConfig:
     logit_bias: dict | None = None
     ignore_eos: bool = False
     seed: int | None = None
+    stop_token_ids: tuple | list | None = None
     _owner: object = field(default=None, repr=False, compare=False)
 
     def set_seed(self, seed) -> None:
@@ -95,6 +102,7 @@ class _ParamTable:
     """Host mirror + device copy of the per-slot parameter arrays."""
 
     NAMES = ("temperature", "top_p", "min_p", "rep_pen", "pres_pen", "freq_pen")
+    NSTOP = 4  # stop ids per slot
 
     def __init__(self, n: int, device):
         self.n = n
@@ -105,9 +113,11 @@ class _ParamTable:
         self.host["rep_pen"][:] = 1.0
         self.host_k = np.zeros(n, np.int32)
         self.host_seed = np.zeros(n, np.int64)
+        self.host_stop = np.full((n, self.NSTOP), -1, np.int32)
         self.dev = {k: torch.from_numpy(v.copy()).to(device) for k, v in self.host.items()}
         self.dev_k = torch.zeros(n, dtype=torch.int32, device=device)
         self.dev_seed = torch.zeros(n, dtype=torch.int64, device=device)
+        self.dev_stop = torch.full((n, self.NSTOP), -1, dtype=torch.int32, device=device)
         self.dirty = True
 
     def write(self, i: int, cfg: SamplingConfig) -> None:
@@ -121,6 +131,14 @@ class _ParamTable:
         self.host["freq_pen"][i] = cfg.frequency_penalty
         s = 0 if cfg.seed is None else cfg.seed
         self.host_seed[i] = np.int64(np.uint64(s & 0xFFFFFFFFFFFFFFFF).view(np.int64))
+        stops = () if cfg.ignore_eos or cfg.stop_token_ids is None else cfg.stop_token_ids
+        if isinstance(stops, int):
+            stops = (stops,)
+        stops = [int(t) for t in stops]
+        if len(stops) > self.NSTOP or any(t < 0 for t in stops):
+            raise ValueError(f"stop_token_ids takes at most {self.NSTOP} non-negative ids, got {stops}")
+        self.host_stop[i] = -1
+        self.host_stop[i, : len(stops)] = stops
         self.dirty = True
 
     def upload(self) -> None:
@@ -130,12 +148,13 @@ class _ParamTable:
             self.dev[k].copy_(torch.from_numpy(v))
         self.dev_k.copy_(torch.from_numpy(self.host_k))
         self.dev_seed.copy_(torch.from_numpy(self.host_seed))
+        self.dev_stop.copy_(torch.from_numpy(self.host_stop))
         self.dirty = False
 
     def kwargs(self) -> dict:
         return dict(temperature=self.dev["temperature"], top_k=self.dev_k, top_p=self.dev["top_p"],
                     min_p=self.dev["min_p"], rep_pen=self.dev["rep_pen"], pres_pen=self.dev["pres_pen"],
-                    freq_pen=self.dev["freq_pen"], seed=self.dev_seed)
+                    freq_pen=self.dev["freq_pen"], seed=self.dev_seed, stop_ids=self.dev_stop)
 
 
 class Sampler:
@@ -161,6 +180,7 @@ class Sampler:
         self.offset = torch.zeros(max_requests, dtype=torch.int64, device=self.device)
         self.hist = torch.full((max_requests, history), -1, dtype=torch.int32, device=self.device)
         self.hist_len = torch.zeros(max_requests, dtype=torch.int32, device=self.device)
+        self.stop_flags = torch.zeros(max_requests, dtype=torch.int32, device=self.device)
         self._slot: dict = {}
         self._free = list(range(max_requests - 1, -1, -1))
         self._sampling_config: dict = {}
@@ -182,6 +202,7 @@ class Sampler:
         self.params.write(s, cfg)
         self.offset[s] = 0
         self.hist_len[s] = 0
+        self.stop_flags[s] = 0
         self._idx_cache.clear()
 
     def set_config(self, rid, **kw) -> None:
@@ -231,7 +252,20 @@ class Sampler:
                             **self.params.kwargs(), offset=self.offset,
                             hist_ids=self.hist if apply_penalty else None,
                             hist_len=self.hist_len if apply_penalty else None,
-                            out_ids=out, flags=flags if apply_penalty else N.FLAG_ADVANCE_OFFSET)
+                            out_ids=out, stop_flags=self.stop_flags,
+                            flags=flags if apply_penalty else N.FLAG_ADVANCE_OFFSET)
+        return out
+
+    def stopped(self, rids) -> list:
+        """The requests among `rids` that have sampled one of their stop
+        tokens (one device read for all of them); their flags are cleared."""
+        if not rids:
+            return []
+        idx = self._index(rids).long()
+        hit = self.stop_flags.index_select(0, idx).tolist()
+        out = [r for r, h in zip(rids, hit) if h]
+        if out:
+            self.stop_flags.index_fill_(0, idx, 0)
         return out
 
 
@@ -261,8 +295,14 @@ class CudaGraphableSampler:
             kw.update(rep_pen=None, pres_pen=None, freq_pen=None)
         kernel.sampler_step(logits, num_slots=sb.max_bs, **kw, offset=sb.offset_buf,
                             seen_bits=sb.seen_tokens.buf, seen_cap=sb.seen_cap, out_ids=self.out,
-                            slot_idx=self.slot_idx, flags=N.FLAG_ADVANCE_OFFSET | N.FLAG_UPDATE_SEEN)
+                            slot_idx=self.slot_idx, stop_flags=sb.stop_flags,
+                            flags=N.FLAG_ADVANCE_OFFSET | N.FLAG_UPDATE_SEEN)
         return self.out
+
+    def stopped(self) -> list:
+        """The gathered requests that sampled a stop token since the flags
+        were last read (see SamplerBuffers.stopped)."""
+        return self.sbuf.stopped(self._rids)
 
     def sync_seen_token_masks(self, masks) -> None:
         """Copy the step rows' seen bits (updated in-graph) back to the
@@ -291,6 +331,8 @@ class SamplerBuffers:
         self.params = _ParamTable(max_bs, self.device)
         self.offset_buf = torch.zeros(max_bs, dtype=torch.int64, device=self.device)
         self.seen_tokens = _SeenTokens(max_bs, self.vocab_size, self.device)
+        self.stop_flags = torch.zeros(max_bs, dtype=torch.int32, device=self.device)  # per step row
+        self._rows: list = []
         self._cfg: dict = {}
         self._req_offset: dict = {}
         self._samplers: dict = {}
@@ -324,12 +366,30 @@ class SamplerBuffers:
         self.offset_buf[:n].copy_(offs)
         if not gather_seen_tokens:
             self.seen_tokens.buf[:n].zero_()
+        if list(rids) != self._rows:  # rows now hold other requests: their stop flags start clear
+            self.stop_flags.zero_()
+            self._rows = list(rids)
         s = self._samplers.get(n)
         if s is None:
             s = CudaGraphableSampler(self, n)
             self._samplers[n] = s
         s._rids = list(rids)
         return s
+
+    def stopped(self, rids) -> list:
+        """The requests among the gathered `rids` (row j = rids[j]) whose row
+        sampled one of their stop tokens in a step since the flags were last
+        read: one device read of the step rows' flags, which are then cleared.
+        The flags stay set across replays, so an engine may read them every
+        few steps instead of after every step."""
+        n = len(rids)
+        if n == 0:
+            return []
+        hit = self.stop_flags[:n].tolist()
+        out = [r for r, h in zip(rids, hit) if h]
+        if out:
+            self.stop_flags[:n].zero_()
+        return out
 
     def _store_offsets(self, rids) -> None:
         vals = self.offset_buf[: len(rids)].tolist()

@@ -192,3 +192,15 @@ def run_np(case: SamplerCase):
         res["ids"][r], res["status"][r] = tok, st
         res["x"][r], res["kept"][r], res["probs"][r] = x, kept, probs
     return res
+
+
+def stop_hits(ids, stop_ids) -> np.ndarray:
+    """Rows whose sampled id is one of their stop ids (entries < 0 unused).
+
+    Restates the engines' host-side stop test after a step,
+    `int(tok.item()) == self.cfg.stop_token_id` (python/mstar_rs/models/
+    orpheus.py:428-432, :518-519), widened to a short list of stop ids per
+    request; `ignore_eos` requests carry none.  ids [n], stop_ids [n, NS]."""
+    ids = np.asarray(ids, np.int64).reshape(-1, 1)
+    st = np.asarray(stop_ids, np.int64)
+    return ((st >= 0) & (st == ids)).any(axis=1)

@@ -38,7 +38,9 @@ def test_exports_every_declared_symbol(L):
 
 
 def test_abi_version(L):
-    assert L.mstar_sampler_abi_version() == 1
+    from mstar_rs_b200 import _native
+
+    assert L.mstar_sampler_abi_version() == _native.ABI_VERSION == 2
 
 
 def test_struct_layout_matches_header():
@@ -84,6 +86,42 @@ def test_invalid_arguments_rejected_on_host(L):
     p.ld = 100
     assert L.mstar_sampler_step(ctypes.byref(p), None) == _native.ERR_INVALID  # no uniforms / seed
     assert L.mstar_sampler_tp_record_words(50) == 104
+
+
+def test_stop_arguments_rejected_on_host(L):
+    from mstar_rs_b200 import _native
+
+    p = _native.Params()
+    p.logits, p.dtype, p.B, p.V, p.ld, p.num_slots = 0x1000, 0, 4, 100, 100, 4
+    p.uniforms, p.out_ids = 0x2000, 0x3000
+    p.stop_flags = 0x4000  # flags without ids
+    assert L.mstar_sampler_step(ctypes.byref(p), None) == _native.ERR_INVALID
+    assert b"stop_flags" in L.mstar_sampler_last_error()
+    p.stop_ids, p.NS = 0x5000, 0
+    assert L.mstar_sampler_step(ctypes.byref(p), None) == _native.ERR_INVALID
+    assert b"NS" in L.mstar_sampler_last_error()
+
+
+def test_stop_ids_in_the_parameter_table():
+    """SamplingConfig.stop_token_ids fill the per-slot stop table (-1 =
+    unused); ignore_eos clears them; more than the table holds is refused."""
+    import numpy as np
+
+    from mstar_rs_b200 import sampling
+
+    t = sampling._ParamTable(3, "cpu")
+    t.write(0, sampling.SamplingConfig(stop_token_ids=[7, 9]))
+    t.write(1, sampling.SamplingConfig(stop_token_ids=7, ignore_eos=True))
+    t.write(2, sampling.SamplingConfig(stop_token_ids=11))
+    np.testing.assert_array_equal(t.host_stop, [[7, 9, -1, -1], [-1] * 4, [11, -1, -1, -1]])
+    t.write(2, sampling.SamplingConfig())
+    np.testing.assert_array_equal(t.host_stop[2], [-1] * 4)
+    t.upload()
+    assert t.kwargs()["stop_ids"].tolist() == t.host_stop.tolist()
+    with pytest.raises(ValueError):
+        t.write(0, sampling.SamplingConfig(stop_token_ids=[1, 2, 3, 4, 5]))
+    with pytest.raises(ValueError):
+        t.write(0, sampling.SamplingConfig(stop_token_ids=[-3]))
 
 
 def test_python_front_end_rejects_cpu_tensors():

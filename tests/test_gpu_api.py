@@ -153,3 +153,104 @@ def test_graph_buckets_match_oracle(oracle_lib):
         np.testing.assert_array_equal(tok, oracle_lib.run(case)["ids"], err_msg=f"batch {batch}")
         for r in rb:
             step[r] += 1
+
+
+def test_stop_flags(oracle_lib):
+    """Stop tokens flagged on the device: the step's status bit, the eager
+    Sampler's per-request flags and the captured step's per-row flags all
+    equal the engines' host-side test (sampled id == a stop id) applied to
+    the oracle's ids; ignore_eos requests are never flagged."""
+    import torch
+
+    from mstar_rs_b200 import _native as N
+    from mstar_rs_b200 import kernel, sampling
+    from oracle.oracle import stop_hits
+
+    rng = np.random.default_rng(33)
+    n, V = 5, 3001
+    cfg = _cfg_rows(rng, n)
+    for k in ("rep_pen",):
+        cfg[k] = np.ones(n, np.float32)
+    for k in ("pres_pen", "freq_pen"):
+        cfg[k] = np.zeros(n, np.float32)
+    seeds = rng.integers(0, 2**62, n).astype(np.uint64)
+    xs = [(rng.standard_normal((n, V)) * 2).astype(np.float32) for _ in range(2)]
+    refs = [oracle_lib.run(Batch(logits=xs[s], **cfg, seed=seeds, offset=np.full(n, s, np.uint64)))["ids"]
+            for s in range(2)]
+    r0 = refs[0]
+    # row 0 hits, row 1 hits but ignores EOS, row 2 misses, row 3 hits on its
+    # second stop id, row 4 has none
+    stops = [[int(r0[0])], [int(r0[1])], [int((r0[2] + 1) % V)], [int((r0[3] + 7) % V), int(r0[3])], None]
+    ignore = [False, True, False, False, False]
+    table = np.full((n, 4), -1, np.int64)
+    for i, s in enumerate(stops):
+        if s and not ignore[i]:
+            table[i, : len(s)] = s
+
+    def config(i):
+        c = sampling.SamplingConfig(vocab_size=V, temperature=float(cfg["temperature"][i]),
+                                    top_k=int(cfg["top_k"][i]), top_p=float(cfg["top_p"][i]),
+                                    min_p=float(cfg["min_p"][i]), stop_token_ids=stops[i], ignore_eos=ignore[i])
+        c.set_seed(int(seeds[i]))
+        return c
+
+    # C ABI: the status bit
+    dev_x = torch.from_numpy(xs[0]).cuda()
+    t = {k: torch.from_numpy(v).cuda() for k, v in cfg.items()}
+    st = torch.zeros(n, dtype=torch.int32, device="cuda")
+    ids = torch.zeros(n, dtype=torch.int64, device="cuda")
+    flags = torch.zeros(n, dtype=torch.int32, device="cuda")
+    kernel.sampler_step(dev_x, **t, seed=torch.from_numpy(seeds.view(np.int64)).cuda(),
+                        offset=torch.zeros(n, dtype=torch.int64, device="cuda"),
+                        stop_ids=torch.from_numpy(table.astype(np.int32)).cuda(), stop_flags=flags,
+                        out_ids=ids, out_status=st)
+    np.testing.assert_array_equal(ids.cpu().numpy(), r0)
+    hit = stop_hits(r0, table)
+    assert hit.tolist() == [True, False, False, True, False]
+    np.testing.assert_array_equal((st.cpu().numpy() & N.STATUS_STOP) != 0, hit)
+    np.testing.assert_array_equal(flags.cpu().numpy(), hit.astype(np.int32))
+
+    # eager Sampler
+    smp = sampling.Sampler(device="cuda", history=16)
+    rids = [f"s{i}" for i in range(n)]
+    for i, r in enumerate(rids):
+        smp.add_request(r)
+        c = config(i)
+        smp.set_config(r, **{k: getattr(c, k) for k in ("vocab_size", "temperature", "top_k", "top_p", "min_p",
+                                                         "stop_token_ids", "ignore_eos")})
+        smp._sampling_config[r].set_seed(int(seeds[i]))
+    tok = smp.sample(rids, dev_x, apply_penalty=False).cpu().numpy()
+    np.testing.assert_array_equal(tok, r0)
+    assert smp.stopped(rids) == [r for r, h in zip(rids, hit) if h]
+    assert smp.stopped(rids) == []
+
+    # captured step: per-row flags stay set across replays until read
+    sbuf = sampling.SamplerBuffers.allocate(8, "cuda", vocab_size=V)
+    for i, r in enumerate(rids):
+        sbuf.register_request(r, config(i))
+    g_logits = torch.zeros(n, V, device="cuda")
+    sampler = sbuf.gather_for_request_ids(rids, n, gather_seen_tokens=False)
+    out = torch.zeros(n, dtype=torch.int64, device="cuda")
+
+    def dec():
+        out.copy_(sampler.sample(rids, g_logits, apply_penalty=True))
+
+    saved_off = sbuf.offset_buf[:n].clone()
+    torch.cuda.synchronize()
+    dec()
+    sbuf.offset_buf[:n].copy_(saved_off)
+    sbuf.seen_tokens.buf.zero_()
+    sbuf.stop_flags.zero_()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        dec()
+    torch.cuda.synchronize()
+    seen = np.zeros(n, bool)
+    for s in range(2):
+        g_logits.copy_(torch.from_numpy(xs[s]))
+        graph.replay()
+        np.testing.assert_array_equal(out.cpu().numpy(), refs[s], err_msg=f"replay {s}")
+        seen |= stop_hits(refs[s], table)
+    assert sampler.stopped() == [r for r, h in zip(rids, seen) if h]
+    assert sampler.stopped() == []

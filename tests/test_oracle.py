@@ -90,3 +90,11 @@ def test_oracle_statistics_small(oracle_lib):
     res = oracle_lib.run(b, debug=True)
     counts = np.bincount(res["ids"], minlength=V) / n
     np.testing.assert_allclose(counts, res["probs"][0], atol=2.0 / n)
+
+
+def test_stop_hits():
+    from oracle import oracle
+
+    ids = [5, 7, 0, 9]
+    st = [[5, -1], [-1, -1], [3, 0], [8, 10]]
+    assert oracle.stop_hits(ids, st).tolist() == [True, False, True, False]
