@@ -44,15 +44,25 @@ def test_tp_local_merge(oracle_lib, tp, cluster):
         got[:, 2] &= ~np.uint32(2)  # STATUS_GENERAL only says which path the shard took
         np.testing.assert_array_equal(got, _records_np(shards[q]), err_msg=f"shard {q} record")
         recv_all.append(send.clone())
+    from mstar_rs_b200 import _native as N
+    from oracle.oracle import stop_hits
+
+    # stop ids: even rows stop on the id they sample, odd rows on another id
+    stops = np.where(np.arange(B) % 2 == 0, ref, (ref + 1) % full.V).astype(np.int32).reshape(B, 1)
+    hits = stop_hits(ref, stops)
     for q, (smp, d) in enumerate(zip(samplers, devs)):
         out = torch.zeros(B, dtype=torch.int64, device="cuda")
         status = torch.zeros(B, dtype=torch.int32, device="cuda")
+        flags = torch.zeros(B, dtype=torch.int32, device="cuda")
         recv = smp.recv[: tp * B * smp.words]
         gather(recv, None)
-        smp.merge(d["_logits"], shards[q].vocab_offset, recv, out_ids=out, out_status=status, **d_params(d))
+        smp.merge(d["_logits"], shards[q].vocab_offset, recv, out_ids=out, out_status=status,
+                  stop_ids=torch.from_numpy(stops).cuda(), stop_flags=flags, **d_params(d))
         torch.cuda.synchronize()
         np.testing.assert_array_equal(out.cpu().numpy(), ref, err_msg=f"merge on shard {q}")
         assert not TP.status_overflowed(status).any().item()
+        np.testing.assert_array_equal((status.cpu().numpy() & N.STATUS_STOP) != 0, hits)
+        np.testing.assert_array_equal(flags.cpu().numpy(), hits.astype(np.int32))
 
 
 def d_params(d):
