@@ -121,6 +121,12 @@ class _ParamTable:
         self.dirty = True
 
     def write(self, i: int, cfg: SamplingConfig) -> None:
+        stops = () if cfg.ignore_eos or cfg.stop_token_ids is None else cfg.stop_token_ids
+        if isinstance(stops, int):
+            stops = (stops,)
+        stops = [int(t) for t in stops]
+        if len(stops) > self.NSTOP or any(t < 0 for t in stops):  # checked before any field changes
+            raise ValueError(f"stop_token_ids takes at most {self.NSTOP} non-negative ids, got {stops}")
         greedy = cfg.temperature < _SAMPLING_EPS
         self.host["temperature"][i] = 0.0 if greedy else cfg.temperature
         self.host_k[i] = 1 if greedy else int(cfg.top_k)
@@ -131,12 +137,6 @@ class _ParamTable:
         self.host["freq_pen"][i] = cfg.frequency_penalty
         s = 0 if cfg.seed is None else cfg.seed
         self.host_seed[i] = np.int64(np.uint64(s & 0xFFFFFFFFFFFFFFFF).view(np.int64))
-        stops = () if cfg.ignore_eos or cfg.stop_token_ids is None else cfg.stop_token_ids
-        if isinstance(stops, int):
-            stops = (stops,)
-        stops = [int(t) for t in stops]
-        if len(stops) > self.NSTOP or any(t < 0 for t in stops):
-            raise ValueError(f"stop_token_ids takes at most {self.NSTOP} non-negative ids, got {stops}")
         self.host_stop[i] = -1
         self.host_stop[i, : len(stops)] = stops
         self.dirty = True
@@ -207,11 +207,18 @@ class Sampler:
 
     def set_config(self, rid, **kw) -> None:
         cfg = self._sampling_config[rid]
-        for k, v in kw.items():
+        for k in kw:
             if not hasattr(cfg, k) or k.startswith("_"):
                 raise TypeError(f"unknown sampling option {k!r}")
+        old = {k: getattr(cfg, k) for k in kw}
+        for k, v in kw.items():
             setattr(cfg, k, v)
-        self.params.write(self._slot[rid], cfg)
+        try:
+            self.params.write(self._slot[rid], cfg)
+        except ValueError:
+            for k, v in old.items():  # a refused option leaves the request as it was
+                setattr(cfg, k, v)
+            raise
 
     def set_history(self, rid, ids) -> None:
         """Seed a request's generated-token history (penalty state)."""

@@ -119,7 +119,8 @@ def test_stop_ids_in_the_parameter_table():
     t.upload()
     assert t.kwargs()["stop_ids"].tolist() == t.host_stop.tolist()
     with pytest.raises(ValueError):
-        t.write(0, sampling.SamplingConfig(stop_token_ids=[1, 2, 3, 4, 5]))
+        t.write(0, sampling.SamplingConfig(temperature=0.5, stop_token_ids=[1, 2, 3, 4, 5]))
+    assert t.host["temperature"][0] == 1.0  # a refused config changes nothing
     with pytest.raises(ValueError):
         t.write(0, sampling.SamplingConfig(stop_token_ids=[-3]))
 
