@@ -469,6 +469,11 @@ class SamplerGraphBuckets:
         self._last = list(rids)
         return self._samplers[b].out[:n]
 
+    def stopped(self, rids) -> list:
+        """The requests of the last `sample` batch that sampled a stop token
+        (SamplerBuffers.stopped over the bucket's rows)."""
+        return self.sbuf.stopped(rids)
+
     def sync(self, rids, masks=None) -> None:
         sb = self.sbuf
         if masks is not None:

@@ -133,24 +133,31 @@ def test_graph_buckets_match_oracle(oracle_lib):
     cfg = _cfg_rows(rng, 8)
     seeds = rng.integers(0, 2**62, 8).astype(np.uint64)
     rids = [f"b{i}" for i in range(8)]
+    cfgs = {}
     for i, r in enumerate(rids):
         c = sampling.SamplingConfig(vocab_size=V, temperature=float(cfg["temperature"][i]),
                                     top_k=int(cfg["top_k"][i]), top_p=float(cfg["top_p"][i]),
                                     min_p=float(cfg["min_p"][i]))
         c.set_seed(int(seeds[i]))
         sbuf.register_request(r, c)
+        cfgs[r] = c
     gb = sampling.SamplerGraphBuckets(sbuf, buckets=(1, 2, 4, 8), dtype=torch.float32)
     gb.capture()
     step = {r: 0 for r in rids}
     for batch in ([0, 3, 5], [2], [1, 4, 6, 7, 0, 3]):
         rb = [rids[i] for i in batch]
         x = (rng.standard_normal((len(batch), V)) * 2).astype(np.float32)
-        tok = gb.sample(rb, torch.from_numpy(x).cuda()).cpu().numpy()
-        gb.sync(rb)
         case = Batch(logits=x, temperature=cfg["temperature"][batch], top_k=cfg["top_k"][batch],
                      top_p=cfg["top_p"][batch], min_p=cfg["min_p"][batch], seed=seeds[batch],
                      offset=np.array([step[r] for r in rb], np.uint64))
-        np.testing.assert_array_equal(tok, oracle_lib.run(case)["ids"], err_msg=f"batch {batch}")
+        ref = oracle_lib.run(case)["ids"]
+        # stop ids: rows at even positions stop on the id they will sample
+        for j, r in enumerate(rb):
+            cfgs[r].stop_token_ids = [int(ref[j]) if j % 2 == 0 else int((ref[j] + 1) % V)]
+        tok = gb.sample(rb, torch.from_numpy(x).cuda()).cpu().numpy()
+        gb.sync(rb)
+        np.testing.assert_array_equal(tok, ref, err_msg=f"batch {batch}")
+        assert gb.stopped(rb) == rb[::2], f"batch {batch}"
         for r in rb:
             step[r] += 1
 
