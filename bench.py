@@ -502,11 +502,37 @@ def run_tp(args, world, rank, local):
         dist.barrier()
     torch.cuda.synchronize(dev)
     K = args.steps
+    # One rank: the exchange is a device copy, so the whole step is captured
+    # once per buffer cycle and replayed (as a decode graph would hold it).
+    # More ranks: eager steps, the NCCL all-gather issued from the host.
+    graphs = []
+    if world == 1:
+        reps, rem = divmod(K, nbuf)
+        cap = torch.cuda.Stream(device=dev)
+        cap.wait_stream(stream)
+        for n in (nbuf, rem):
+            if n == 0:
+                continue
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                for i in range(n):
+                    step(i)
+            graphs.append(g)
+        stream.wait_stream(cap)
+        for g in graphs:  # graph warm-up (uploads the graphs)
+            g.replay()
+        torch.cuda.synchronize(dev)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for i in range(K):
-        step(i)
+    if graphs:
+        for _ in range(reps):
+            graphs[0].replay()
+        if rem:
+            graphs[-1].replay()
+    else:
+        for i in range(K):
+            step(i)
     t1.record(stream)
     torch.cuda.synchronize(dev)
     ms = t0.elapsed_time(t1)
@@ -523,7 +549,8 @@ def run_tp(args, world, rank, local):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"tp{world}_b{B}_v{V_global}_bf16", "B": B, "V": V_global, "logits_dtype": "bf16",
                    "history": int(shard.hist_ids.shape[1]), "parallelism": f"tp{world}",
-                   "launch": "eager: shard records, all-gather, merge per step",
+                   "launch": ("CUDA graph replay: shard records, exchange copy, merge per step" if graphs
+                              else "eager: shard records, NCCL all-gather, merge per step"),
                    "l2": f"{nbuf} rotating shard buffers ({nbuf * step_bytes / 2**20:.0f} MiB > 2x L2)"},
         "gpu_launches": 2 * K,
     }), flush=True)
