@@ -132,3 +132,40 @@ def test_python_front_end_rejects_cpu_tensors():
 
     with pytest.raises(ValueError, match="CUDA"):
         kernel.build_params(torch.zeros(2, 10))
+
+
+def _plan(L, B, V, dtype, H=0, cluster_size=0):
+    from mstar_rs_b200 import _native
+
+    p = _native.Params()
+    p.logits, p.dtype, p.B, p.V, p.ld, p.num_slots = 0x1000, dtype, B, V, V, B
+    p.uniforms, p.out_ids = 0x2000, 0x3000  # never dereferenced by the planner
+    if H:
+        p.hist_ids, p.hist_len, p.H = 0x4000, 0x5000, H
+    p.cluster_size = cluster_size
+    cs, sm = _native.I32(), _native.I64()
+    rc = L.mstar_sampler_plan(ctypes.byref(p), ctypes.byref(cs), ctypes.byref(sm))
+    return rc, cs.value, sm.value
+
+
+def test_planner_cluster_widths(L):
+    """The launch planner (no GPU needed): single-wave grids widen each row's
+    cluster while SMs would sit idle; a grid of several waves keeps a width
+    that holds the row; an explicit width is honoured or refused."""
+    from mstar_rs_b200 import _native
+
+    optin = 227 * 1024
+    # headline: 64 bf16 rows of 151936 with 1024-token histories -> pairs (128 CTAs)
+    assert _plan(L, 64, 151936, _native.DTYPE_BF16, H=1024) == (0, 2, 223104)
+    # one f32 row (Orpheus) and eight (bucket of 8): eight CTAs per row
+    rc, s, smem = _plan(L, 1, 156940, _native.DTYPE_F32, H=256)
+    assert (rc, s) == (0, 8) and smem <= optin
+    rc, s, smem = _plan(L, 8, 128256, _native.DTYPE_F32)
+    assert (rc, s) == (0, 8) and smem <= optin
+    # 128 f32 rows: more than one wave; the narrowest width that fits is 3
+    rc, s, smem = _plan(L, 128, 128256, _native.DTYPE_F32)
+    assert rc == 0 and 3 <= s <= 8 and smem <= optin
+    assert _plan(L, 128, 128256, _native.DTYPE_F32, cluster_size=3) == (0, 3, 229888)
+    # a whole f32 row does not fit one CTA; widths above 16 are invalid
+    assert _plan(L, 8, 128256, _native.DTYPE_F32, cluster_size=1)[0] == _native.ERR_UNSUPPORTED
+    assert _plan(L, 8, 128256, _native.DTYPE_F32, cluster_size=17)[0] == _native.ERR_INVALID
