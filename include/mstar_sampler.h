@@ -43,14 +43,17 @@ extern "C" {
 #define MSTAR_FLAG_UPDATE_SEEN 0x2u    /* set the sampled id's bit in seen_bits */
 #define MSTAR_FLAG_ADVANCE_OFFSET 0x4u /* offset[slot] += 1 after the draw */
 #define MSTAR_FLAG_FORCE_GENERAL 0x8u  /* testing: take the multi-round selection path */
+#define MSTAR_FLAG_TEST_WITHHOLD 0x10u /* testing: leave each CTA's last bulk copy unissued, so its
+                                          bounded wait (2 ms) runs out: MSTAR_STATUS_TIMEOUT */
 
 /* per-row status bits written to out_status */
 #define MSTAR_STATUS_EMPTY 0x1u        /* no token had positive weight; id 0 returned */
 #define MSTAR_STATUS_GENERAL 0x2u      /* row took the multi-round selection path */
 #define MSTAR_STATUS_SPECIAL_OVERFLOW 0x4u /* more penalised/biased ids than the table holds */
 #define MSTAR_STATUS_TP_OVERFLOW 0x8u  /* TP: a shard's candidate set exceeded tp_cap */
-#define MSTAR_STATUS_TIMEOUT 0x10u     /* a bounded wait on a bulk copy gave up */
+#define MSTAR_STATUS_TIMEOUT 0x10u     /* a bounded wait (2 ms) on a bulk copy gave up; the id is not valid */
 #define MSTAR_STATUS_STOP 0x20u        /* the sampled id is one of the slot's stop ids */
+#define MSTAR_STATUS_BAD_RECORD 0x40u  /* TP merge: a record entry held an id >= V_global (left out) */
 
 /* return codes */
 #define MSTAR_OK 0
@@ -84,7 +87,8 @@ typedef struct mstar_sampler_params {
    *   token history  hist_ids [num_slots, H] (global ids, ring of the last H
    *                  generated tokens) + hist_len [num_slots]
    *   seen bitmask   seen_bits [num_slots, seen_words] (bit g&31 of word g>>5)
-   * seen_cap bounds the set bits per row the kernel accepts (0 = 2048). */
+   * Any number of bits may be set.  seen_cap is not read (kept so the layout
+   * of this struct stays the same). */
   int32_t *hist_ids;
   int32_t *hist_len;
   int32_t H;

@@ -18,12 +18,14 @@ FLAG_UPDATE_HISTORY = 0x1
 FLAG_UPDATE_SEEN = 0x2
 FLAG_ADVANCE_OFFSET = 0x4
 FLAG_FORCE_GENERAL = 0x8
+FLAG_TEST_WITHHOLD = 0x10
 STATUS_EMPTY = 0x1
 STATUS_GENERAL = 0x2
 STATUS_SPECIAL_OVERFLOW = 0x4
 STATUS_TP_OVERFLOW = 0x8
 STATUS_TIMEOUT = 0x10
 STATUS_STOP = 0x20
+STATUS_BAD_RECORD = 0x40
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
 
 P = ctypes.c_void_p

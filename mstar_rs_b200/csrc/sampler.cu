@@ -82,7 +82,10 @@ static_assert(TAIL_CAP * 44 + NBK * 12 <= LEAN_SCRATCH, "fast tail scratch");
 static_assert(NBK % NT == 0, "tail bucket scan");
 static_assert(NBK >= 2 * 256 && NBK >= NT, "value-bucket tail: counts and starts over the bucket counts, weights over the masses");
 static_assert(NT == 512, "the rank sort splits 512 threads into 64 / 128 / 256 slots");
-constexpr unsigned kWaitLimit = 1u << 24;
+// Bound on one wait for a bulk copy: 2 ms of %globaltimer (a copy of at
+// most 32 KB lands within microseconds), with an iteration cap behind it.
+constexpr uint64_t kWaitNs = 2000000ull;
+constexpr unsigned kWaitIters = 1u << 26;
 
 struct __align__(8) Cand {
   float x;
@@ -96,6 +99,7 @@ struct Plan {
   int64_t slice;       // elements per CTA slice
   int32_t data_bytes;  // slice data (>= LEAN_SCRATCH: reused by the fast tail)
   int32_t map_bytes;   // skip bitmap (one bit per resident position)
+  int32_t seen_map;    // 1: a seen map of the same size follows the skip bitmap
   int32_t ht_cap;      // hash table slots (power of two)
   int32_t spec_cap;    // special list entries
   int32_t off_work, off_spec, off_lcand, off_bias;
@@ -187,6 +191,7 @@ struct CtaSh {
   uint32_t goff[16], gcnt[16];
   uint32_t min_all;
   int nemit;
+  int kcut_bin;         // candidates: value bin of this CTA's K-th largest (top_k cut)
   Row row;
   int tp_ovf;
   int bcast_i;
@@ -253,18 +258,28 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                : "memory");
 }
 
-// Bounded wait on phase `parity`; false if the limit ran out.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on phase `parity` (kWaitNs); false if the limit ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
-  for (unsigned i = 0; i < kWaitLimit; ++i) {
+  uint64_t t0 = 0;
+  for (unsigned i = 0; i < kWaitIters; ++i) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000000;\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
         : "r"(a), "r"(parity)
         : "memory");
     if (ok) return true;
+    const uint64_t t = global_ns();
+    if (i == 0) t0 = t;
+    else if (t - t0 > kWaitNs) return false;
   }
   return false;
 }
@@ -579,7 +594,52 @@ struct Slice {
   const uint8_t *skip;
   int nvec;
   int64_t pos0_gid;
+  const uint32_t *seen;  // seen map (seen-bit mode) or NULL
+  int map_words;         // words of the skip and seen maps
+  const uint8_t *rowp;   // the row in global memory
+  int64_t c0al;          // row position of data position 0
 };
+
+// Final value of a seen-mask special at data position pos (count 1; no
+// bias: bias ids are in the materialized list), from the resident data or,
+// with rowp, from global memory.  Same operations as the list's finalize.
+template <typename T>
+__device__ __forceinline__ float seen_x(const Slice &sl, int pos, const Row &r, bool from_global) {
+  float v = from_global ? Elem<T>::load(sl.rowp, sl.c0al + pos)
+                        : Elem<T>::smem_elem(reinterpret_cast<const uint8_t *>(sl.data), pos);
+  v = (v > 0.0f) ? __fdiv_rn(v, r.R) : __fmul_rn(v, r.R);
+  v = __fsub_rn(v, __fmul_rn(r.F, 1.0f));
+  v = __fsub_rn(v, r.Pp);
+  return v != v ? v : (r.greedy ? v : __fmul_rn(v, r.invT));
+}
+
+// The seen-mask specials of the slice as a list that is never materialized:
+// every set bit of the seen map (a seen, allowed id that is not a bias id)
+// is visited and its final value computed on the spot, so the number of
+// seen ids a row may carry is not bounded by a shared-memory list.
+// fn(c, valid) is called by all 32 lanes of each participating warp (the
+// threads t0 = 0 .. stride-1 of the group, whole warps); no barrier.
+template <typename T, typename F>
+__device__ __forceinline__ void for_each_seen(const Slice &sl, const Row &r, bool from_global, int t0, int stride,
+                                              F &&fn) {
+  if (!sl.seen) return;
+  const int lane = threadIdx.x & 31;
+  for (int w0 = t0 & ~31; w0 < sl.map_words; w0 += stride) {  // warp-uniform
+    const int wi = w0 + lane;
+    uint32_t bits = wi < sl.map_words ? sl.seen[wi] : 0u;
+    while (__any_sync(~0u, bits != 0u)) {
+      const bool valid = bits != 0u;
+      Cand c{-INFINITY, 0u};
+      if (valid) {
+        const int pos = wi * 32 + __ffs(bits) - 1;
+        bits &= bits - 1u;
+        c.x = seen_x<T>(sl, pos, r, from_global);
+        c.gid = (uint32_t)(sl.pos0_gid + pos);
+      }
+      fn(c, valid);
+    }
+  }
+}
 
 template <typename T>
 __device__ __forceinline__ uint4 load_masked(const Slice &sl, int k) {
@@ -678,6 +738,11 @@ __device__ __forceinline__ void for_each_value(const Slice &sl, const Cand *spec
     const uint64_t w = weight_A(r, c.x, m);
     fn(c.x, c.gid, w, in && w != 0);
   }
+  for_each_seen<T>(sl, r, false, threadIdx.x, NT, [&](const Cand &c, bool valid) {
+    const bool in = valid && in_range(c.x, c.gid);
+    const uint64_t w = weight_A(r, c.x, m);
+    fn(c.x, c.gid, w, in && w != 0);
+  });
 }
 
 // ------------------------------------------------------------- fast tail
@@ -806,6 +871,7 @@ __device__ __forceinline__ uint64_t S_excl(const uint64_t *S, int j) { return j 
 struct Layout {
   uint8_t *data;
   uint8_t *skip;
+  uint32_t *seen;  // seen-bit mode: seen, allowed, non-bias positions (or NULL)
   int2 *ht;    // {pos, count | HT_MASKED}
   int *queue;  // [QCAP] vector indices queued by the first scan
   Cand *spec;
@@ -828,15 +894,18 @@ __device__ __forceinline__ Layout make_layout(uint8_t *smem, const Plan &pl) {
   L.data = smem;
   L.work = smem + pl.off_work;
   L.skip = L.work;
-  L.ht = reinterpret_cast<int2 *>(L.work + pl.map_bytes);
-  L.queue = reinterpret_cast<int *>(L.work + pl.map_bytes + pl.ht_cap * 8);
+  L.seen = pl.seen_map ? reinterpret_cast<uint32_t *>(L.work + pl.map_bytes) : nullptr;
+  uint8_t *const maps_end = L.work + pl.map_bytes * (pl.seen_map ? 2 : 1);
+  L.ht = reinterpret_cast<int2 *>(maps_end);
+  L.queue = reinterpret_cast<int *>(maps_end + pl.ht_cap * 8);
   L.spec = reinterpret_cast<Cand *>(smem + pl.off_spec);
   L.lcand = reinterpret_cast<Cand *>(smem + pl.off_lcand);
   L.bias_id = reinterpret_cast<int32_t *>(smem + pl.off_bias);
   L.bias_val = reinterpret_cast<float *>(smem + pl.off_bias + BIAS_SMEM * 4);
-  // general-path area: after the skip bitmap (which every scan still reads),
-  // over the hash table and the first scan's queue, dead by then
-  uint8_t *g = L.work + pl.map_bytes;
+  // general-path area: after the skip bitmap and the seen map (which every
+  // scan still reads), over the hash table and the first scan's queue, dead
+  // by then
+  uint8_t *g = maps_end;
   L.l1c = reinterpret_cast<uint32_t *>(g);
   L.l1p = reinterpret_cast<uint32_t *>(g + NBIN * 4);
   L.l1m = reinterpret_cast<uint64_t *>(g + NBIN * 4);
@@ -1867,7 +1936,10 @@ __device__ __forceinline__ void debug_dense(const RowCtx &c, CtaSh &sh) {
       if (res.greedy) {
         kept = gid == res.token;
         prob = kept ? 1.0f : 0.0f;
-      } else if (x > -INFINITY && x <= res.m && ckey(kmm, x, gid) <= res.ckK) {
+      } else if (x > -INFINITY && x <= res.m && ckey(kmm, x, gid) <= res.ckK && weight_A(r, x, res.m) != 0) {
+        // (kept members are members of A: positive weight, past min_p; the
+        // last kept key alone does not say that for keys between theta and
+        // the A boundary)
         kept = true;
         prob = (float)__ddiv_rn((double)spec_w_from_e(spec_e(x, res.m)), (double)res.WK);
       }
@@ -1888,6 +1960,11 @@ __device__ __forceinline__ void debug_dense(const RowCtx &c, CtaSh &sh) {
   }
   __syncthreads();
   for (int i = threadIdx.x; i < c.nspec; i += NT) emit((int64_t)c.L.spec[i].gid - c.gbase, c.L.spec[i].x);
+  // seen-mask ids from global memory (the leader's resident slice may hold
+  // the tail's scratch by now)
+  for_each_seen<T>(c.sl, r, true, threadIdx.x, NT, [&](const Cand &cd, bool valid) {
+    if (valid) emit((int64_t)cd.gid - c.gbase, cd.x);
+  });
 }
 
 template <typename T, int MODE>
@@ -1938,7 +2015,10 @@ __global__ void __launch_bounds__(NT, 1)
   if (tid == 0) {
     for (int j = 0; j < nchunk; ++j) mbar_init(&sh.mbar[j], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int j = 0; j < nchunk; ++j) {
+    // (testing: with MSTAR_FLAG_TEST_WITHHOLD the last copy is never issued
+    // and its barrier never completes, so its waits run out)
+    const int nissue = (p.flags & MSTAR_FLAG_TEST_WITHHOLD) ? nchunk - 1 : nchunk;
+    for (int j = 0; j < nissue; ++j) {
       const uint32_t bytes = (uint32_t)min((int64_t)CHUNK_BYTES, nbulk - (int64_t)j * CHUNK_BYTES);
       mbar_expect_tx(&sh.mbar[j], bytes);
       bulk_g2s(L.data + (b0 - a_al) + (int64_t)j * CHUNK_BYTES,
@@ -2020,21 +2100,25 @@ __global__ void __launch_bounds__(NT, 1)
   uint32_t *skip32 = reinterpret_cast<uint32_t *>(L.skip);
   if (has_spec)
     for (int i = tid; i < pl.ht_cap; i += NT) L.ht[i] = make_int2(-1, 0);
-  if (p.allowed_bits) {
-    const uint32_t *aw = p.allowed_bits + (int64_t)slot * p.allowed_words;
+  if (p.allowed_bits || p.seen_bits) {
+    // word by word: disallowed positions, and (seen-bit mode) the seen ones,
+    // which also go into the seen map unless disallowed
+    const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)slot * p.allowed_words : nullptr;
+    const uint32_t *sw = p.seen_bits ? p.seen_bits + (int64_t)slot * p.seen_words : nullptr;
     for (int wi = tid; wi < map_words; wi += NT) {
       const int64_t e0 = c0al + (int64_t)wi * 32;
       const int64_t lo_in = min((int64_t)32, max((int64_t)0, c0 - e0));
       const int64_t hi_in = min((int64_t)32, max((int64_t)0, c1 - e0));
-      uint32_t dis = 0u;
+      uint32_t dis = 0u, sn = 0u;
       if (hi_in > lo_in) {
         const uint32_t hm = hi_in == 32 ? ~0u : ((1u << hi_in) - 1u);
         const uint32_t lm = lo_in == 32 ? ~0u : ((1u << lo_in) - 1u);
         const uint32_t inmask = hm & ~lm;
-        const uint32_t bits = allowed32(aw, p.allowed_words, gbase + e0 + lo_in) << lo_in;
-        dis = inmask & ~bits;
+        if (aw) dis = inmask & ~(allowed32(aw, p.allowed_words, gbase + e0 + lo_in) << lo_in);
+        if (sw) sn = inmask & ~dis & (allowed32(sw, p.seen_words, gbase + e0 + lo_in) << lo_in);
       }
-      skip32[wi] = dis;
+      skip32[wi] = dis | sn;
+      if (L.seen) L.seen[wi] = sn;
     }
   } else {
     uint4 *s4 = reinterpret_cast<uint4 *>(L.skip);
@@ -2085,11 +2169,18 @@ __global__ void __launch_bounds__(NT, 1)
     if (created < 0) {
       sh.ht_fail = 1;
     } else if (created) {
-      if (!mark_first) {
-        const int64_t pos = e - c0al;
-        const uint32_t bit = 1u << (pos & 31);
-        if (atomicOr(&skip32[pos >> 5], bit) & bit) atomicOr(&L.ht[h].y, HT_MASKED);
+      const int64_t pos = e - c0al;
+      const uint32_t bit = 1u << (pos & 31);
+      // seen-bit mode: a bias id that is also seen takes its count (1) here
+      // and leaves the seen map, so it is visited once, from the list
+      bool seen_here = false;
+      if (L.seen) {
+        seen_here = (atomicAnd(&L.seen[pos >> 5], ~bit) & bit) != 0u;
+        if (seen_here) atomicAdd(&L.ht[h].y, 1);
       }
+      // an already set skip bit of a position that is not seen means the
+      // mask disallows it (seen positions in the map are allowed)
+      if (!mark_first && (atomicOr(&skip32[pos >> 5], bit) & bit) && !seen_here) atomicOr(&L.ht[h].y, HT_MASKED);
       new_entry(h);
     }
   };
@@ -2097,27 +2188,15 @@ __global__ void __launch_bounds__(NT, 1)
     const int64_t pos = e - c0al;
     atomicOr(&skip32[pos >> 5], 1u << (pos & 31));
   };
-  // fn(e, count) for every special occurrence of this slice (e = position in the row)
+  // fn(e, count) for every materialized special occurrence of this slice
+  // (e = position in the row): history ids and bias ids.  Seen-mask ids
+  // are in the seen map (and the skip bitmap) already.
   auto for_each_special = [&](auto &&fn) {
     if (has_hist) {
       const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
       for (int j = tid, u = 0; j < hlen; j += NT, ++u) {
         const int64_t g = (int64_t)(u < HP ? (u == 0 ? hpre[0] : hpre[1]) : h[j]) - gbase;
         if (g >= c0 && g < c1) fn(g, 1);
-      }
-    } else if (p.seen_bits) {
-      const uint32_t *sw = p.seen_bits + (int64_t)slot * p.seen_words;
-      const int64_t g0 = gbase + c0, g1 = gbase + c1;
-      if (g1 > g0) {
-        for (int64_t w = (g0 >> 5) + tid; w <= ((g1 - 1) >> 5); w += NT) {
-          uint32_t bits = sw[w];
-          while (bits) {
-            const int b = __ffs(bits) - 1;
-            bits &= bits - 1;
-            const int64_t g = (w << 5) + b;
-            if (g >= g0 && g < g1) fn(g - gbase, 1);
-          }
-        }
       }
     }
     if (p.bias_ids && p.bias_vals) {
@@ -2138,7 +2217,7 @@ __global__ void __launch_bounds__(NT, 1)
     __syncthreads();  // bitmap, table and special list entries complete
   }
   const Row r = sh.row;
-  const Slice sl{data4, L.skip, nvec, pos0_gid};
+  const Slice sl{data4, L.skip, nvec, pos0_gid, L.seen, map_words, rowp, c0al};
   const bool one = r.greedy || r.K == 1;
 
   // ---- pass A, block by block as the bulk copies land: masked raw max; a
@@ -2244,6 +2323,9 @@ __global__ void __launch_bounds__(NT, 1)
       L.spec[i] = Cand{x, (uint32_t)(ent.x + gbase)};
       spec_max = fmaxf(spec_max, x);
     }
+    for_each_seen<T>(sl, r, false, t0, stride, [&](const Cand &c, bool valid) {
+      if (valid) spec_max = fmaxf(spec_max, c.x);
+    });
   };
   {
     // blocks in order: bulk chunk 0 (it sets the threshold), the fringe
@@ -2316,6 +2398,71 @@ __global__ void __launch_bounds__(NT, 1)
                         (thq > -INFINITY && !(xform(r, prev_float(thq)) < tcut));
     Cand *const lead = cluster.map_shared_rank(L.lcand, 0) + rank * capq;
     uint32_t best = 0xFFFFFFFFu;
+    // A top_k row whose queue overflowed (far more candidates than this CTA
+    // may push): the row's K largest are among every CTA's own K largest, so
+    // the push may leave out what lies below the value bin holding this CTA's
+    // K-th largest candidate (bin b holds E(b+1) < x <= E(b), E(b) = cm - b w,
+    // w = (cm - theta) / NBIN).  One histogram pass over the resident slice
+    // and the specials finds that bin; the queue's memory holds the counts
+    // (a rescan does not read the queue).  Ties at the cut are all pushed.
+    bool kcut = false;
+    float kcut_x = -INFINITY;  // pushed: x > kcut_x (with kcut)
+    if (!one && r.topk && r.K <= capq && rescan &&
+        __any_sync(~0u, lane < NWARP && sh.wqn[lane] > (uint32_t)WQCAP)) {  // CTA-uniform
+      VBins vb;
+      vb.m = cm;
+      vb.w = __fmul_rn(__fsub_rn(cm, theta_l), 1.0f / NBIN);
+      vb.iw = 1.0f / vb.w;
+      if (vb.w > 0.0f && vb.w < INFINITY && vb.iw < INFINITY) {  // CTA-uniform
+        uint32_t *hist = reinterpret_cast<uint32_t *>(L.queue);
+        for (int i = tid; i < NBIN; i += NT) hist[i] = 0u;
+        __syncthreads();
+        for (int k = tid; k < nvec; k += NT) {
+          const uint4 v = load_masked<T>(sl, k);
+          if (!(xform(r, Elem<T>::vmax(v)) >= theta_l)) continue;
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            const float x = xform(r, Elem<T>::get(v, j));
+            if (x >= theta_l) atomicAdd(&hist[vb_bin(vb, x)], 1u);
+          }
+        }
+        for (int i = tid; i < nspec; i += NT) {
+          const float x = L.spec[i].x;
+          if (x >= theta_l) atomicAdd(&hist[vb_bin(vb, x)], 1u);
+        }
+        for_each_seen<T>(sl, r, false, tid, NT, [&](const Cand &c, bool valid) {
+          if (valid && c.x >= theta_l) atomicAdd(&hist[vb_bin(vb, c.x)], 1u);
+        });
+        __syncthreads();
+        if (tid < 32) {  // the first bin where the count from the top reaches K
+          constexpr int PER = NBIN / 32;
+          uint32_t s = 0;
+          for (int i = 0; i < PER; ++i) s += hist[lane * PER + i];
+          uint32_t inc = s;
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(~0u, inc, o);
+            if (lane >= o) inc += t;
+          }
+          const unsigned reach = __ballot_sync(~0u, inc >= (uint32_t)r.K);
+          int bk = NBIN - 1;
+          if (reach && lane == __ffs(reach) - 1) {
+            uint32_t c = inc - s;
+            for (bk = lane * PER; bk < (lane + 1) * PER - 1; ++bk) {
+              c += hist[bk];
+              if (c >= (uint32_t)r.K) break;
+            }
+          }
+          bk = __shfl_sync(~0u, bk, reach ? __ffs(reach) - 1 : 0);
+          if (lane == 0) sh.kcut_bin = reach ? bk : NBIN - 1;
+        }
+        __syncthreads();
+        const int bk = sh.kcut_bin;
+        if (bk < NBIN - 1) {
+          kcut = true;
+          kcut_x = vb_edge(vb, bk + 1);
+        }
+      }
+    }
     // one vector per lane per step (warp-uniform step count); the passing
     // values are appended with one atomic per warp
     auto scan_vec = [&](int k, bool valid) {
@@ -2333,7 +2480,7 @@ __global__ void __launch_bounds__(NT, 1)
           const float x = xform(r, Elem<T>::get(v, j));
           if (one) {
             if (x == cm) best = min(best, gid0 + (uint32_t)j);
-          } else if (x >= theta_l) {
+          } else if (x >= theta_l && (!kcut || x > kcut_x)) {
             pm |= 1u << j;
           }
         }
@@ -2362,19 +2509,22 @@ __global__ void __launch_bounds__(NT, 1)
       const int nq = (int)min(wq, (uint32_t)WQCAP);
       for (int i0 = 0; i0 < nq; i0 += 32) scan_vec(i0 + lane < nq ? wqueue[i0 + lane] : 0, i0 + lane < nq);
     }
+    auto push_special = [&](const Cand &c, bool valid) {  // all 32 lanes
+      if (one) {
+        if (valid && c.x == cm) best = min(best, c.gid);
+        return;
+      }
+      const bool pass = valid && c.x >= theta_l && (!kcut || c.x > kcut_x);
+      if (!__any_sync(~0u, pass)) return;
+      const uint32_t o = warp_reserve(&sh.nloc, pass ? 1u : 0u);
+      if (pass && o < (uint32_t)capq) lead[o] = c;
+    };
     for (int i0 = 0; i0 < nspec; i0 += NT) {
       const int i = i0 + tid;
       const bool valid = i < nspec;
-      const Cand c = valid ? L.spec[i] : Cand{-INFINITY, 0u};
-      if (one) {
-        if (valid && c.x == cm) best = min(best, c.gid);
-        continue;
-      }
-      const bool pass = valid && c.x >= theta_l;
-      if (!__any_sync(~0u, pass)) continue;
-      const uint32_t o = warp_reserve(&sh.nloc, pass ? 1u : 0u);
-      if (pass && o < (uint32_t)capq) lead[o] = c;
+      push_special(valid ? L.spec[i] : Cand{-INFINITY, 0u}, valid);
     }
+    for_each_seen<T>(sl, r, false, tid, NT, push_special);
     if (best != 0xFFFFFFFFu) atomicMin(&sh.best, best);
   }
   __syncthreads();
@@ -2555,6 +2705,7 @@ __global__ void __launch_bounds__(NT, 1)
     sh.nloc = 0;
     sh.best = 0xFFFFFFFFu;
     sh.res.token = 0;
+    sh.status = 0;
     sh.theta = 0.0f;
     sh.u = p.uniforms ? p.uniforms[row]
                       : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
@@ -2579,6 +2730,10 @@ __global__ void __launch_bounds__(NT, 1)
       for (int j = tid; j < n; j += NT) {
         const float x = __uint_as_float(rec[4 + 2 * j]);
         const uint32_t gid = rec[5 + 2 * j];
+        if ((int64_t)gid >= V_global) {  // not an id of this vocabulary: the entry is left out
+          atomicOr(&sh.status, MSTAR_STATUS_BAD_RECORD);
+          continue;
+        }
         if (one) {
           if (x == m) best = min(best, gid);
         } else if (x >= theta) {
@@ -2599,7 +2754,8 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();
   if (tid == 0) {
     uint32_t token = sh.res.token;
-    if (empty) {
+    status |= sh.status;
+    if (empty || (int64_t)token >= V_global) {  // (no valid entry stood)
       status |= MSTAR_STATUS_EMPTY;
       token = 0;
     }
@@ -2657,24 +2813,40 @@ static int validate(const mstar_sampler_params_t *p) {
   return MSTAR_OK;
 }
 
-static int max_smem_optin() {
-  static int v = -1;
-  if (v < 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 232448;
+// Device properties the planner reads, cached per device (the calling
+// thread's current device; a process may drive several GPUs, possibly of
+// different kinds) under one lock.
+constexpr int kMaxDevices = 64;
+static std::mutex g_dev_mu;
+
+static int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+  return dev;
+}
+
+static int device_attr(cudaDeviceAttr what, int (&cache)[kMaxDevices], int fallback) {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> g(g_dev_mu);
+  if (cache[dev] <= 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, what, dev) != cudaSuccess || v <= 0) {
+      cudaGetLastError();
+      v = fallback;
+    }
+    cache[dev] = v;
   }
-  return v;
+  return cache[dev];
+}
+
+static int max_smem_optin() {
+  static int cache[kMaxDevices] = {};
+  return device_attr(cudaDevAttrMaxSharedMemoryPerBlockOptin, cache, 232448);
 }
 
 static int sm_count() {
-  static int v = -1;
-  if (v < 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) v = 148;
-  }
-  return v;
+  static int cache[kMaxDevices] = {};
+  return device_attr(cudaDevAttrMultiProcessorCount, cache, 148);
 }
 
 template <typename T, int MODE>
@@ -2685,11 +2857,12 @@ __global__ void sampler_kernel(const mstar_sampler_params_t p, const Plan pl, ui
 // whole, inside one GPC, so the width decides how many SMs a wave can use);
 // 0 if the runtime cannot say.  Cached per configuration.
 static int resident_ctas(int dtype, int mode, int S, int smem) {
-  static std::mutex mu;
-  static int keys[64][4], vals[64], used = 0;
-  std::lock_guard<std::mutex> g(mu);
+  static int keys[256][5], vals[256], used = 0;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> g(g_dev_mu);
   for (int i = 0; i < used; ++i)
-    if (keys[i][0] == dtype && keys[i][1] == mode && keys[i][2] == S && keys[i][3] == smem) return vals[i];
+    if (keys[i][0] == dtype && keys[i][1] == mode && keys[i][2] == S && keys[i][3] == smem && keys[i][4] == dev)
+      return vals[i];
   const void *fn = dtype == MSTAR_DTYPE_BF16
                        ? (mode ? (const void *)sampler_kernel<__nv_bfloat16, 1> : (const void *)sampler_kernel<__nv_bfloat16, 0>)
                        : (mode ? (const void *)sampler_kernel<float, 1> : (const void *)sampler_kernel<float, 0>);
@@ -2710,11 +2883,12 @@ static int resident_ctas(int dtype, int mode, int S, int smem) {
     if (cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) == cudaSuccess) v = clusters * S;
   }
   cudaGetLastError();  // a refused query leaves no error behind
-  if (used < 64) {
+  if (used < 256) {
     keys[used][0] = dtype;
     keys[used][1] = mode;
     keys[used][2] = S;
     keys[used][3] = smem;
+    keys[used][4] = dev;
     vals[used++] = v;
   }
   return v;
@@ -2722,8 +2896,9 @@ static int resident_ctas(int dtype, int mode, int S, int smem) {
 
 static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Plan &pl) {
   const int es = p->dtype == MSTAR_DTYPE_BF16 ? 2 : 4;
-  const int spec_max = (p->hist_ids ? p->H : (p->seen_bits ? (p->seen_cap > 0 ? p->seen_cap : 2048) : 0)) +
-                       (p->bias_ids ? p->NB : 0);
+  // materialized specials: the distinct history ids (at most H) and the bias
+  // ids; seen-mask ids are visited from the seen map instead (no bound)
+  const int spec_max = (p->hist_ids ? p->H : 0) + (p->bias_ids ? p->NB : 0);
   const int spec_cap = std::max(16, spec_max);
   const int ht_cap = next_pow2(std::max(32, 2 * spec_cap));
   const int static_bytes = (int)sizeof(CtaSh);
@@ -2740,9 +2915,10 @@ static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Pl
     const int64_t positions = nvec * (16 / es);
     q.map_bytes = (int)(((positions + 31) / 32) * 4);
     q.map_bytes = (q.map_bytes + 127) / 128 * 128;
+    q.seen_map = p->seen_bits ? 1 : 0;
     q.ht_cap = ht_cap;
     q.spec_cap = spec_cap;
-    const int work = q.map_bytes + std::max(WORK_BYTES_MIN, ht_cap * 8 + QCAP * 4);
+    const int work = q.map_bytes * (1 + q.seen_map) + std::max(WORK_BYTES_MIN, ht_cap * 8 + QCAP * 4);
     q.off_work = q.data_bytes;
     q.off_spec = q.off_work + (work + 127) / 128 * 128;
     q.off_lcand = q.off_spec + (spec_cap * 8 + 127) / 128 * 128;
@@ -2881,7 +3057,12 @@ int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int3
   if (!recv) return fail(MSTAR_ERR_INVALID, "recv is NULL");
   if (tp_world < 1 || tp_world * tp_cap > TAIL_CAP)
     return fail(MSTAR_ERR_INVALID, "tp_world * tp_cap must be in [1, 2048]");
-  if (V_global < p->V) return fail(MSTAR_ERR_INVALID, "V_global < V");
+  if (V_global < p->V || V_global > (1 << 21) * (int64_t)tp_world)
+    return fail(MSTAR_ERR_INVALID, "V_global must be in [V, tp_world * 2^21]");
+  // the merged id may come from any rank's shard: per-slot state indexed by
+  // the global id must cover the whole vocabulary
+  if (p->seen_bits && p->seen_words * 32 < V_global)
+    return fail(MSTAR_ERR_INVALID, "seen_words too small for V_global");
   const int smem = LEAN_SCRATCH;
   cudaError_t e = cudaFuncSetAttribute(tp_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));

@@ -11,7 +11,8 @@ from mstar_rs_b200.workloads import Batch, f32_to_bf16_bits, pack_bits
 def random_case(seed: int, B: int = 8, V: int = 1000, dtype: str = "f32", *, penalty: str = "hist",
                 bias: bool = True, mask: bool = True, ties: bool = False, greedy_frac: float = 0.15,
                 specials: bool = True, philox: bool = False, pad_rows: bool = False,
-                vocab_offset: int = 0, scale: float = 2.0, V_global: int | None = None) -> Batch:
+                vocab_offset: int = 0, scale: float = 2.0, V_global: int | None = None,
+                seen_density: float = 0.02) -> Batch:
     rng = np.random.default_rng(seed)
     x = rng.standard_normal((B, V)).astype(np.float32) * np.float32(scale)
     if ties:  # quantise hard so many exact ties exist
@@ -42,7 +43,7 @@ def random_case(seed: int, B: int = 8, V: int = 1000, dtype: str = "f32", *, pen
         b.hist_ids = rng.integers(-2, Vg, (B, H)).astype(np.int32)
         b.hist_len = rng.integers(0, 2 * H, B).astype(np.int32)
     elif penalty == "seen":
-        seen = rng.random((B, Vg)) < 0.02
+        seen = rng.random((B, Vg)) < seen_density
         b.seen_bits = pack_bits(seen)
     if bias:
         NB = 6

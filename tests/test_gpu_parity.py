@@ -50,6 +50,26 @@ def test_large_flat_rows(oracle_lib, seed):
         assert (g["status"] & 2).any(), "expected the general path"
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("cluster", [1, 2])
+@pytest.mark.parametrize("mask", [False, True])
+def test_many_seen_ids(oracle_lib, dtype, cluster, mask):
+    """Seen-bit rows with far more seen ids in one slice than any fixed list
+    would hold (about 12,000 and 24,000 of 40,000 ids): every seen id is
+    penalised, none is dropped, and no overflow status is raised.  Bias ids
+    that are also seen count once."""
+    case = random_case(300 + cluster, B=4, V=40000, dtype=dtype, penalty="seen", mask=mask, specials=False,
+                       seen_density=0.3 if cluster == 1 else 0.6, greedy_frac=0.0)
+    case.bias_ids[:, 2] = np.flatnonzero(np.unpackbits(case.seen_bits[0].view(np.uint8), bitorder="little"))[5]
+    from mstar_rs_b200 import _native as N
+
+    o = oracle_lib.run(case, debug=True)
+    for flags in (0, N.FLAG_FORCE_GENERAL):
+        g = run_gpu(case, cluster_size=cluster, flags=flags)
+        assert_parity(g, o, case)
+        assert not (g["status"] & N.STATUS_SPECIAL_OVERFLOW).any()
+
+
 def test_state_updates():
     """History append, seen-bit set and Philox offset advance happen on the
     device, exactly once per row."""
