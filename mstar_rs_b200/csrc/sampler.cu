@@ -66,9 +66,8 @@ constexpr int CHUNK_BYTES = 32768;  // bulk-copy granule (one mbarrier each)
 constexpr int MAX_CHUNKS = 8;       // slice data <= 256 KB
 constexpr int MAX_ROUNDS = 96;      // bound on general-path rounds
 constexpr int BIAS_SMEM = 256;      // bias entries staged in shared memory
-constexpr int QCAP = 2048;          // vectors queued by the first pass (all warps)
-constexpr int WQCAP = QCAP / (NT / 32);  // per-warp share of the queue
-constexpr int PU = 4;                    // vectors per thread per trip of the first pass
+constexpr int NPARAM = 7;           // per-row sampling parameter words
+constexpr int NVR = 19;             // vectors per thread in the register tile (152 KB per CTA)
 constexpr int HIST_BYTES = NBIN * 16;  // per histogram: counts + three 11-bit mass parts
 constexpr int GEN_BYTES = 2 * HIST_BYTES + GCAP * 8;  // L1 | REF (aliased by the sort scratch) | sort input
 static_assert(NBIN * 8 <= NBIN * 12, "64-bit mass prefixes fit over the part arrays");
@@ -172,7 +171,6 @@ struct CtaSh {
   uint32_t gmin[16];   // per-CTA lowest id at the max (greedy / top-1), pushed
   uint32_t nloc;       // CTA-local candidate count
   uint32_t scanned;    // vectors a full candidate scan covered before it stopped (0: no full scan)
-  uint32_t runmax;     // okey of the raw running max the queue threshold follows
   uint32_t cmax;       // okey of the CTA max (transformed)
   uint32_t best;       // lowest id at the max (greedy / top-1)
   uint32_t status;     // status bits of this CTA
@@ -182,8 +180,6 @@ struct CtaSh {
   float u;              // the row's uniform draw
   uint32_t n_spec;
   uint32_t ht_fail;
-  uint32_t qcount;
-  uint32_t wqn[NWARP];  // vectors each warp queued in the first pass
   float theta;
   float m;
   int fast;
@@ -196,6 +192,8 @@ struct CtaSh {
   int tp_ovf;
   int bcast_i;
   uint64_t bcast_u64;
+  uint32_t pw[NPARAM];  // the row's parameter words, staged for row_init
+  uint64_t rng[2];      // the row's uniform (bits) or Philox seed, and offset
   Cmd cmd;
   Planner pl;
   Result res;
@@ -512,26 +510,62 @@ __device__ __forceinline__ void block_exscan2_u64(uint64_t a, uint64_t b, uint64
 
 
 
-__device__ __forceinline__ void row_init(Row &r, const mstar_sampler_params_t &p, int row, int slot, int64_t V) {
+// The row's sampling parameters as raw 32-bit words, in the order
+// temperature, top_k, min_p, top_p, repetition, frequency, presence
+// (defaults for absent arrays); word j is loaded by one thread.
+__device__ __forceinline__ uint32_t param_word(const mstar_sampler_params_t &p, int j, int slot) {
+  switch (j) {
+    case 0: return p.temperature ? __float_as_uint(p.temperature[slot]) : __float_as_uint(1.0f);
+    case 1: return p.top_k ? (uint32_t)p.top_k[slot] : 0u;
+    case 2: return p.min_p ? __float_as_uint(p.min_p[slot]) : 0u;
+    case 3: return p.top_p ? __float_as_uint(p.top_p[slot]) : __float_as_uint(1.0f);
+    case 4: return p.rep_pen ? __float_as_uint(p.rep_pen[slot]) : __float_as_uint(1.0f);
+    case 5: return p.freq_pen ? __float_as_uint(p.freq_pen[slot]) : 0u;
+    default: return p.pres_pen ? __float_as_uint(p.pres_pen[slot]) : 0u;
+  }
+}
+
+__device__ __forceinline__ void row_init(Row &r, const uint32_t *w, const mstar_sampler_params_t &p, int row,
+                                         int64_t V) {
   r.V = V;
   r.gbase = p.vocab_offset;
   const int es = p.dtype == MSTAR_DTYPE_BF16 ? 2 : 4;
   r.rowp = static_cast<const uint8_t *>(p.logits) + (int64_t)row * p.ld * es;
-  r.T = p.temperature ? p.temperature[slot] : 1.0f;
+  r.T = __uint_as_float(w[0]);
   r.greedy = !(r.T >= 1e-5f);
   r.invT = r.greedy ? 1.0f : __fdiv_rn(1.0f, r.T);
-  const int K = p.top_k ? p.top_k[slot] : 0;
+  const int K = (int)w[1];
   r.topk = K > 0 && (int64_t)K < r.V;
   r.K = r.topk ? K : 0;
-  const float Mp = p.min_p ? p.min_p[slot] : 0.0f;
+  const float Mp = __uint_as_float(w[2]);
   r.minp = Mp > 0.0f;
   r.Mp = fminf(Mp, 1.0f);
   r.lnMp = r.minp ? logf(r.Mp) : 0.0f;
-  r.P = p.top_p ? p.top_p[slot] : 1.0f;
+  r.P = __uint_as_float(w[3]);
   r.topp = r.P < 1.0f;
-  r.R = p.rep_pen ? p.rep_pen[slot] : 1.0f;
-  r.F = p.freq_pen ? p.freq_pen[slot] : 0.0f;
-  r.Pp = p.pres_pen ? p.pres_pen[slot] : 0.0f;
+  r.R = __uint_as_float(w[4]);
+  r.F = __uint_as_float(w[5]);
+  r.Pp = __uint_as_float(w[6]);
+}
+
+__device__ __forceinline__ void row_init(Row &r, const mstar_sampler_params_t &p, int row, int slot, int64_t V) {
+  uint32_t w[NPARAM];
+#pragma unroll
+  for (int j = 0; j < NPARAM; ++j) w[j] = param_word(p, j, slot);
+  row_init(r, w, p, row, V);
+}
+
+// A 16-byte streaming load (read once) issued exactly where it stands: the
+// asm is volatile and clobbers memory, so the compiler neither sinks it
+// below the setup that follows nor hoists the smaller loads above it behind
+// it; its registers are waited for only where they are first used.
+__device__ __forceinline__ uint4 ld_stream(const uint4 *g) {
+  uint4 v;
+  asm volatile("ld.global.cs.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(g)
+               : "memory");
+  return v;
 }
 
 // value-A predicate of x given the row max m (positive weight and min_p).
@@ -873,7 +907,7 @@ struct Layout {
   uint8_t *skip;
   uint32_t *seen;  // seen-bit mode: seen, allowed, non-bias positions (or NULL)
   int2 *ht;    // {pos, count | HT_MASKED}
-  int *queue;  // [QCAP] vector indices queued by the first scan
+  int *queue;  // [NBIN] counts of the top_k cut's histogram
   Cand *spec;
   Cand *lcand;  // leader: candidates pushed by every CTA; general path: CTA-local list
   int32_t *bias_id;
@@ -986,7 +1020,7 @@ __device__ __forceinline__ void write_row_outputs(const mstar_sampler_params_t &
     p.hist_ids[(int64_t)slot * p.H + (len % p.H)] = (int32_t)token;
     p.hist_len[slot] = len + 1;
   }
-  if ((p.flags & MSTAR_FLAG_UPDATE_SEEN) && p.seen_bits) {
+  if ((p.flags & MSTAR_FLAG_UPDATE_SEEN) && p.seen_bits && (int64_t)(token >> 5) < p.seen_words) {
     atomicOr(&p.seen_bits[(int64_t)slot * p.seen_words + (token >> 5)], 1u << (token & 31));
   }
 }
@@ -2010,37 +2044,28 @@ __global__ void __launch_bounds__(NT, 1)
   // may have written the logits or the per-slot state) has completed
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // ---- the bulk copies go out before anything else (they depend on nothing
-  // but the geometry)
-  if (tid == 0) {
-    for (int j = 0; j < nchunk; ++j) mbar_init(&sh.mbar[j], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    // (testing: with MSTAR_FLAG_TEST_WITHHOLD the last copy is never issued
-    // and its barrier never completes, so its waits run out)
-    const int nissue = (p.flags & MSTAR_FLAG_TEST_WITHHOLD) ? nchunk - 1 : nchunk;
-    for (int j = 0; j < nissue; ++j) {
-      const uint32_t bytes = (uint32_t)min((int64_t)CHUNK_BYTES, nbulk - (int64_t)j * CHUNK_BYTES);
-      mbar_expect_tx(&sh.mbar[j], bytes);
-      bulk_g2s(L.data + (b0 - a_al) + (int64_t)j * CHUNK_BYTES,
-               reinterpret_cast<const void *>(b0 + (uintptr_t)j * CHUNK_BYTES), bytes, &sh.mbar[j]);
-    }
-  }
+  // ---- loads.  A slice whose aligned interior fits one register tile (NVR
+  // vectors per thread) is loaded straight into registers: every thread
+  // issues all of its loads at once, which lands a 152 KB slice about 1.5 us
+  // sooner than bulk copies into shared memory do; the registers are copied
+  // to shared memory once the skip bitmap is known.  A larger slice is
+  // bulk-copied in 32 KB chunks (one mbarrier each), all issued by thread 0.
+  const bool rt = nbv <= NT * NVR;  // uniform
+  const bool has_hist = p.hist_ids && p.hist_len;
+  // slot_idx costs one round trip before anything that depends on the slot
   const int slot = p.slot_idx ? p.slot_idx[row] : row;
-  if (slot < 0) {  // padding row (uniform across the cluster): drain the copies, write the padding outputs
-    if (tid == 0) {
-      for (int j = 0; j < nchunk; ++j) mbar_wait(&sh.mbar[j], 0);
-      if (rank == 0) {
-        if (MODE == 0) {
-          if (p.out_ids) p.out_ids[row] = p.vocab_offset;
-          if (p.out_ids32) p.out_ids32[row] = (int32_t)p.vocab_offset;
-          if (p.out_status) p.out_status[row] = 0;
-        } else {
-          uint32_t *rec = tp_send + (int64_t)row * pl.rec_words;
-          rec[0] = __float_as_uint(-INFINITY);
-          rec[1] = 0;
-          rec[2] = 0;
-          rec[3] = 0;
-        }
+  if (slot < 0) {  // padding row (uniform across the cluster): no load issued; write the padding outputs
+    if (tid == 0 && rank == 0) {
+      if (MODE == 0) {
+        if (p.out_ids) p.out_ids[row] = p.vocab_offset;
+        if (p.out_ids32) p.out_ids32[row] = (int32_t)p.vocab_offset;
+        if (p.out_status) p.out_status[row] = 0;
+      } else {
+        uint32_t *rec = tp_send + (int64_t)row * pl.rec_words;
+        rec[0] = __float_as_uint(-INFINITY);
+        rec[1] = 0;
+        rec[2] = 0;
+        rec[3] = 0;
       }
     }
     if (MODE == 0 && (p.out_x || p.out_kept || p.out_probs)) {
@@ -2053,49 +2078,100 @@ __global__ void __launch_bounds__(NT, 1)
     }
     return;
   }
-  // row parameters and the history words this thread inserts: loads issued
-  // now, used after the first barrier
+  // ---- the small loads first, into registers, so they are not queued
+  // behind the slice: history length and words, the row's parameter words
+  // (one per thread of warp 2), its uniform or Philox key and counter, the
+  // fringe elements (warp 0) and the bias entries
   constexpr int HP = 2;  // history words prefetched per thread
   static_assert(HP == 2, "the insertion loop reads hpre[0] / hpre[1]");
-  const bool has_hist = p.hist_ids && p.hist_len;
-  int hpre[HP];
-  int hlen = 0;
+  int hpre[HP] = {-1, -1};
+  const int hlen = has_hist ? min(p.hist_len[slot], p.H) : 0;
   if (has_hist) {
     const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
-    hlen = min(p.hist_len[slot], p.H);
 #pragma unroll
     for (int u = 0; u < HP; ++u) {
       const int j = u * NT + tid;
       hpre[u] = j < p.H ? h[j] : -1;
     }
   }
+  uint64_t pword = 0;
+  if (tid >= 64 && tid < 64 + NPARAM) {
+    pword = param_word(p, tid - 64, slot);
+  } else if (MODE == 0 && tid == 64 + NPARAM) {
+    pword = p.uniforms ? (uint64_t)__float_as_uint(p.uniforms[row]) : (p.seed ? p.seed[slot] : 0ull);
+  } else if (MODE == 0 && tid == 65 + NPARAM) {
+    pword = (!p.uniforms && p.offset) ? p.offset[slot] : 0ull;
+  }
+  const int nfr = nvec - nbv;  // fringe vectors (at most one at each end)
+  uint32_t fbits = Elem<T>::neg_inf();
+  const bool has_fe = tid < nfr * VEC;  // this thread stages one fringe element
+  int64_t fe = 0;  // its row position (may lie before the row: -inf there)
+  if (has_fe) {
+    const int f = tid / VEC;
+    fe = c0al + (int64_t)(f < hv ? f : nbv + f) * VEC + tid % VEC;
+    if (fe >= c0 && fe < c1) fbits = Elem<T>::load_bits(rowp, fe);
+  }
+  const bool bias_smem = p.bias_ids && p.NB <= BIAS_SMEM;
+  int32_t bid = -1;
+  float bval = 0.0f;
+  if (bias_smem && tid < p.NB) {
+    bid = p.bias_ids[(int64_t)slot * p.NB + tid];
+    bval = p.bias_vals[(int64_t)slot * p.NB + tid];
+  }
+  // ---- the slice: a register tile, or bulk copies
+  uint4 rv[NVR];
+  if (rt) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(b0);
+#pragma unroll
+    for (int i = 0; i < NVR; ++i) {
+      const int q = i * NT + tid;
+      rv[i] = q < nbv ? ld_stream(src + q) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  } else if (tid == 0) {
+    for (int j = 0; j < nchunk; ++j) mbar_init(&sh.mbar[j], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // (testing: with MSTAR_FLAG_TEST_WITHHOLD the last copy is never issued
+    // and its barrier never completes, so its waits run out)
+    const int nissue = (p.flags & MSTAR_FLAG_TEST_WITHHOLD) ? nchunk - 1 : nchunk;
+    for (int j = 0; j < nissue; ++j) {
+      const uint32_t bytes = (uint32_t)min((int64_t)CHUNK_BYTES, nbulk - (int64_t)j * CHUNK_BYTES);
+      mbar_expect_tx(&sh.mbar[j], bytes);
+      bulk_g2s(L.data + (b0 - a_al) + (int64_t)j * CHUNK_BYTES,
+               reinterpret_cast<const void *>(b0 + (uintptr_t)j * CHUNK_BYTES), bytes, &sh.mbar[j]);
+    }
+  }
+  // ---- staging of the small values in shared memory
+  if (tid >= 64 && tid < 64 + NPARAM) sh.pw[tid - 64] = (uint32_t)pword;
+  else if (MODE == 0 && tid >= 64 + NPARAM && tid < 66 + NPARAM) sh.rng[tid - 64 - NPARAM] = pword;
+  if (has_fe) {
+    const int64_t pos = fe - c0al;
+    if (es == 2) reinterpret_cast<uint16_t *>(L.data)[pos] = (uint16_t)fbits;
+    else reinterpret_cast<uint32_t *>(L.data)[pos] = fbits;
+  }
+  if (bias_smem && tid < p.NB) {
+    L.bias_id[tid] = bid;
+    L.bias_val[tid] = bval;
+  }
   if (tid == 0) {
     sh.nloc = 0;
     sh.scanned = 0;
-    sh.qcount = 0;
     sh.status = 0;
     sh.n_spec = 0;
     sh.ht_fail = 0;
     sh.tp_ovf = 0;
     sh.nemit = 0;
-    sh.runmax = okey(-INFINITY);
     sh.cmax = okey(-INFINITY);
     sh.best = 0xFFFFFFFFu;
     tail_reset(sh);
-  } else if (tid == 64) {  // row parameters: loads issued while thread 0 still issues the bulk copies
-    row_init(sh.row, p, row, slot, p.V);
-  } else if (MODE == 0 && tid == 32) {
-    sh.u = p.uniforms ? p.uniforms[row]
-                      : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
   }
 
   const int64_t gbase = p.vocab_offset;
   const int64_t pos0_gid = gbase + c0al;  // gid of data position 0
   const bool has_spec = has_hist || p.seen_bits || p.bias_ids;
 
-  // ---- setup while the copies fly: the skip bitmap (disallowed and
-  // special positions; positions outside the slice are -inf in the data)
-  // and the specials' hash table
+  // ---- setup while the logits are on their way: the skip bitmap
+  // (disallowed and special positions; positions outside the slice are -inf
+  // in the data) and the specials' hash table
   const int map_words = pl.map_bytes / 4;
   uint32_t *skip32 = reinterpret_cast<uint32_t *>(L.skip);
   if (has_spec)
@@ -2124,36 +2200,19 @@ __global__ void __launch_bounds__(NT, 1)
     uint4 *s4 = reinterpret_cast<uint4 *>(L.skip);
     for (int i = tid; i < map_words / 4; i += NT) s4[i] = make_uint4(0u, 0u, 0u, 0u);
   }
-  auto load_fringe = [&](int k) {
-    uint4 v = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      const int64_t e = c0al + (int64_t)k * VEC + j;
-      const uint32_t bits = (e >= c0 && e < c1) ? Elem<T>::load_bits(rowp, e) : Elem<T>::neg_inf();
-      Elem<T>::set_bits(v, j, bits);
-    }
-    data4[k] = v;
-  };
-  for (int k = tid; k < hv; k += NT) load_fringe(k);
-  for (int k = hv + nbv + tid; k < nvec; k += NT) load_fringe(k);
-  if (p.bias_ids && p.NB <= BIAS_SMEM) {
-    for (int j = tid; j < p.NB; j += NT) {
-      L.bias_id[j] = p.bias_ids[(int64_t)slot * p.NB + j];
-      L.bias_val[j] = p.bias_vals[(int64_t)slot * p.NB + j];
-    }
+  __syncthreads();  // skip words written, table cleared, small values staged
+  if (tid == 64) {
+    row_init(sh.row, sh.pw, p, row, p.V);
+  } else if (MODE == 0 && tid == 32) {
+    sh.u = p.uniforms ? __uint_as_float((uint32_t)sh.rng[0]) : philox_uniform(sh.rng[0], sh.rng[1]);
   }
-  __syncthreads();  // skip words written, table cleared
-  // Specials: history / seen bits / bias ids that fall in [c0, c1).  Each
-  // gets a skip bit (the first pass leaves it out), a hash-table entry (its
-  // count and flags) and a list entry; its final value is computed from the
-  // resident data after the last chunk.
-  //  - With an allowed mask the thread that creates a table entry sets the
-  //    position's skip bit and learns from the old bit whether the position
-  //    was disallowed; the table is complete before the first pass.
-  //  - Without one only the skip bits are set before the first pass (plain
-  //    ORs); the table is built after the first chunk, while later chunks
-  //    are still landing.
-  const bool mark_first = has_spec && !p.allowed_bits;
+  // Specials: history ids and bias ids that fall in [c0, c1) (seen-mask
+  // ids are in the seen map).  Each gets a skip bit (the max pass leaves it
+  // out), a hash-table entry (its count and flags) and a list entry; its
+  // final value is computed from the resident data after the max pass.  The
+  // thread that creates a table entry sets the position's skip bit and
+  // learns from the old bit whether the mask disallows the position.  The
+  // table is complete before the logits are read.
   uint32_t *spec32 = reinterpret_cast<uint32_t *>(L.spec);
   auto new_entry = [&](int h) {  // list entry of a created table entry
     cg::coalesced_group g = cg::coalesced_threads();
@@ -2180,13 +2239,9 @@ __global__ void __launch_bounds__(NT, 1)
       }
       // an already set skip bit of a position that is not seen means the
       // mask disallows it (seen positions in the map are allowed)
-      if (!mark_first && (atomicOr(&skip32[pos >> 5], bit) & bit) && !seen_here) atomicOr(&L.ht[h].y, HT_MASKED);
+      if ((atomicOr(&skip32[pos >> 5], bit) & bit) && !seen_here) atomicOr(&L.ht[h].y, HT_MASKED);
       new_entry(h);
     }
-  };
-  auto mark_special = [&](int64_t e, int) {
-    const int64_t pos = e - c0al;
-    atomicOr(&skip32[pos >> 5], 1u << (pos & 31));
   };
   // fn(e, count) for every materialized special occurrence of this slice
   // (e = position in the row): history ids and bias ids.  Seen-mask ids
@@ -2209,87 +2264,20 @@ __global__ void __launch_bounds__(NT, 1)
       }
     }
   };
-  if (mark_first) {
-    for_each_special(mark_special);
-    __syncthreads();  // skip bits of the specials in
-  } else if (has_spec) {
-    for_each_special(add_special);
-    __syncthreads();  // bitmap, table and special list entries complete
-  }
+  if (has_spec) for_each_special(add_special);
+  __syncthreads();  // bitmap, table and special list entries complete; row parameters in
   const Row r = sh.row;
   const Slice sl{data4, L.skip, nvec, pos0_gid, L.seen, map_words, rowp, c0al};
   const bool one = r.greedy || r.K == 1;
 
-  // ---- pass A, block by block as the bulk copies land: masked raw max; a
-  // per-warp queue of the vectors whose max reaches the running threshold
-  // thr(M) = M - |M| 2^-10 + lq T (1 + 2^-10) (M a raw max seen so far, lq
-  // the lowest offset below the CTA max that this CTA's value threshold can
-  // take); then the specials' final values.
-  float lq = 0.0f;
-  if (!one) {
-    lq = -33.0f;
-    if (r.minp) lq = fmaxf(lq, __fadd_rn(r.lnMp, -0.25f));
-  }
-  const float lqr = one ? 0.0f : __fmul_rn(lq, __fmul_rn(r.T, 1.0009765625f));
-  auto thr_of = [&](float M) -> float {
-    if (M == -INFINITY || M == INFINITY) return M;
-    return __fadd_rn(__fmaf_rn(fabsf(M), -0x1p-10f, M), lqr);
-  };
+  // ---- max pass: the masked raw max of the slice (specials and disallowed
+  // positions left out), then the specials' final values.  The register
+  // tile keeps each vector's masked max for the candidate pass and is copied
+  // to shared memory, where the slice stays resident for the later passes.
   Acc racc = Elem<T>::acc_init();
-  float runM = -INFINITY, spec_max = -INFINITY;
-  bool boot = true, timed_out = false;
-  uint32_t wq = 0;  // vectors this warp queued (warp-uniform)
-  int *const wqueue = L.queue + (tid >> 5) * WQCAP;
-  auto enqueue = [&](bool pass, int k) {
-    const unsigned bal = __ballot_sync(~0u, pass);
-    if (bal) {
-      if (pass) {
-        const uint32_t idx = wq + (uint32_t)__popc(bal & ((1u << lane) - 1u));
-        if (idx < (uint32_t)WQCAP) wqueue[idx] = k;
-      }
-      wq += (uint32_t)__popc(bal);
-    }
-  };
-  auto process = [&](int kb, int ke) {  // vectors [kb, ke); uniform trip count
-    float th = -INFINITY;
-    if (!boot) {
-      runM = okey_inv(*reinterpret_cast<volatile uint32_t *>(&sh.runmax));
-      th = thr_of(runM);
-    }
-    float cmx = -INFINITY;
-    for (int base = kb; base < ke; base += PU * NT) {
-      Acc a[PU];
-#pragma unroll
-      for (int u = 0; u < PU; ++u) {
-        const int k = base + u * NT + tid;
-        a[u] = k < ke ? Elem<T>::vred(load_masked<T>(sl, k)) : Elem<T>::acc_init();
-      }
-      Acc at = a[0];
-#pragma unroll
-      for (int u = 1; u < PU; ++u) at = Elem<T>::acc_max(at, a[u]);
-      racc = Elem<T>::acc_max(racc, at);
-      const float vm = Elem<T>::acc_f(at);
-      if (boot) {  // first trip: the CTA max over it sets the threshold
-        float w = vm;
-        for (int o = 16; o; o >>= 1) w = fmaxf(w, __shfl_xor_sync(~0u, w, o));
-        if (lane == 0 && w > -INFINITY) atomicMax(&sh.runmax, okey(w));
-        __syncthreads();  // uniform: every thread runs the same trips
-        runM = okey_inv(sh.runmax);
-        th = thr_of(runM);
-        boot = false;
-      }
-      cmx = fmaxf(cmx, vm);
-      // one vote per trip; the per-vector queue appends only when a lane passes
-      if (__any_sync(~0u, vm > -INFINITY && vm >= th)) {
-#pragma unroll
-        for (int u = 0; u < PU; ++u) {
-          const float vu = Elem<T>::acc_f(a[u]);
-          enqueue(vu > -INFINITY && vu >= th, base + u * NT + tid);
-        }
-      }
-    }
-    if (cmx > runM) atomicMax(&sh.runmax, okey(cmx));
-  };
+  float spec_max = -INFINITY;
+  bool timed_out = false;
+  Acc gm[NVR];
   const float penR = r.R, penF = r.F, penP = r.Pp;
   // Specials: bias (list order) -> penalties -> mask -> transform, after the
   // last block, from the resident data.  Entry i of the list holds its table
@@ -2327,38 +2315,37 @@ __global__ void __launch_bounds__(NT, 1)
       if (valid) spec_max = fmaxf(spec_max, c.x);
     });
   };
-  {
-    // blocks in order: bulk chunk 0 (it sets the threshold), the fringe
-    // vectors (head, tail), then the remaining chunks as they land
-    constexpr int CV = CHUNK_BYTES / 16;
-    const int nblk = max(nchunk, 1) + 2;
-    for (int bi = 0; bi < nblk; ++bi) {
-      int kb, ke;
-      if (bi == 1) {
-        kb = 0;
-        ke = hv;
-      } else if (bi == 2) {
-        kb = hv + nbv;
-        ke = nvec;
-      } else {
-        const int j = bi == 0 ? 0 : bi - 2;
-        if (j >= nchunk) continue;
-        if (!mbar_wait(&sh.mbar[j], 0)) timed_out = true;
-        kb = hv + j * CV;
-        ke = hv + min(nbv, (j + 1) * CV);
+  if (rt) {
+#pragma unroll
+    for (int i = 0; i < NVR; ++i) {
+      const int q = i * NT + tid, k = hv + q;
+      gm[i] = Elem<T>::acc_init();
+      if (q < nbv) {
+        const uint32_t b = Elem<T>::bits_of(L.skip, k);
+        gm[i] = Elem<T>::vred(b ? Elem<T>::mask_out(rv[i], b) : rv[i]);
+        data4[k] = rv[i];
       }
-      if (mark_first && bi == 1) for_each_special(add_special);  // the table, after the first chunk
-      process(kb, ke);
+      racc = Elem<T>::acc_max(racc, gm[i]);
+    }
+  } else {
+    constexpr int CV = CHUNK_BYTES / 16;
+    for (int j = 0; j < nchunk; ++j) {
+      if (!mbar_wait(&sh.mbar[j], 0)) timed_out = true;
+      const int ke = hv + min(nbv, (j + 1) * CV);
+      for (int k = hv + j * CV + tid; k < ke; k += NT)
+        racc = Elem<T>::acc_max(racc, Elem<T>::vred(load_masked<T>(sl, k)));
     }
   }
+  // the fringe vectors (at most one at each end, resident since the setup)
+  for (int f = tid; f < nfr; f += NT)
+    racc = Elem<T>::acc_max(racc, Elem<T>::vred(load_masked<T>(sl, f < hv ? f : nbv + f)));
   if (timed_out) atomicOr(&sh.status, MSTAR_STATUS_TIMEOUT);
-  if (lane == 0) sh.wqn[tid >> 5] = wq;
   {  // this CTA's max over its non-special values
     float cmx = xform(r, Elem<T>::acc_f(racc));
     for (int o = 16; o; o >>= 1) cmx = fmaxf(cmx, __shfl_xor_sync(~0u, cmx, o));
     if (lane == 0 && cmx > -INFINITY) atomicMax(&sh.cmax, okey(cmx));
   }
-  __syncthreads();  // non-special max and queues complete; specials' table built, every chunk landed
+  __syncthreads();  // non-special max complete; the slice is resident
   // ---- this CTA's value threshold theta(cm), cm its max: every member of
   // the row's A set (whose max m >= cm) has x >= theta(cm).  Warp 0 computes
   // it from the non-special max while the other warps finalize the specials;
@@ -2387,28 +2374,110 @@ __global__ void __launch_bounds__(NT, 1)
   const int capq = TAIL_CAP / S;  // candidates each CTA may push to the leader
   cluster_wait();                 // every CTA of the cluster runs: remote stores are safe
 
-  // ---- candidates: x >= theta(cm) (or x == cm for greedy / top-1) from the
-  // queued vectors and the specials, pushed into the leader's region
+  // ---- candidates: x >= theta(cm) (or x == cm for greedy / top-1),
+  // pushed into the leader's region: the register tile's vectors whose max
+  // reaches the cut (a bulk-copied slice: every vector), the fringe vectors
+  // and the specials.  Once this CTA holds more candidates than it may push
+  // the scan stops and the row takes the general path (which scans again) --
+  // unless it is a top_k row: the row's K largest are among every CTA's own
+  // K largest, so the push is redone leaving out what lies below the value
+  // bin holding this CTA's K-th largest candidate (bin b holds
+  // E(b+1) < x <= E(b), E(b) = cm - b w, w = (cm - theta) / NBIN), found by
+  // one histogram pass over the resident slice and the specials.  Ties at
+  // the cut are all pushed.
   if (cm > -INFINITY) {
     const float tcut = one ? cm : theta_l;
-    // every queue threshold used was <= thr(CTA raw max): if a value below
-    // it can still reach tcut, or a queue overflowed, scan every vector
-    const float thq = thr_of(okey_inv(sh.runmax));
-    const bool rescan = __any_sync(~0u, lane < NWARP && sh.wqn[lane] > (uint32_t)WQCAP) ||
-                        (thq > -INFINITY && !(xform(r, prev_float(thq)) < tcut));
     Cand *const lead = cluster.map_shared_rank(L.lcand, 0) + rank * capq;
     uint32_t best = 0xFFFFFFFFu;
-    // A top_k row whose queue overflowed (far more candidates than this CTA
-    // may push): the row's K largest are among every CTA's own K largest, so
-    // the push may leave out what lies below the value bin holding this CTA's
-    // K-th largest candidate (bin b holds E(b+1) < x <= E(b), E(b) = cm - b w,
-    // w = (cm - theta) / NBIN).  One histogram pass over the resident slice
-    // and the specials finds that bin; the queue's memory holds the counts
-    // (a rescan does not read the queue).  Ties at the cut are all pushed.
     bool kcut = false;
     float kcut_x = -INFINITY;  // pushed: x > kcut_x (with kcut)
-    if (!one && r.topk && r.K <= capq && rescan &&
-        __any_sync(~0u, lane < NWARP && sh.wqn[lane] > (uint32_t)WQCAP)) {  // CTA-uniform
+    // one vector per lane per step (warp-uniform step count); the passing
+    // values are appended with one atomic per warp
+    auto scan_vec = [&](int k, bool valid) {
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      bool any = false;
+      if (valid) {
+        v = load_masked<T>(sl, k);
+        any = xform(r, Elem<T>::vmax(v)) >= tcut;
+      }
+      const uint32_t gid0 = (uint32_t)(pos0_gid + (int64_t)k * VEC);
+      uint32_t pm = 0;
+      if (any) {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float x = xform(r, Elem<T>::get(v, j));
+          if (one) {
+            if (x == cm) best = min(best, gid0 + (uint32_t)j);
+          } else if (x >= theta_l && (!kcut || x > kcut_x)) {
+            pm |= 1u << j;
+          }
+        }
+      }
+      if (one || !__any_sync(~0u, pm != 0u)) return;
+      uint32_t o = warp_reserve(&sh.nloc, (uint32_t)__popc(pm));
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        if (!((pm >> j) & 1u)) continue;
+        if (o < (uint32_t)capq) lead[o] = Cand{xform(r, Elem<T>::get(v, j)), gid0 + (uint32_t)j};
+        ++o;
+      }
+    };
+    auto push_special = [&](const Cand &c, bool valid) {  // all 32 lanes
+      if (one) {
+        if (valid && c.x == cm) best = min(best, c.gid);
+        return;
+      }
+      const bool pass = valid && c.x >= theta_l && (!kcut || c.x > kcut_x);
+      if (!__any_sync(~0u, pass)) return;
+      const uint32_t o = warp_reserve(&sh.nloc, pass ? 1u : 0u);
+      if (pass && o < (uint32_t)capq) lead[o] = c;
+    };
+    // (one vector per lane per step, warp-uniform step counts)
+    auto push_all = [&]() {
+      int stop = -1;  // warp-uniform: the step at which this warp stopped
+      auto held_over = [&]() {
+        return __shfl_sync(~0u, *reinterpret_cast<volatile uint32_t *>(&sh.nloc), 0) > (uint32_t)capq;
+      };
+      if (rt) {
+        // the tile's vectors whose max reaches the cut, as a bit mask (one
+        // compact unrolled test), then one rolled loop over the set bits:
+        // the scan's code is instantiated once, not once per vector
+        uint32_t pm = 0;
+#pragma unroll
+        for (int i = 0; i < NVR; ++i)
+          pm |= (i * NT + tid < nbv && xform(r, Elem<T>::acc_f(gm[i])) >= tcut) ? 1u << i : 0u;
+        int steps = 0;
+        while (__any_sync(~0u, pm != 0u)) {  // warp-uniform
+          if (held_over()) {
+            stop = steps;
+            break;
+          }
+          const bool valid = pm != 0u;
+          const int i = valid ? __ffs(pm) - 1 : 0;
+          pm &= pm - 1u;
+          scan_vec(hv + i * NT + tid, valid);
+          ++steps;
+        }
+        if (stop >= 0 && lane == 0) atomicAdd(&sh.scanned, (uint32_t)stop * 32u + 1u);
+      } else {
+        int k0 = 0;
+        for (; k0 < nbv; k0 += NT) {
+          if (held_over()) break;
+          scan_vec(hv + k0 + tid, k0 + tid < nbv);
+        }
+        if (k0 < nbv && lane == 0) atomicAdd(&sh.scanned, (uint32_t)k0 / NWARP + 1u);
+      }
+      if (tid < 32) scan_vec(lane < hv ? lane : nbv + lane, lane < nfr);  // the fringe vectors
+      for (int i0 = 0; i0 < nspec; i0 += NT) {
+        const int i = i0 + tid;
+        const bool valid = i < nspec;
+        push_special(valid ? L.spec[i] : Cand{-INFINITY, 0u}, valid);
+      }
+      for_each_seen<T>(sl, r, false, tid, NT, push_special);
+    };
+    push_all();
+    __syncthreads();
+    if (!one && r.topk && r.K <= capq && sh.nloc > (uint32_t)capq) {  // CTA-uniform: a top_k row overflowed
       VBins vb;
       vb.m = cm;
       vb.w = __fmul_rn(__fsub_rn(cm, theta_l), 1.0f / NBIN);
@@ -2462,69 +2531,15 @@ __global__ void __launch_bounds__(NT, 1)
           kcut_x = vb_edge(vb, bk + 1);
         }
       }
-    }
-    // one vector per lane per step (warp-uniform step count); the passing
-    // values are appended with one atomic per warp
-    auto scan_vec = [&](int k, bool valid) {
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      bool any = false;
-      if (valid) {
-        v = load_masked<T>(sl, k);
-        any = xform(r, Elem<T>::vmax(v)) >= tcut;
-      }
-      const uint32_t gid0 = (uint32_t)(pos0_gid + (int64_t)k * VEC);
-      uint32_t pm = 0;
-      if (any) {
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          const float x = xform(r, Elem<T>::get(v, j));
-          if (one) {
-            if (x == cm) best = min(best, gid0 + (uint32_t)j);
-          } else if (x >= theta_l && (!kcut || x > kcut_x)) {
-            pm |= 1u << j;
-          }
+      if (kcut) {  // CTA-uniform
+        if (tid == 0) {
+          sh.nloc = 0;
+          sh.scanned = 0;
         }
+        __syncthreads();
+        push_all();
       }
-      if (one || !__any_sync(~0u, pm != 0u)) return;
-      uint32_t o = warp_reserve(&sh.nloc, (uint32_t)__popc(pm));
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        if (!((pm >> j) & 1u)) continue;
-        if (o < (uint32_t)capq) lead[o] = Cand{xform(r, Elem<T>::get(v, j)), gid0 + (uint32_t)j};
-        ++o;
-      }
-    };
-    if (rescan) {
-      // once this CTA holds more candidates than it may push, the row takes
-      // the general path (which scans again): the warp stops, and the share
-      // of the slice it covered stays on record for that path's density
-      int k0 = 0;
-      for (; k0 < nvec; k0 += NT) {
-        const uint32_t held = __shfl_sync(~0u, *reinterpret_cast<volatile uint32_t *>(&sh.nloc), 0);
-        if (held > (uint32_t)capq) break;  // warp-uniform
-        scan_vec(k0 + tid, k0 + tid < nvec);
-      }
-      if (lane == 0) atomicAdd(&sh.scanned, (uint32_t)min(k0, nvec) / NWARP + 1u);
-    } else {  // each warp drains its own queue
-      const int nq = (int)min(wq, (uint32_t)WQCAP);
-      for (int i0 = 0; i0 < nq; i0 += 32) scan_vec(i0 + lane < nq ? wqueue[i0 + lane] : 0, i0 + lane < nq);
     }
-    auto push_special = [&](const Cand &c, bool valid) {  // all 32 lanes
-      if (one) {
-        if (valid && c.x == cm) best = min(best, c.gid);
-        return;
-      }
-      const bool pass = valid && c.x >= theta_l && (!kcut || c.x > kcut_x);
-      if (!__any_sync(~0u, pass)) return;
-      const uint32_t o = warp_reserve(&sh.nloc, pass ? 1u : 0u);
-      if (pass && o < (uint32_t)capq) lead[o] = c;
-    };
-    for (int i0 = 0; i0 < nspec; i0 += NT) {
-      const int i = i0 + tid;
-      const bool valid = i < nspec;
-      push_special(valid ? L.spec[i] : Cand{-INFINITY, 0u}, valid);
-    }
-    for_each_seen<T>(sl, r, false, tid, NT, push_special);
     if (best != 0xFFFFFFFFu) atomicMin(&sh.best, best);
   }
   __syncthreads();
@@ -2918,7 +2933,7 @@ static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Pl
     q.seen_map = p->seen_bits ? 1 : 0;
     q.ht_cap = ht_cap;
     q.spec_cap = spec_cap;
-    const int work = q.map_bytes * (1 + q.seen_map) + std::max(WORK_BYTES_MIN, ht_cap * 8 + QCAP * 4);
+    const int work = q.map_bytes * (1 + q.seen_map) + std::max(WORK_BYTES_MIN, ht_cap * 8 + NBIN * 4);
     q.off_work = q.data_bytes;
     q.off_spec = q.off_work + (work + 127) / 128 * 128;
     q.off_lcand = q.off_spec + (spec_cap * 8 + 127) / 128 * 128;
@@ -2935,10 +2950,17 @@ static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Pl
     if (!need(p->cluster_size, pl)) return fail(MSTAR_ERR_UNSUPPORTED, "row does not fit the requested cluster size");
     return MSTAR_OK;
   }
-  // the smallest cluster the row fits, widened while the grid leaves SMs
-  // idle (small batches: each row's slice is then streamed by more SMs),
+  // the smallest cluster the row fits with slices that fit the register
+  // tile (else the smallest it fits at all), widened while the grid leaves
+  // SMs idle (small batches: each row's slice is then streamed by more SMs),
   // up to the portable cluster size and keeping slices >= 8192 elements
+  auto in_tile = [&](int s) {
+    const int64_t slice = ((p->V + s - 1) / s + 63) / 64 * 64;
+    return slice * es <= (int64_t)NT * NVR * 16;
+  };
   int smin = 0;
+  for (int s = 1; s <= 16 && !smin; ++s)
+    if (in_tile(s) && need(s, pl)) smin = s;
   for (int s = 1; s <= 16 && !smin; ++s)
     if (need(s, pl)) smin = s;
   if (!smin) return fail(MSTAR_ERR_UNSUPPORTED, "row too large for a 16-CTA cluster");

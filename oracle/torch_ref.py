@@ -80,8 +80,11 @@ def _allowed(case, slot: int, V: int, goff: int) -> torch.Tensor | None:
     return torch.from_numpy(bits[goff:goff + V].astype(bool))
 
 
-def sample_row(case, r: int, drop_tiny: bool = True):
-    """One row -> (token, kept bool[V], probs f64[V]); probs over the kept set."""
+def sample_row(case, r: int, drop_tiny: bool = True, nudge: tuple = (0.0, 0.0, 0.0)):
+    """One row -> (token, kept bool[V], probs f64[V], x f32[V]); probs over
+    the kept set; x the processed logits (NaN stays NaN, disallowed -inf).
+    `nudge` = relative changes of (top_p, min_p, u): used to show that a
+    disagreement with the spec oracle sits on a boundary."""
     V = case.V
     goff = case.vocab_offset
     slot = int(case.slot_idx[r]) if case.slot_idx is not None else r
@@ -100,7 +103,8 @@ def sample_row(case, r: int, drop_tiny: bool = True):
     pen = pen - F * cnt.to(torch.float32)
     pen = pen - P
     v = torch.where(hit, pen, v)
-    ok = ~torch.isnan(v)
+    nan = torch.isnan(v)
+    ok = ~nan
     al = _allowed(case, slot, V, goff)
     if al is not None:
         ok &= al
@@ -109,39 +113,40 @@ def sample_row(case, r: int, drop_tiny: bool = True):
     probs = torch.zeros(V, dtype=torch.float64)
     T = float(g(case.temperature, 1.0))
     K = int(g(case.top_k, 0))
+    greedy = not (T >= 1e-5)
+    x = v if greedy else v * torch.tensor(np.float32(1.0) / np.float32(T), dtype=torch.float32)
+    xdbg = torch.where(nan, torch.tensor(float("nan")), x)
     if not ok.any() or not (v.max() > -float("inf")):
-        return goff, kept, probs
-    if not (T >= 1e-5) or K == 1:
-        if not (T >= 1e-5):
-            x = v
-        else:
-            x = v * torch.tensor(np.float32(1.0) / np.float32(T), dtype=torch.float32)
+        return goff, kept, probs, xdbg
+    if greedy or K == 1:
         tok = int(torch.argmax(x))  # first index of the maximum
         kept[tok] = True
         probs[tok] = 1.0
-        return tok + goff, kept, probs
-    x = v * torch.tensor(np.float32(1.0) / np.float32(T), dtype=torch.float32)
+        return tok + goff, kept, probs, xdbg
     order = torch.sort(x, descending=True, stable=True).indices
     xs = x[order].to(torch.float64)
     m = xs[0]
-    logp = xs - m  # log of unnormalised probability relative to the max
+    # log of the unnormalised probability relative to the max; tokens equal
+    # to the max count as the max (this also defines rows whose max is +inf,
+    # where plain softmax would give NaN)
+    logp = torch.where(xs == m, torch.zeros_like(xs), xs - m)
     n = V
     if 0 < K < V:
         n = K
     live = torch.isfinite(logp[:n])
     if drop_tiny:
         live &= logp[:n] >= TINY_LOG
-    Mp = float(g(case.min_p, 0.0))
+    Mp = float(g(case.min_p, 0.0)) * (1.0 + nudge[1])
     if Mp > 0:
         live &= logp[:n] >= np.log(min(Mp, 1.0))
     # A is the longest prefix of live members
     nA = int(torch.argmin(live.to(torch.int8))) if not bool(live.all()) else n
     if nA == 0:
         tok = int(order[0])
-        return tok + goff, kept, probs
+        return tok + goff, kept, probs, xdbg
     w = torch.exp(logp[:nA])
     pA = w / w.sum()
-    Ptop = float(g(case.top_p, 1.0))
+    Ptop = float(g(case.top_p, 1.0)) * (1.0 + nudge[0])
     nK = nA
     if Ptop < 1.0:
         excl = torch.cumsum(pA, 0) - pA
@@ -154,26 +159,28 @@ def sample_row(case, r: int, drop_tiny: bool = True):
         u = float(case.uniforms[r])
     else:
         u = _philox_uniform(int(g(case.seed, 0)), int(g(case.offset, 0)))
+    u = u * (1.0 + nudge[2])
     cum = torch.cumsum(pk, 0)
     j = int(torch.searchsorted(cum, torch.tensor([u], dtype=torch.float64), right=True)[0])
     j = min(j, nK - 1)
     ids = order[:nK]
     kept[ids] = True
     probs[ids] = pk
-    return int(ids[j]) + goff, kept, probs
+    return int(ids[j]) + goff, kept, probs, xdbg
 
 
 def run(case, drop_tiny: bool = True):
-    """All rows; returns dict(ids, kept, probs).  Padding rows (slot < 0)
-    return vocab_offset with an empty kept set."""
+    """All rows; returns dict(ids, kept, probs, x).  Padding rows (slot < 0)
+    return vocab_offset with an empty kept set and x = -inf."""
     B, V = case.B, case.V
     ids = np.zeros(B, np.int64)
     kept = np.zeros((B, V), bool)
     probs = np.zeros((B, V), np.float64)
+    x = np.full((B, V), -np.inf, np.float32)
     for r in range(B):
         if case.slot_idx is not None and int(case.slot_idx[r]) < 0:
             ids[r] = case.vocab_offset
             continue
-        t, k, p = sample_row(case, r, drop_tiny=drop_tiny)
-        ids[r], kept[r], probs[r] = t, k.numpy(), p.numpy()
-    return dict(ids=ids, kept=kept, probs=probs)
+        t, k, p, xr = sample_row(case, r, drop_tiny=drop_tiny)
+        ids[r], kept[r], probs[r], x[r] = t, k.numpy(), p.numpy(), xr.numpy()
+    return dict(ids=ids, kept=kept, probs=probs, x=x)

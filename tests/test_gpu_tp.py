@@ -67,3 +67,40 @@ def test_tp_local_merge(oracle_lib, tp, cluster):
 
 def d_params(d):
     return {k: v for k, v in d.items() if not k.startswith("_") and k != "vocab_offset"}
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_tp_full_size(oracle_lib, tp):
+    """The vocab-sharded workload at its real size (B=128, V=152064, 512-token
+    histories) through tp_local / tp_merge with the shards emulated on one
+    device: every shard's record equals the numpy restatement's and every
+    rank's merge returns the full row's oracle ids."""
+    import torch
+
+    from mstar_rs_b200 import tp as TP
+
+    shards = W.tp_sharded(tp, seed=2)
+    full = W.tp_full(shards)
+    assert (full.B, full.V) == (128, 152064)
+    ref = oracle_lib.run(full)["ids"]
+    B = full.B
+    sends = []
+    samplers = [TP.VocabParallelSampler(B, full.V, tp, q, "cuda", tp_cap=TP_CAP, gather=None) for q in range(tp)]
+    devs = [W.to_device(s) for s in shards]
+    for q, (smp, d) in enumerate(zip(samplers, devs)):
+        logits = d.pop("logits")
+        d["_logits"] = logits
+        send = smp.local(logits, shards[q].vocab_offset, **d_params(d))
+        torch.cuda.synchronize()
+        got = send.cpu().numpy().view(np.uint32).reshape(B, -1).copy()
+        got[:, 2] &= ~np.uint32(2)
+        np.testing.assert_array_equal(got, _records_np(shards[q]), err_msg=f"shard {q} record")
+        sends.append(send.clone())
+    recv = torch.cat(sends)
+    for q, (smp, d) in enumerate(zip(samplers, devs)):
+        out = torch.zeros(B, dtype=torch.int64, device="cuda")
+        status = torch.zeros(B, dtype=torch.int32, device="cuda")
+        smp.merge(d["_logits"], shards[q].vocab_offset, recv, out_ids=out, out_status=status, **d_params(d))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy(), ref, err_msg=f"merge on shard {q}")
+        assert not TP.status_overflowed(status).any().item()

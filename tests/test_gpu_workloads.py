@@ -24,7 +24,7 @@ def test_qwen_mixed_batch(oracle_lib, seed):
     assert_parity(run_gpu(case), o, case)
 
 
-@pytest.mark.parametrize("B", [1, 8, 32, 128])
+@pytest.mark.parametrize("B", [1, 8, 32, 128, 256, 512])
 def test_bucket_sweep(oracle_lib, B):
     from mstar_rs_b200 import workloads
 
@@ -39,6 +39,16 @@ def test_constrained(oracle_lib):
     case = workloads.constrained(0, B=128)
     o = oracle_lib.run(case, debug=True)
     assert_parity(run_gpu(case), o, case)
+
+
+def test_constrained_full_batch(oracle_lib):
+    """All 512 rows of the constrained workload (ids and status)."""
+    from mstar_rs_b200 import workloads
+
+    case = workloads.constrained(1)
+    assert case.B == 512
+    o = oracle_lib.run(case, debug=False)
+    assert_parity(run_gpu(case, debug=False), o, case, debug=False)
 
 
 def test_tp_full_row_reference(oracle_lib):
