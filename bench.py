@@ -13,14 +13,20 @@ ours:       K steps replayed from CUDA graphs over rotating logits buffers whose
             total size exceeds 2x the 126 MB L2 (every step reads cold HBM);
             CUDA-event timing on the launching stream, max over ranks.
             roofline: algorithmic bytes / the kernel's mean launch duration over
-            the timed region (events around every single launch, captured in a
-            second graph, are reported beside it); e2e: the same steps through
-            the public Python API from pinned host logits (H2D + step + D2H of
-            the ids inside the timed region).
-reference:  the CPU restatement of the sampler spec (oracle/, C + OpenMP) on
-            the host cores, rank 0 only, on a bounded sample of the workload.
-Multi-GPU (torchrun): data-parallel replicas, each rank samples its own batch
-(weak scaling, no collective on the data path).
+            the timed region.  e2e: the same steps through the public Python API
+            from pinned host logits (H2D + step + D2H of the ids timed).
+            api_graph: the drop-in CudaGraphableSampler replayed with the
+            engine's stage / gather / sync around every replay, device logits.
+            per_config (one GPU): every other workload the sampler is measured
+            on, each with its roofline and CPU baseline.
+            More GPUs (torchrun): the line is data-parallel (each rank its own
+            batch, weak scaling); `tp` is the vocabulary-sharded workload over
+            the ranks (shard records, NCCL all-gather, merge, captured in one
+            graph) and `dp_split` the constrained workload's 512 rows split
+            across the ranks (strong scaling).
+reference:  the torch-formulated CPU restatement of the sampler (oracle/
+            torch_ref.py, batched over the rows, all host cores), rank 0 only,
+            on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -51,22 +57,23 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cluster", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
     return ap.parse_args()
 
 
-def make_case(args, rank):
+def make_case(name, rank=0, seed=0, bucket=128):
     from mstar_rs_b200 import workloads as W
 
-    if args.workload == "qwen_mixed":
-        return W.qwen_mixed(seed=args.seed + rank)
-    if args.workload == "orpheus_single":
-        return W.orpheus_single(seed=args.seed + rank)
-    if args.workload == "bucket":
-        return W.bucket_sweep(args.bucket, seed=args.seed + rank)
-    if args.workload == "tp":  # the reference arm samples the whole row (vocab sharding is ours)
-        return W.tp_full(W.tp_sharded(1, seed=args.seed))
-    return W.constrained(seed=args.seed + rank)
+    if name == "qwen_mixed":
+        return W.qwen_mixed(seed=seed + rank)
+    if name == "orpheus_single":
+        return W.orpheus_single(seed=seed + rank)
+    if name == "bucket":
+        return W.bucket_sweep(bucket, seed=seed + rank)
+    if name == "tp":  # the whole row (the reference arm samples it unsharded)
+        return W.tp_full(W.tp_sharded(1, seed=seed))
+    return W.constrained(seed=seed + rank)
 
 
 def algorithmic_bytes(case) -> int:
@@ -165,135 +172,162 @@ def dist_setup(args):
     return world, rank, local
 
 
-def cpu_baseline(case, budget_s: float = 10.0, max_rows: int | None = None):
-    """Time the oracle (C, all host cores) on whole batches of the workload."""
+def config_of(case, world):
+    """The workload description both arms print (the same keys in both)."""
+    return {"workload": case.name, "B": case.B, "V": case.V, "logits_dtype": case.dtype,
+            "history": None if case.hist_ids is None else int(case.hist_ids.shape[1]),
+            "parallelism": f"dp{world}" if world > 1 else "single",
+            "rng": "philox in-kernel, offset advanced per step",
+            "state_updates": "history append + offset" if case.hist_ids is not None else "offset",
+            "history_reset": "restored from the initial Zipf history once per cycle over the logits buffers",
+            "l2": "inputs larger than 2x L2 per step (rotating logits buffers)"}
+
+
+def torch_cpu_baseline(case, budget_s: float = 8.0, max_rows: int | None = None):
+    """The torch-formulated CPU sampler (oracle/torch_ref.py, batched over the
+    rows, every host core) on a bounded sample of the workload's rows."""
+    import torch
+
+    from oracle import torch_ref
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows = min(case.B, max(1, max_rows or case.B))
+    sub = case.row_slice(0, rows) if rows < case.B else case
+    torch_ref.run_batched(sub)  # warm
+    done, t0 = 0, time.perf_counter()
+    while True:
+        torch_ref.run_batched(sub)
+        done += rows
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": "rows/s", "cores": threads, "kind": "port",
+            "sample": f"{done} rows of {case.name} ({done // rows} batches of {rows}) through the torch-formulated "
+                      f"CPU sampler (float64 softmax, sort, cumsum; {threads} threads), {dt:.1f} s"}
+
+
+def c_oracle_baseline(case, budget_s: float = 4.0):
+    """The C spec oracle (OpenMP over rows, every host core), for reference."""
     from oracle import oracle
 
     threads = os.cpu_count() or 1
     oracle.build()
-    oracle.run(case, threads=threads)  # warm
-    rows = 0
-    t0 = time.perf_counter()
+    oracle.run(case, threads=threads)
+    rows, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < budget_s:
         oracle.run(case, threads=threads)
         rows += case.B
-        if max_rows and rows >= max_rows:
-            break
-    dt = time.perf_counter() - t0
-    return {"value": rows / dt, "unit": "rows/s", "cores": threads, "kind": "port",
-            "sample": f"{rows} rows of {case.name} ({rows // case.B} full batches) through the C oracle "
-                      f"with {threads} OpenMP threads, {dt:.1f} s"}
+    return {"value": rows / (time.perf_counter() - t0), "unit": "rows/s", "cores": threads,
+            "kind": "port", "sample": f"{rows} rows of {case.name} through the C spec oracle"}
 
 
 def run_reference(args, world, rank):
-    """CPU arm: the spec restatement on the host cores, rank 0 only."""
-    from oracle import oracle
-    from mstar_rs_b200 import workloads as W
+    """CPU arm: the torch-formulated sampler on the host cores, rank 0 only,
+    each step a bounded sample of the workload's rows."""
+    import torch
+
+    from oracle import torch_ref
 
     if rank != 0:
         return
-    case = make_case(args, 0)
+    case = make_case(args.workload, 0, args.seed, args.bucket)
     threads = os.cpu_count() or 1
-    oracle.build()
+    torch.set_num_threads(threads)
+    probe = case.row_slice(0, min(case.B, 4)) if case.B > 4 else case
     t0 = time.perf_counter()
-    oracle.run(case, threads=threads)
-    t_batch = time.perf_counter() - t0
-    budget = 90.0
+    torch_ref.run_batched(probe)
+    per_row = (time.perf_counter() - t0) / probe.B
+    budget = 120.0
     rows_per_step = case.B
-    if (args.steps + args.warmup) * t_batch > budget:
-        rows_per_step = max(1, int(case.B * budget / ((args.steps + args.warmup) * t_batch)))
+    if (args.steps + args.warmup) * per_row * case.B > budget:
+        rows_per_step = max(1, int(budget / ((args.steps + args.warmup) * per_row)))
     sub = case.row_slice(0, rows_per_step) if rows_per_step < case.B else case
     for _ in range(args.warmup):
-        oracle.run(sub, threads=threads)
+        torch_ref.run_batched(sub)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.run(sub, threads=threads)
+        torch_ref.run_batched(sub)
     dt = time.perf_counter() - t0
     value = rows_per_step * args.steps / dt
-    sample = (f"{args.steps} steps of {rows_per_step} rows of {case.name} through the C oracle "
-              f"(spec restatement) with {threads} OpenMP threads")
+    sample = (f"{args.steps} steps of {rows_per_step} rows of {case.name} through the torch-formulated CPU "
+              f"sampler (oracle/torch_ref.py, batched, {threads} threads)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": config_of(case, args, world, rows_per_step=rows_per_step),
+        "data": "synthetic", "config": config_of(case, world),
+        "rows_per_step": rows_per_step,
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
-def config_of(case, args, world, **extra):
-    c = {"workload": case.name, "B": case.B, "V": case.V, "logits_dtype": case.dtype,
-         "history": None if case.hist_ids is None else int(case.hist_ids.shape[1]),
-         "parallelism": f"dp{world}" if world > 1 else "single",
-         "rng": "philox in-kernel, offset advanced per step", "state_updates": "history append + offset",
-         "history_reset": "restored from the initial Zipf history once per cycle over the logits buffers"}
-    c.update(extra)
-    return c
+def _peak():
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:  # noqa: BLE001
+        peaks = {}
+    p = peaks.get("hbm_gbs")
+    return (p, "measured") if p else (6650.0, "fallback")
 
 
-def run_ours(args, world, rank, local):
-    import numpy as np
+def _rotating(base, torch):
+    step_bytes = base.numel() * base.element_size()
+    nbuf = max(2, -(-2 * L2_BYTES // step_bytes))
+    return [base] + [torch.roll(base, shifts=997 * i, dims=1).contiguous() for i in range(1, nbuf)], nbuf
+
+
+def time_graph_steps(case, dev, stream, steps, warmup, cluster=0, restore_history=True):
+    """Graph replay of `steps` sampling steps of `case` over rotating cold
+    buffers; returns (ms per step, mean isolated launch ms, cluster width)."""
     import torch
 
     from mstar_rs_b200 import _native as N
-    from mstar_rs_b200 import kernel, workloads as W
+    from mstar_rs_b200 import kernel
+    from mstar_rs_b200 import workloads as W
 
-    dev = torch.device("cuda", local)
-    case = make_case(args, rank)
     d = W.to_device(case, device=dev, with_uniforms=False)
     if d.get("seed") is None:
         d["seed"] = torch.arange(case.B, dtype=torch.int64, device=dev) + 12345
         d["offset"] = torch.zeros(case.B, dtype=torch.int64, device=dev)
     base = d.pop("logits")
-    step_bytes = base.numel() * base.element_size()
-    nbuf = max(2, -(-2 * L2_BYTES // step_bytes))
-    bufs = [base] + [torch.roll(base, shifts=997 * i, dims=1).contiguous() for i in range(1, nbuf)]
-    B = case.B
-    out = torch.zeros(B, dtype=torch.int64, device=dev)
+    bufs, nbuf = _rotating(base, torch)
+    out = torch.zeros(case.B, dtype=torch.int64, device=dev)
     flags = N.FLAG_ADVANCE_OFFSET | (N.FLAG_UPDATE_HISTORY if d.get("hist_ids") is not None else 0)
-    params = [kernel.build_params(b, **d, out_ids=out, flags=flags, cluster_size=args.cluster) for b in bufs]
-
+    params = [kernel.build_params(b, **d, out_ids=out, flags=flags, cluster_size=cluster) for b in bufs]
     # The logits buffers repeat every nbuf steps, so tokens appended to the
-    # history would pile up penalties on the same ids step after step and
-    # drift the workload away from its 1024-token Zipf history; the history
-    # is therefore restored (device copy, inside the timed graphs) at the
-    # start of every cycle over the buffers.
+    # history would pile up penalties on the same ids step after step; the
+    # history is restored (device copy, inside the timed graphs) at the start
+    # of every cycle over the buffers.
     hist0 = None
-    if d.get("hist_ids") is not None:
+    if d.get("hist_ids") is not None and restore_history:
         hist0 = (d["hist_ids"].clone(), d["hist_len"].clone())
 
-    def restore(i):
+    def step(i):
         if hist0 is not None and i % nbuf == 0:
             d["hist_ids"].copy_(hist0[0])
             d["hist_len"].copy_(hist0[1])
-
-    def step(i):
-        restore(i)
         kernel.launch_step(params[i % nbuf], dev)
 
-    stream = torch.cuda.Stream(device=dev)
     torch.cuda.synchronize(dev)
     with torch.cuda.stream(stream):
-        for i in range(max(3, args.warmup)):
+        for i in range(max(3, warmup)):
             step(i)
     torch.cuda.synchronize(dev)
+    g = min(steps, 8 * nbuf)
+    reps, rem = divmod(steps, g)
 
-    K = args.steps
-    g = min(K, 8 * nbuf)
-    reps, rem = divmod(K, g)
-
-    def capture(n, with_events=False, start=0):
+    def capture(n, start=0, events=False):
         graph = torch.cuda.CUDAGraph()
         evs = []
         with torch.cuda.graph(graph, stream=stream):
             for i in range(n):
-                if with_events:
+                if events:
                     e0 = torch.cuda.Event(enable_timing=True, external=True)
                     e1 = torch.cuda.Event(enable_timing=True, external=True)
-                    restore(start + i)
                     e0.record()
-                    kernel.launch_step(params[(start + i) % nbuf], dev)
+                    step(start + i)
                     e1.record()
                     evs.append((e0, e1))
                 else:
@@ -301,65 +335,80 @@ def run_ours(args, world, rank, local):
         return graph, evs
 
     gmain, _ = capture(g)
-    grem, _ = capture(rem, start=g * reps) if rem else (None, [])
-    gev, evs = capture(min(g, 2 * nbuf), with_events=True)
+    grem = capture(rem, start=g * reps)[0] if rem else None
+    gev, evs = capture(min(g, 2 * nbuf), events=True)
     with torch.cuda.stream(stream):
-        gmain.replay()  # graph warm-up
+        gmain.replay()
     torch.cuda.synchronize(dev)
+    return dict(graphs=(gmain, grem, reps), events=(gev, evs), plan=kernel.plan(bufs[0], **d, out_ids=out)[0],
+                step_bytes=base.numel() * base.element_size(), nbuf=nbuf)
+
+
+def replay_ms(t, stream, dev):
+    import torch
+
+    gmain, grem, reps = t["graphs"]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            gmain.replay()
+        if grem is not None:
+            grem.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1)
+
+
+def isolated_ms(t, stream, dev):
+    import torch
+
+    gev, evs = t["events"]
+    with torch.cuda.stream(stream):
+        gev.replay()
+    torch.cuda.synchronize(dev)
+    return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+
+def run_ours(args, world, rank, local):
+    import torch
+
+    dev = torch.device("cuda", local)
+    case = make_case(args.workload, rank, args.seed, args.bucket)
+    stream = torch.cuda.Stream(device=dev)
+    K = args.steps
+    t = time_graph_steps(case, dev, stream, K, args.warmup, cluster=args.cluster)
 
     dist = None
     if world > 1:
         import torch.distributed as dist
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
     if dist:
         dist.barrier()
     torch.cuda.synchronize(dev)
     clocks = ClockSampler(local)
     with clocks:
-        with torch.cuda.stream(stream):
-            t0.record(stream)
-            for _ in range(reps):
-                gmain.replay()
-            if grem is not None:
-                grem.replay()
-            t1.record(stream)
-        torch.cuda.synchronize(dev)
+        ms = replay_ms(t, stream, dev)
     if dist:
         dist.barrier()
-    ms = t0.elapsed_time(t1)
-    if dist:
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
+    k_ms = isolated_ms(t, stream, dev)
 
-    # kernel durations (events around each launch, cold buffers)
-    with torch.cuda.stream(stream):
-        gev.replay()
-    torch.cuda.synchronize(dev)
-    kdur = [a.elapsed_time(b) for a, b in evs]
-    k_ms = statistics.mean(kdur)
-
-    # e2e through the public API from pinned host memory
-    e2e = run_e2e(args, case, d, dev, stream, world)
-
+    e2e = run_e2e(args, case, dev, stream, world)
+    api = run_api_graph(case, dev, world)
+    extra = {}
+    if world > 1:
+        extra["tp"] = run_tp_multi(args, world, rank, local)
+        extra["dp_split"] = run_dp_split(args, world, rank, local)
+    plan, nbuf, step_bytes = t["plan"], t["nbuf"], t["step_bytes"]
+    del t
     if rank != 0:
         return
-    rows = B * K * world
+    rows = case.B * K * world
     value = rows / (ms / 1e3)
     alg = algorithmic_bytes(case)
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except Exception:  # noqa: BLE001
-        pass
-    peak = peaks.get("hbm_gbs")
-    peak_src = "measured" if peak else "fallback"
-    peak = peak or 6650.0
-    # the kernel's average launch duration over the timed region (one launch
-    # per step, back to back from the graph, as in a decode loop); the mean
-    # of events placed around each single launch is reported beside it
-    # (those events add their own overhead and keep launches from overlapping)
+    peak, peak_src = _peak()
     region_ms = ms / K
     achieved = alg / (region_ms / 1e3) / 1e9
     traffic = None
@@ -373,25 +422,60 @@ def run_ours(args, world, rank, local):
         "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_of(case, args, world, l2=f"{nbuf} rotating logits buffers "
-                            f"({nbuf * step_bytes / 2**20:.0f} MiB > 2x L2)",
-                            launch="CUDA graph replay", cluster_size=kernel.plan(bufs[0], **d, out_ids=out)[0]),
+        "config": config_of(case, world),
+        "measurement": {"launch": "CUDA graph replay", "cluster_size": plan,
+                        "l2": f"{nbuf} rotating logits buffers ({nbuf * step_bytes / 2**20:.0f} MiB)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
                      "kernel_us": region_ms * 1e3, "kernel_us_isolated": k_ms * 1e3,
                      "algorithmic_bytes": alg},
         "e2e": e2e,
+        "api_graph": api,
         "gpu_launches": K,
         "clocks": clocks.summary(),
     }
+    line.update(extra)
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(case)
+        line["cpu_baseline"] = torch_cpu_baseline(case)
+        line["cpu_spec_oracle"] = c_oracle_baseline(case)
+    if world == 1 and not args.no_per_config and args.workload == "qwen_mixed":
+        line["per_config"] = run_per_config(args, dev, stream, no_cpu=args.no_cpu_baseline)
     print(json.dumps(line), flush=True)
 
 
-def run_e2e(args, case, d, dev, stream, world):
+def run_per_config(args, dev, stream, no_cpu=False):
+    """Every other workload at one GPU: µs per step, rows/s, roofline and the
+    torch-formulated CPU baseline on a few rows."""
+    import torch
+
+    out = {}
+    peak, peak_src = _peak()
+    for name, bucket in (("orpheus_single", 0), ("bucket", 128), ("bucket", 512), ("constrained", 0)):
+        case = make_case(name, 0, args.seed, bucket)
+        steps = 200 if case.B >= 256 else 500
+        t = time_graph_steps(case, dev, stream, steps, 5)
+        ms = replay_ms(t, stream, dev) / steps
+        alg = algorithmic_bytes(case)
+        ent = {"us_per_step": ms * 1e3, "rows_per_s": case.B / (ms / 1e3), "cluster_size": t["plan"],
+               "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                            "frac": alg / (ms / 1e3) / 1e9 / peak, "peak_source": peak_src,
+                            "algorithmic_bytes": alg}}
+        if not no_cpu:
+            ent["cpu_baseline"] = torch_cpu_baseline(case, budget_s=3.0, max_rows=4)
+        out[case.name] = ent
+        del t
+        torch.cuda.empty_cache()
+    tp1 = run_tp_single(args, dev, stream)
+    if not no_cpu:
+        tp1["cpu_baseline"] = torch_cpu_baseline(make_case("tp", 0, args.seed), budget_s=3.0, max_rows=8)
+    out[tp1.pop("name")] = tp1
+    return out
+
+
+def run_e2e(args, case, dev, stream, world):
     """Same workload through mstar_rs_b200.sampling (the drop-in API) with the
     logits in pinned host memory: H2D copy, sample, D2H of the ids, per step."""
+    import numpy as np
     import torch
 
     from mstar_rs_b200 import sampling
@@ -399,26 +483,12 @@ def run_e2e(args, case, d, dev, stream, world):
     B, V = case.B, case.V
     dt = torch.bfloat16 if case.dtype == "bf16" else torch.float32
     host = [torch.empty(B, V, dtype=dt).pin_memory() for _ in range(2)]
-    src = d  # noqa: F841
-    import numpy as np
-
     lf = case.logits_f32()
     for i, h in enumerate(host):
         h.copy_(torch.from_numpy(np.roll(lf, 13 * i, axis=1)).to(dt))
     engine = sampling.Sampler(device=dev, max_requests=max(256, B))
     rids = [f"r{i}" for i in range(B)]
-    for i, rid in enumerate(rids):
-        engine.add_request(rid)
-        engine.set_config(rid, vocab_size=V, temperature=float(case.temperature[i]),
-                          top_k=int(case.top_k[i]) if case.top_k is not None else 0,
-                          top_p=float(case.top_p[i]) if case.top_p is not None else 1.0,
-                          min_p=float(case.min_p[i]) if case.min_p is not None else 0.0,
-                          repetition_penalty=float(case.rep_pen[i]) if case.rep_pen is not None else 1.0,
-                          presence_penalty=float(case.pres_pen[i]) if case.pres_pen is not None else 0.0,
-                          frequency_penalty=float(case.freq_pen[i]) if case.freq_pen is not None else 0.0)
-        engine._sampling_config[rid].set_seed(1000 + i)
-        if case.hist_ids is not None:
-            engine.set_history(rid, case.hist_ids[i, : int(case.hist_len[i])].tolist())
+    _configure(engine, rids, case)
     # Double-buffered: step i+1's logits cross PCIe on a copy stream while
     # step i samples; a buffer is refilled only after the step that read it.
     dev_logits = [torch.empty(B, V, dtype=dt, device=dev) for _ in range(2)]
@@ -465,94 +535,267 @@ def run_e2e(args, case, d, dev, stream, world):
             "pipeline": "two device logits buffers; step i+1's H2D copy overlaps step i's sampling"}
 
 
-def run_tp(args, world, rank, local):
-    """Vocab-parallel sampling (B=128, V=152064 bf16 split evenly over the
-    ranks): each step is this rank's shard records, an NCCL all-gather of the
-    records and the merge that gives every rank the same ids.  Strong scaling:
-    the rows and the vocabulary are fixed, the ranks share the vocabulary."""
+def _configure(engine, rids, case):
+    for i, rid in enumerate(rids):
+        engine.add_request(rid)
+        engine.set_config(rid, vocab_size=case.V, temperature=float(case.temperature[i]),
+                          top_k=int(case.top_k[i]) if case.top_k is not None else 0,
+                          top_p=float(case.top_p[i]) if case.top_p is not None else 1.0,
+                          min_p=float(case.min_p[i]) if case.min_p is not None else 0.0,
+                          repetition_penalty=float(case.rep_pen[i]) if case.rep_pen is not None else 1.0,
+                          presence_penalty=float(case.pres_pen[i]) if case.pres_pen is not None else 0.0,
+                          frequency_penalty=float(case.freq_pen[i]) if case.freq_pen is not None else 0.0)
+        engine._sampling_config[rid].set_seed(1000 + i)
+        if case.hist_ids is not None:
+            engine.set_history(rid, case.hist_ids[i, : int(case.hist_len[i])].tolist())
+
+
+def run_api_graph(case, dev, world, steps=200):
+    """The drop-in graph path as an engine drives it: SamplerBuffers +
+    CudaGraphableSampler captured once, then per step stage / gather /
+    replay / sync with device-resident logits (no host transfer)."""
+    import numpy as np
+    import torch
+
+    from mstar_rs_b200 import sampling
+
+    B, V = case.B, case.V
+    dt = torch.bfloat16 if case.dtype == "bf16" else torch.float32
+    sbuf = sampling.SamplerBuffers.allocate(B, dev, vocab_size=V)
+    rids = [f"g{i}" for i in range(B)]
+    masks = []
+    for i, r in enumerate(rids):
+        c = sampling.SamplingConfig(vocab_size=V, temperature=float(case.temperature[i]),
+                                    top_k=int(case.top_k[i]) if case.top_k is not None else 0,
+                                    top_p=float(case.top_p[i]) if case.top_p is not None else 1.0,
+                                    min_p=float(case.min_p[i]) if case.min_p is not None else 0.0,
+                                    repetition_penalty=float(case.rep_pen[i]) if case.rep_pen is not None else 1.0,
+                                    presence_penalty=float(case.pres_pen[i]) if case.pres_pen is not None else 0.0,
+                                    frequency_penalty=float(case.freq_pen[i]) if case.freq_pen is not None else 0.0)
+        c.set_seed(2000 + i)
+        sbuf.register_request(r, c)
+        m = sampling.SeenTokenMask.new(r, V, dev)
+        if case.hist_ids is not None:
+            m.add_tokens(torch.from_numpy(case.hist_ids[i].astype(np.int64)).to(dev))
+        masks.append(m)
+    lf = case.logits_f32()
+    base = torch.from_numpy(lf).to(dt).to(dev)
+    bufs, nbuf = _rotating(base, torch)
+    g_logits = torch.empty(B, V, dtype=dt, device=dev)
+    sbuf.stage_seen_token_masks(rids, masks)
+    sampler = sbuf.gather_for_request_ids(rids, B)
+    out = torch.zeros(B, dtype=torch.int64, device=dev)
+
+    def dec():
+        out.copy_(sampler.sample(rids, g_logits, apply_penalty=True))
+
+    saved = (sbuf.offset_buf.clone(), sbuf.seen_tokens.buf.clone())
+    torch.cuda.synchronize(dev)
+    dec()
+    sbuf.offset_buf.copy_(saved[0])
+    sbuf.seen_tokens.buf.copy_(saved[1])
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        dec()
+    torch.cuda.synchronize(dev)
+
+    def one(i):
+        g_logits.copy_(bufs[i % nbuf])  # the LM head's output, written into the captured buffer
+        sbuf.stage_seen_token_masks(rids, masks)
+        sbuf.gather_for_request_ids(rids, B)
+        graph.replay()
+        sampler.sync_seen_token_masks(masks)
+
+    for i in range(5):
+        one(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    t0 = time.perf_counter()
+    for i in range(steps):
+        one(i)
+    host_us = (time.perf_counter() - t0) / steps * 1e6
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    # the logits copy alone (it stands in for the LM head's write)
+    c0.record()
+    for i in range(steps):
+        g_logits.copy_(bufs[i % nbuf])
+    c1.record()
+    torch.cuda.synchronize(dev)
+    copy_ms = c0.elapsed_time(c1) / steps
+    del graph
+    return {"value": B * world / ((ms - copy_ms) / 1e3), "unit": "rows/s", "us_per_step": (ms - copy_ms) * 1e3,
+            "us_per_step_with_copy": ms * 1e3, "host_us_per_step": host_us,
+            "api": "SamplerBuffers.stage_seen_token_masks / gather_for_request_ids, CUDA-graph replay of "
+                   "CudaGraphableSampler.sample, sync_seen_token_masks; device-resident logits (the time of a "
+                   "device copy standing in for the LM head's write is subtracted)"}
+
+
+def _tp_setup(world, rank, dev, seed):
     import torch
 
     from mstar_rs_b200 import tp as TP
     from mstar_rs_b200 import workloads as W
 
-    dev = torch.device("cuda", local)
-    shard = W.tp_sharded(world, seed=args.seed)[rank]
+    shard = W.tp_sharded(world, seed=seed)[rank]
     d = W.to_device(shard, device=dev)
     base = d.pop("logits")
     off = int(d.pop("vocab_offset", shard.vocab_offset) or 0)
-    V_global = shard.V * world
-    step_bytes = base.numel() * base.element_size()
-    nbuf = max(2, -(-2 * L2_BYTES // step_bytes))
-    bufs = [base] + [torch.roll(base, shifts=997 * i, dims=1).contiguous() for i in range(1, nbuf)]
+    bufs, nbuf = _rotating(base, torch)
+    return shard, d, bufs, nbuf, off
+
+
+def run_tp_single(args, dev, stream):
+    """Vocab-parallel sampling at one rank (B=128, V=152064 bf16): shard
+    records, the exchange (a device copy) and the merge, captured in a graph."""
+    import torch
+
+    from mstar_rs_b200 import tp as TP
+
+    shard, d, bufs, nbuf, off = _tp_setup(1, 0, dev, args.seed)
     B = shard.B
-    gather = None if world > 1 else (lambda recv, send: recv.copy_(send))
-    smp = TP.VocabParallelSampler(B, V_global, world, rank, dev, tp_cap=64, gather=gather)
+    smp = TP.VocabParallelSampler(B, shard.V, 1, 0, dev, tp_cap=64, gather=lambda recv, send: recv.copy_(send))
     out = torch.zeros(B, dtype=torch.int64, device=dev)
-    stream = torch.cuda.current_stream(dev)
-
-    def step(i):
-        smp.sample(bufs[i % nbuf], off, out, **d)
-
-    for i in range(max(3, args.warmup)):
-        step(i)
+    K = 500
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            smp.sample(bufs[i % nbuf], off, out, **d)
     torch.cuda.synchronize(dev)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(nbuf):
+            smp.sample(bufs[i], off, out, **d)
+    reps = max(1, K // nbuf)
+    with torch.cuda.stream(stream):
+        graph.replay()
     torch.cuda.synchronize(dev)
-    K = args.steps
-    # One rank: the exchange is a device copy, so the whole step is captured
-    # once per buffer cycle and replayed (as a decode graph would hold it).
-    # More ranks: eager steps, the NCCL all-gather issued from the host.
-    graphs = []
-    if world == 1:
-        reps, rem = divmod(K, nbuf)
-        cap = torch.cuda.Stream(device=dev)
-        cap.wait_stream(stream)
-        for n in (nbuf, rem):
-            if n == 0:
-                continue
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=cap):
-                for i in range(n):
-                    step(i)
-            graphs.append(g)
-        stream.wait_stream(cap)
-        for g in graphs:  # graph warm-up (uploads the graphs)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / (reps * nbuf)
+    peak, peak_src = _peak()
+    alg = B * shard.V * 2 + shard.hist_ids.nbytes + B * 64
+    del graph
+    return {"name": f"tp1_b{B}_v{shard.V}_bf16", "us_per_step": ms * 1e3, "rows_per_s": B / (ms / 1e3),
+            "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": alg / (ms / 1e3) / 1e9 / peak, "peak_source": peak_src, "algorithmic_bytes": alg},
+            "launch": "CUDA graph: shard records, exchange copy, merge per step"}
+
+
+def run_tp_multi(args, world, rank, local):
+    """The vocabulary-sharded workload over the ranks: per step this rank's
+    shard records, an NCCL all-gather of the records and the merge (every
+    rank gets the same ids), the whole step captured in one CUDA graph.
+    Reported: µs per step (max over ranks) and the all-gather's share."""
+    import torch
+    import torch.distributed as dist
+
+    from mstar_rs_b200 import tp as TP
+
+    dev = torch.device("cuda", local)
+    shard, d, bufs, nbuf, off = _tp_setup(world, rank, dev, args.seed)
+    B = shard.B
+    smp = TP.VocabParallelSampler(B, shard.V * world, world, rank, dev, tp_cap=64, group=dist.group.WORLD)
+    out = torch.zeros(B, dtype=torch.int64, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            smp.sample(bufs[i % nbuf], off, out, **d)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(nbuf):
+            smp.sample(bufs[i], off, out, **d)
+    send = smp.send[: B * smp.words]
+    recv = smp.recv[: world * B * smp.words]
+    ag = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ag, stream=stream):
+        for i in range(nbuf):
+            dist.all_gather_into_tensor(recv, send)
+    reps = max(1, 400 // nbuf)
+
+    def timed(g):
+        with torch.cuda.stream(stream):
             g.replay()
         torch.cuda.synchronize(dev)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    if graphs:
-        for _ in range(reps):
-            graphs[0].replay()
-        if rem:
-            graphs[-1].replay()
-    else:
-        for i in range(K):
-            step(i)
-    t1.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = t0.elapsed_time(t1)
-    if world > 1:
         dist.barrier()
-        tt = torch.tensor([ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) / (reps * nbuf)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = timed(graph)
+    ag_ms = timed(ag)
+    ids_ok = torch.tensor([1], device=dev)
+    ref = out.clone()
+    dist.broadcast(ref, src=0)
+    ids_ok[0] = int(torch.equal(ref, out))
+    dist.all_reduce(ids_ok, op=dist.ReduceOp.MIN)
+    del graph, ag
+    return {"workload": f"tp{world}_b{B}_v{shard.V * world}_bf16", "us_per_step": ms * 1e3,
+            "rows_per_s": B / (ms / 1e3), "allgather_us": ag_ms * 1e3, "allgather_share": ag_ms / ms,
+            "record_bytes_per_rank": B * smp.words * 4, "ids_identical_on_every_rank": bool(ids_ok.item()),
+            "scaling": "strong", "launch": "one CUDA graph per cycle: tp_local, NCCL all-gather, tp_merge"}
+
+
+def run_dp_split(args, world, rank, local):
+    """The constrained workload's 512 rows split evenly across the ranks (no
+    collective on the data path); µs per step is the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local)
+    full = make_case("constrained", 0, args.seed)
+    per = full.B // world
+    case = full.row_slice(rank * per, (rank + 1) * per)
+    case.name = f"constrained_b{full.B}_split{world}"
+    stream = torch.cuda.Stream(device=dev)
+    t = time_graph_steps(case, dev, stream, 100, 5)
+    dist.barrier()
+    ms = replay_ms(t, stream, dev) / 100
+    tt = torch.tensor([ms], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    del t
+    return {"workload": case.name, "rows_per_rank": per, "us_per_step": ms * 1e3, "rows_per_s": full.B / (ms / 1e3),
+            "scaling": "strong"}
+
+
+def run_tp_line(args, world, rank, local):
+    """--workload tp: the vocabulary-sharded workload as the line itself
+    (strong scaling over the ranks)."""
+    import torch
+
+    dev = torch.device("cuda", local)
+    if world == 1:
+        r = run_tp_single(args, dev, torch.cuda.Stream(device=dev))
+        r["workload"] = r.pop("name")
+    else:
+        r = run_tp_multi(args, world, rank, local)
     if rank != 0:
         return
+    case = make_case("tp", 0, args.seed)
     print(json.dumps({
-        "metric": METRIC, "value": B * K / (ms / 1e3), "unit": "rows/s", "n_gpus": world, "steps": K,
-        "warmup": args.warmup, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+        "metric": "vocab-parallel sampled rows/sec at B=128, V=152064 bf16", "value": r["rows_per_s"],
+        "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": r["us_per_step"] / 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"tp{world}_b{B}_v{V_global}_bf16", "B": B, "V": V_global, "logits_dtype": "bf16",
-                   "history": int(shard.hist_ids.shape[1]), "parallelism": f"tp{world}",
-                   "launch": ("CUDA graph replay: shard records, exchange copy, merge per step" if graphs
-                              else "eager: shard records, NCCL all-gather, merge per step"),
-                   "l2": f"{nbuf} rotating shard buffers ({nbuf * step_bytes / 2**20:.0f} MiB > 2x L2)"},
-        "gpu_launches": 2 * K,
+        "config": dict(config_of(case, world), workload=r["workload"], parallelism=f"tp{world}"), "tp": r,
+        "gpu_launches": 2,
     }), flush=True)
 
 
@@ -563,7 +806,7 @@ def main():
         if args.impl == "reference":
             run_reference(args, world, rank)
         elif args.workload == "tp":
-            run_tp(args, world, rank, local)
+            run_tp_line(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:

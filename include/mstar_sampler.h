@@ -163,6 +163,19 @@ int mstar_sampler_tp_local(const mstar_sampler_params_t *p, int32_t tp_cap, uint
 int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world,
                            int64_t V_global, const uint32_t *recv, void *stream);
 
+/* State updates for ids chosen elsewhere: for every row r of [0, p->B)
+ * whose slot (slot_idx[r], or r) is >= 0 and whose id ids[r] lies in
+ * [vocab_offset, vocab_offset + V): append the id to the slot's history ring
+ * (MSTAR_FLAG_UPDATE_HISTORY), set its seen bit (MSTAR_FLAG_UPDATE_SEEN),
+ * advance the slot's RNG offset (MSTAR_FLAG_ADVANCE_OFFSET) and flag a stop
+ * id (stop_ids / stop_flags), exactly as a step that sampled those ids would.
+ * Used after the tensor-parallel broadcast of rank 0's ids (the reference's
+ * tp_group broadcast, python/mstar_rs/models/qwen3_omni.py:401-404), so the
+ * per-slot state of every rank takes the same ids; also for ids an engine
+ * appends itself (SeenTokenMask.add_tokens, orpheus.py:500).  Reads only the
+ * fields named here; logits may be NULL.  ids: [B] int64 (device). */
+int mstar_sampler_commit(const mstar_sampler_params_t *p, const int64_t *ids, void *stream);
+
 /* The sampler's Philox4x32-10 uniform for (seed, offset), computed on the
  * host; lets callers reproduce a draw without a device. */
 float mstar_sampler_philox_uniform(uint64_t seed, uint64_t offset);

@@ -62,7 +62,7 @@ _lock = threading.Lock()
 EXPORTS = (
     "mstar_sampler_abi_version", "mstar_sampler_last_error", "mstar_sampler_plan",
     "mstar_sampler_step", "mstar_sampler_tp_record_words", "mstar_sampler_tp_local",
-    "mstar_sampler_tp_merge", "mstar_sampler_philox_uniform",
+    "mstar_sampler_tp_merge", "mstar_sampler_philox_uniform", "mstar_sampler_commit",
 )
 
 
@@ -91,6 +91,8 @@ def lib() -> ctypes.CDLL:
         L.mstar_sampler_tp_local.restype = ctypes.c_int
         L.mstar_sampler_tp_merge.argtypes = [ctypes.POINTER(Params), I32, I32, I64, P, P]
         L.mstar_sampler_tp_merge.restype = ctypes.c_int
+        L.mstar_sampler_commit.argtypes = [ctypes.POINTER(Params), P, P]
+        L.mstar_sampler_commit.restype = ctypes.c_int
         L.mstar_sampler_philox_uniform.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
         L.mstar_sampler_philox_uniform.restype = ctypes.c_float
         if L.mstar_sampler_abi_version() != ABI_VERSION:

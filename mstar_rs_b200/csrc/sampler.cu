@@ -969,6 +969,17 @@ constexpr int HT_MASKED = 1 << 30;
 __device__ __forceinline__ int ht_insert(int2 *ht, int cap, int e, int c, int &slot) {
   uint32_t h = ht_hash((uint32_t)e, cap);
   for (int probe = 0; probe < cap; ++probe) {
+    // a key never changes once set: seen already, it needs no compare-and-swap
+    const int seen = *reinterpret_cast<volatile int *>(&ht[h].x);
+    if (seen == e) {
+      if (c) atomicAdd(&ht[h].y, c);
+      slot = (int)h;
+      return 0;
+    }
+    if (seen != -1) {
+      h = (h + 1) & (uint32_t)(cap - 1);
+      continue;
+    }
     const int prev = atomicCAS(&ht[h].x, -1, e);
     if (prev == -1 || prev == e) {
       if (c) atomicAdd(&ht[h].y, c);
@@ -2248,9 +2259,14 @@ __global__ void __launch_bounds__(NT, 1)
   // are in the seen map (and the skip bitmap) already.
   auto for_each_special = [&](auto &&fn) {
     if (has_hist) {
+#pragma unroll
+      for (int u = 0; u < HP; ++u) {
+        const int64_t g = (int64_t)hpre[u] - gbase;
+        if (u * NT + tid < hlen && g >= c0 && g < c1) fn(g, 1);
+      }
       const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
-      for (int j = tid, u = 0; j < hlen; j += NT, ++u) {
-        const int64_t g = (int64_t)(u < HP ? (u == 0 ? hpre[0] : hpre[1]) : h[j]) - gbase;
+      for (int j = HP * NT + tid; j < hlen; j += NT) {
+        const int64_t g = (int64_t)h[j] - gbase;
         if (g >= c0 && g < c1) fn(g, 1);
       }
     }
@@ -2315,18 +2331,29 @@ __global__ void __launch_bounds__(NT, 1)
       if (valid) spec_max = fmaxf(spec_max, c.x);
     });
   };
+  uint32_t taint = 0;  // register tile: the vectors holding a skipped position
   if (rt) {
+    // each vector's raw max (a few instructions) and its copy to shared
+    // memory; vectors with a skipped position (special or disallowed; rare
+    // without an allowed mask) are then reduced again, masked, from shared
+    // memory, and always rescanned by the candidate pass
 #pragma unroll
     for (int i = 0; i < NVR; ++i) {
-      const int q = i * NT + tid, k = hv + q;
+      const int q = i * NT + tid;
+      if (q < nbv && Elem<T>::bits_of(L.skip, hv + q)) taint |= 1u << i;
+    }
+#pragma unroll
+    for (int i = 0; i < NVR; ++i) {
+      const int q = i * NT + tid;
       gm[i] = Elem<T>::acc_init();
       if (q < nbv) {
-        const uint32_t b = Elem<T>::bits_of(L.skip, k);
-        gm[i] = Elem<T>::vred(b ? Elem<T>::mask_out(rv[i], b) : rv[i]);
-        data4[k] = rv[i];
+        gm[i] = Elem<T>::vred(rv[i]);
+        data4[hv + q] = rv[i];
+        if (!((taint >> i) & 1u)) racc = Elem<T>::acc_max(racc, gm[i]);
       }
-      racc = Elem<T>::acc_max(racc, gm[i]);
     }
+    for (uint32_t t = taint; t; t &= t - 1u)
+      racc = Elem<T>::acc_max(racc, Elem<T>::vred(load_masked<T>(sl, hv + (__ffs(t) - 1) * NT + tid)));
   } else {
     constexpr int CV = CHUNK_BYTES / 16;
     for (int j = 0; j < nchunk; ++j) {
@@ -2442,6 +2469,8 @@ __global__ void __launch_bounds__(NT, 1)
         // the tile's vectors whose max reaches the cut, as a bit mask (one
         // compact unrolled test), then one rolled loop over the set bits:
         // the scan's code is instantiated once, not once per vector
+        // (a vector's raw max bounds its masked max: tainted vectors pass
+        // the same test)
         uint32_t pm = 0;
 #pragma unroll
         for (int i = 0; i < NVR; ++i)
@@ -2685,6 +2714,24 @@ __global__ void __launch_bounds__(NT, 1)
     debug_dense<T>(ctx, sh);
   }
   if (!fast || debug) cluster.sync();  // keep shared memory alive until every remote access is done
+}
+
+// ------------------------------------------------------------ commit
+
+// State updates for ids chosen elsewhere: one thread per row.  Ids outside
+// [vocab_offset, vocab_offset + V) change nothing.
+__global__ void __launch_bounds__(128) commit_kernel(const mstar_sampler_params_t p, const int64_t *ids) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= p.B) return;
+  const int slot = p.slot_idx ? p.slot_idx[row] : row;
+  const int64_t id = ids[row];
+  if (slot < 0 || id < p.vocab_offset || id >= p.vocab_offset + p.V) return;
+  mstar_sampler_params_t q = p;
+  q.out_ids = nullptr;
+  q.out_ids32 = nullptr;
+  q.out_status = nullptr;
+  q.uniforms = nullptr;  // (the offset advances when asked to)
+  write_row_outputs(q, row, slot, (uint32_t)id, 0u);
 }
 
 // ------------------------------------------------------------ TP merge
@@ -3070,6 +3117,28 @@ int mstar_sampler_tp_local(const mstar_sampler_params_t *p, int32_t tp_cap, uint
     return fail(MSTAR_ERR_UNSUPPORTED, "dense debug outputs are single-shard only");
   q.flags &= ~(MSTAR_FLAG_UPDATE_HISTORY | MSTAR_FLAG_UPDATE_SEEN | MSTAR_FLAG_ADVANCE_OFFSET);
   return launch(&q, 1, tp_cap, send, static_cast<cudaStream_t>(stream));
+}
+
+int mstar_sampler_commit(const mstar_sampler_params_t *p, const int64_t *ids, void *stream) {
+  if (!p) return fail(MSTAR_ERR_INVALID, "params is NULL");
+  if (!ids) return fail(MSTAR_ERR_INVALID, "ids is NULL");
+  if (p->B < 1 || p->B > (1 << 24)) return fail(MSTAR_ERR_INVALID, "B must be in [1, 2^24]");
+  if (p->V < 1 || p->vocab_offset < 0 || p->vocab_offset + p->V > 0x7FFFFFFFLL)
+    return fail(MSTAR_ERR_INVALID, "V / vocab_offset out of range");
+  if (p->num_slots < 1 || (!p->slot_idx && p->num_slots < p->B))
+    return fail(MSTAR_ERR_INVALID, "num_slots must cover the rows");
+  if ((p->flags & MSTAR_FLAG_UPDATE_HISTORY) && (!p->hist_ids || !p->hist_len || p->H < 1))
+    return fail(MSTAR_ERR_INVALID, "UPDATE_HISTORY needs hist_ids, hist_len and H >= 1");
+  if ((p->flags & MSTAR_FLAG_UPDATE_SEEN) && (!p->seen_bits || p->seen_words * 32 < p->vocab_offset + p->V))
+    return fail(MSTAR_ERR_INVALID, "UPDATE_SEEN needs seen_bits covering the vocabulary");
+  if ((p->flags & MSTAR_FLAG_ADVANCE_OFFSET) && !p->offset)
+    return fail(MSTAR_ERR_INVALID, "ADVANCE_OFFSET needs offset");
+  if (p->stop_ids && p->NS < 1) return fail(MSTAR_ERR_INVALID, "NS must be >= 1 with stop_ids");
+  if (p->stop_flags && !p->stop_ids) return fail(MSTAR_ERR_INVALID, "stop_flags needs stop_ids");
+  commit_kernel<<<(p->B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(*p, ids);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return MSTAR_OK;
 }
 
 int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world, int64_t V_global,

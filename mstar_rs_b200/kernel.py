@@ -164,3 +164,35 @@ def tp_merge(logits: torch.Tensor, tp_cap: int, tp_world: int, V_global: int, re
         N.check(N.lib().mstar_sampler_tp_merge(ctypes.byref(p), tp_cap, tp_world, V_global,
                                                ctypes.c_void_p(recv.data_ptr()), ctypes.c_void_p(stream)),
                 "mstar_sampler_tp_merge")
+
+
+def commit(ids: torch.Tensor, *, V: int, num_slots: int, slot_idx=None, hist_ids=None, hist_len=None,
+           seen_bits=None, stop_ids=None, stop_flags=None, offset=None, flags=0, vocab_offset=0) -> None:
+    """Per-slot state updates for ids chosen elsewhere (mstar_sampler_commit):
+    history append / seen bit / RNG offset as `flags` selects, stop flags."""
+    if ids.dtype != torch.int64 or ids.dim() != 1 or not ids.is_cuda or not ids.is_contiguous():
+        raise ValueError("ids must be a contiguous 1-D int64 CUDA tensor")
+    dev = ids.device
+    B = ids.shape[0]
+    _need(slot_idx, "slot_idx", torch.int32, dev, B)
+    _need(hist_len, "hist_len", torch.int32, dev, num_slots)
+    _need(offset, "offset", _U64, dev, num_slots)
+    _need(stop_flags, "stop_flags", torch.int32, dev, num_slots)
+    _need(hist_ids, "hist_ids", torch.int32, dev, num_slots, 2)
+    _need(seen_bits, "seen_bits", torch.int32, dev, num_slots, 2)
+    _need(stop_ids, "stop_ids", torch.int32, dev, num_slots, 2)
+    p = N.Params()
+    p.B, p.V, p.num_slots, p.vocab_offset = B, V, num_slots, vocab_offset
+    p.slot_idx = _ptr(slot_idx)
+    p.hist_ids, p.hist_len = _ptr(hist_ids), _ptr(hist_len)
+    p.H = 0 if hist_ids is None else hist_ids.shape[1]
+    p.seen_bits = _ptr(seen_bits)
+    p.seen_words = 0 if seen_bits is None else seen_bits.shape[1]
+    p.stop_ids, p.stop_flags = _ptr(stop_ids), _ptr(stop_flags)
+    p.NS = 0 if stop_ids is None else stop_ids.shape[1]
+    p.offset = _ptr(offset)
+    p.flags = flags
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        N.check(N.lib().mstar_sampler_commit(ctypes.byref(p), ctypes.c_void_p(ids.data_ptr()),
+                                             ctypes.c_void_p(stream)), "mstar_sampler_commit")

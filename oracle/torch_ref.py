@@ -184,3 +184,93 @@ def run(case, drop_tiny: bool = True):
         t, k, p, xr = sample_row(case, r, drop_tiny=drop_tiny)
         ids[r], kept[r], probs[r], x[r] = t, k.numpy(), p.numpy(), xr.numpy()
     return dict(ids=ids, kept=kept, probs=probs, x=x)
+
+
+def run_batched(case, drop_tiny: bool = True):
+    """The same formulation as `sample_row`, vectorised over the rows of the
+    batch (batched sort, cumsum and searchsorted use torch's intra-op
+    threads): the timed CPU baseline.  Its float64 sums run over whole rows,
+    so on a boundary it may round differently from `sample_row`; the
+    comparison tests use `sample_row`."""
+    B, V = case.B, case.V
+    goff = case.vocab_offset
+    slots = np.arange(B) if case.slot_idx is None else case.slot_idx.astype(np.int64)
+    live_row = slots >= 0
+    sl = np.where(live_row, slots, 0)
+    g = lambda a, d: np.full(B, d) if a is None else np.asarray(a)[sl]  # noqa: E731
+    v = torch.from_numpy(np.ascontiguousarray(case.logits_f32()).copy())
+    rows = torch.arange(B)
+    if case.bias_ids is not None:
+        for k in range(case.bias_ids.shape[1]):  # list order
+            ids = case.bias_ids[sl, k].astype(np.int64) - goff
+            ok = (ids >= 0) & (ids < V)
+            r = rows[torch.from_numpy(ok)]
+            c = torch.from_numpy(ids[ok])
+            v[r, c] = v[r, c] + torch.from_numpy(case.bias_vals[sl, k][ok].astype(np.float32))
+    cnt = torch.zeros(B, V, dtype=torch.int64)
+    if case.hist_ids is not None:
+        H = case.hist_ids.shape[1]
+        hid = torch.from_numpy(case.hist_ids[sl].astype(np.int64)) - goff
+        hl = torch.from_numpy(np.minimum(case.hist_len[sl], H).astype(np.int64))
+        ok = (torch.arange(H)[None, :] < hl[:, None]) & (hid >= 0) & (hid < V)
+        cnt.scatter_add_(1, torch.where(ok, hid, 0), ok.to(torch.int64))
+    elif case.seen_bits is not None:
+        bits = np.unpackbits(case.seen_bits[sl].astype(np.uint32).view(np.uint8), axis=1, bitorder="little")
+        cnt = torch.from_numpy(bits[:, goff:goff + V].astype(np.int64))
+    R = torch.from_numpy(g(case.rep_pen, 1.0).astype(np.float32))[:, None]
+    F = torch.from_numpy(g(case.freq_pen, 0.0).astype(np.float32))[:, None]
+    P = torch.from_numpy(g(case.pres_pen, 0.0).astype(np.float32))[:, None]
+    pen = torch.where(v > 0, v / R, v * R) - F * cnt.to(torch.float32) - P
+    v = torch.where(cnt > 0, pen, v)
+    ok = ~torch.isnan(v)
+    if case.allowed_bits is not None:
+        bits = np.unpackbits(case.allowed_bits[sl].astype(np.uint32).view(np.uint8), axis=1, bitorder="little")
+        ok &= torch.from_numpy(bits[:, goff:goff + V].astype(bool))
+    v = torch.where(ok, v, torch.tensor(-float("inf")))
+    T = g(case.temperature, 1.0).astype(np.float32)
+    K = g(case.top_k, 0).astype(np.int64)
+    greedy = ~(T >= 1e-5)
+    invT = np.where(greedy, np.float32(1.0), np.float32(1.0) / np.where(greedy, np.float32(1.0), T))
+    x = v * torch.from_numpy(invT.astype(np.float32))[:, None]
+    ids = np.full(B, goff, np.int64)
+    empty = ~(ok.any(1) & (v.max(1).values > -float("inf"))).numpy()
+    one = greedy | (K == 1)
+    am = torch.argmax(x, dim=1).numpy()
+    ids[one & ~empty] = am[one & ~empty] + goff
+    rest = live_row & ~one & ~empty
+    if rest.any():
+        ri = torch.from_numpy(np.flatnonzero(rest))
+        xs, order = torch.sort(x[ri], dim=1, descending=True, stable=True)
+        xs = xs.to(torch.float64)
+        m = xs[:, :1]
+        logp = torch.where(xs == m, torch.zeros_like(xs), xs - m)
+        pos = torch.arange(V)[None, :]
+        Kr = torch.from_numpy(np.where((K[rest] > 0) & (K[rest] < V), K[rest], V))[:, None]
+        alive = torch.isfinite(logp) & (pos < Kr)
+        if drop_tiny:
+            alive &= logp >= TINY_LOG
+        Mp = g(case.min_p, 0.0)[rest].astype(np.float64)
+        lmp = torch.from_numpy(np.where(Mp > 0, np.log(np.minimum(np.where(Mp > 0, Mp, 1.0), 1.0)), -np.inf))[:, None]
+        alive &= logp >= lmp
+        nA = torch.cumprod(alive.to(torch.int64), dim=1).sum(1, keepdim=True)
+        inA = pos < nA
+        w = torch.where(inA, torch.exp(logp), torch.zeros_like(logp))
+        pA = w / w.sum(1, keepdim=True).clamp_min(1e-300)
+        Pt = torch.from_numpy(g(case.top_p, 1.0)[rest].astype(np.float64))[:, None]
+        excl = torch.cumsum(pA, 1) - pA
+        keep = ((excl < Pt) | (pos == 0)) & inA
+        nK = torch.where(Pt < 1.0, keep.sum(1, keepdim=True), nA)
+        wk = torch.where(pos < nK, w, torch.zeros_like(w))
+        pk = wk / wk.sum(1, keepdim=True).clamp_min(1e-300)
+        if case.uniforms is not None:
+            u = case.uniforms[np.flatnonzero(rest)].astype(np.float64)
+        else:
+            u = np.array([_philox_uniform(int(g(case.seed, 0)[i]), int(g(case.offset, 0)[i]))
+                          for i in np.flatnonzero(rest)], np.float64)
+        cum = torch.cumsum(pk, 1)
+        j = torch.searchsorted(cum, torch.from_numpy(u)[:, None], right=True)
+        j = torch.minimum(j, (nK - 1).clamp_min(0))
+        tok = torch.gather(order, 1, j)[:, 0]
+        tok = torch.where(nA[:, 0] > 0, tok, order[:, 0])
+        ids[rest] = tok.numpy() + goff
+    return dict(ids=ids)

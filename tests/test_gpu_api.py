@@ -261,3 +261,129 @@ def test_stop_flags(oracle_lib):
         seen |= stop_hits(refs[s], table)
     assert sampler.stopped() == [r for r, h in zip(rids, seen) if h]
     assert sampler.stopped() == []
+
+
+def test_captured_step_has_no_host_sync():
+    """An Orpheus-shaped decode step (static hidden states -> LM head ->
+    in-graph sampler) captured once and replayed 100 times with the
+    engine's stage / gather / sync around every replay, under
+    torch.cuda.set_sync_debug_mode("error"): no call on the path waits for
+    the device, including the steps where a request leaves and another
+    takes its row.  Every request's RNG offset then equals its step count."""
+    import torch
+
+    from mstar_rs_b200 import sampling
+
+    n, V, d = 8, 4099, 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    W = torch.randn(V, d, device="cuda", generator=g).to(torch.bfloat16)
+    hidden = torch.zeros(n, d, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros(n, dtype=torch.int64, device="cuda")
+    sbuf = sampling.SamplerBuffers.allocate(n, "cuda", vocab_size=V)
+    pool = [f"q{i}" for i in range(n + 6)]
+    masks, steps = {}, {}
+
+    def admit(rid):
+        c = sampling.SamplingConfig(vocab_size=V, temperature=0.9, top_p=0.9, repetition_penalty=1.3)
+        c.set_seed(hash(rid) & 0xFFFF)
+        sbuf.register_request(rid, c)
+        masks[rid] = sampling.SeenTokenMask.new(rid, V, "cuda")
+        steps[rid] = 0
+
+    rids = pool[:n]
+    for r in rids:
+        admit(r)
+    sbuf.stage_seen_token_masks(rids, [masks[r] for r in rids])
+    sampler = sbuf.gather_for_request_ids(rids, n, gather_seen_tokens=True)
+
+    def dec():
+        logits = hidden @ W.t()  # [n, V], the LM head
+        out.copy_(sampler.sample(rids, logits, apply_penalty=True))
+
+    saved_off = sbuf.offset_buf[:n].clone()
+    saved_seen = sbuf.seen_tokens.buf[:n].clone()
+    torch.cuda.synchronize()
+    for _ in range(2):
+        dec()
+    sbuf.offset_buf[:n].copy_(saved_off)
+    sbuf.seen_tokens.buf[:n].copy_(saved_seen)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        dec()
+    torch.cuda.synchronize()
+    waiting = pool[n:]
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        for step in range(100):
+            if step % 17 == 16 and waiting:  # a request leaves, another takes its row
+                j = step % n
+                gone = rids[j]
+                sbuf.unregister_request(gone)
+                rids[j] = waiting.pop(0)
+                admit(rids[j])
+            hidden.normal_(generator=g)
+            cur = [masks[r] for r in rids]
+            sbuf.stage_seen_token_masks(rids, cur)
+            sbuf.gather_for_request_ids(rids, n, gather_seen_tokens=True)
+            graph.replay()
+            sampler.sync_seen_token_masks(cur)
+            for r in rids:
+                steps[r] += 1
+    finally:
+        torch.cuda.set_sync_debug_mode(0)
+    torch.cuda.synchronize()
+    off = sbuf.offset_buf[:n].cpu().tolist()
+    assert off == [steps[r] for r in rids]
+    tok = out.cpu().numpy()
+    assert ((tok >= 0) & (tok < V)).all()
+    for j, r in enumerate(rids):  # the last sampled id is in its request's seen mask
+        assert bool(masks[r].to_bool()[int(tok[j])])
+
+
+def test_tp_group_commit():
+    """Under a tensor-parallel group the sampled ids are replaced by rank
+    0's (here a stand-in group whose broadcast writes fixed ids) before the
+    per-slot state takes them: history, seen bits and stop flags follow the
+    broadcast ids, not the locally sampled ones."""
+    import torch
+
+    from mstar_rs_b200 import sampling
+
+    n, V = 4, 3001
+    forced = torch.tensor([5, 17, 2999, 1234], dtype=torch.int64, device="cuda")
+
+    class Group:
+        world_size = 2
+
+        def broadcast(self, t, src):
+            t.copy_(forced)
+
+    # eager Sampler (history ring)
+    smp = sampling.Sampler(device="cuda", tp_group=Group(), history=8)
+    rids = [f"t{i}" for i in range(n)]
+    for i, r in enumerate(rids):
+        smp.add_request(r)
+        smp.set_config(r, temperature=1.0, stop_token_ids=[int(forced[i])] if i % 2 == 0 else [3])
+    x = torch.randn(n, V, device="cuda")
+    tok = smp.sample(rids, x)
+    assert tok.tolist() == forced.tolist()
+    idx = [smp._slot[r] for r in rids]
+    assert smp.hist[idx, 0].tolist() == forced.tolist()
+    assert smp.hist_len[idx].tolist() == [1] * n
+    assert smp.offset[idx].tolist() == [1] * n
+    assert smp.stopped(rids) == rids[::2]
+    # SamplerBuffers (seen bits)
+    sbuf = sampling.SamplerBuffers(n, "cuda", tp_group=Group(), vocab_size=V)
+    for r in rids:
+        sbuf.register_request(r, sampling.SamplingConfig(vocab_size=V, temperature=1.0))
+    masks = [sampling.SeenTokenMask.new(r, V, "cuda") for r in rids]
+    sbuf.stage_seen_token_masks(rids, masks)
+    s = sbuf.gather_for_request_ids(rids, n)
+    tok = s.sample(rids, x)
+    assert tok.tolist() == forced.tolist()
+    s.sync_seen_token_masks(masks)
+    for m, t in zip(masks, forced.tolist()):
+        b = m.to_bool()
+        assert bool(b[t]) and int(b.sum()) == 1
+    assert sbuf.offset_buf[:n].tolist() == [1] * n

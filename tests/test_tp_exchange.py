@@ -93,3 +93,36 @@ def test_gloo_exchange_two_ranks(oracle_lib, tmp_path):
         got.append(_merge_all(recv, full))
     np.testing.assert_array_equal(got[0], got[1])  # every rank draws the same ids
     np.testing.assert_array_equal(got[0], ref)
+
+
+def _agree_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    from mstar_rs_b200.sampling import _tp_agree, _tp_world
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        ids = torch.tensor([1, 2, 3]) if rank == 0 else torch.tensor([9, 9, 9])
+        _tp_agree(dist.group.WORLD, ids)
+        q.put((rank, _tp_world(dist.group.WORLD), ids.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_group_broadcast_gloo():
+    """The tp_group agreement step (rank 0's ids on every rank) over a
+    world-size-2 gloo group on 127.0.0.1."""
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_agree_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got == [(0, 2, [1, 2, 3]), (1, 2, [1, 2, 3])]
