@@ -289,8 +289,9 @@ def time_graph_steps(case, dev, stream, steps, warmup, cluster=0, restore_histor
 
     d = W.to_device(case, device=dev, with_uniforms=False)
     if d.get("seed") is None:
-        d["seed"] = torch.arange(case.B, dtype=torch.int64, device=dev) + 12345
-        d["offset"] = torch.zeros(case.B, dtype=torch.int64, device=dev)
+        slots = case.temperature.shape[0] if case.temperature is not None else case.B
+        d["seed"] = torch.arange(slots, dtype=torch.int64, device=dev) + 12345
+        d["offset"] = torch.zeros(slots, dtype=torch.int64, device=dev)
     base = d.pop("logits")
     bufs, nbuf = _rotating(base, torch)
     out = torch.zeros(case.B, dtype=torch.int64, device=dev)

@@ -2716,6 +2716,366 @@ __global__ void __launch_bounds__(NT, 1)
   if (!fast || debug) cluster.sync();  // keep shared memory alive until every remote access is done
 }
 
+// ------------------------------------------------------------ small rows
+
+// Rows of at most SMALL_V ids (a codec vocabulary sampled over and over in
+// the Talker's per-frame depth loop, python/mstar_rs/models/qwen3_omni.py:
+// 1085-1094) take a kernel of their own: one CTA per row, the row in
+// registers (SMALL_EPT ids per thread), occurrence counts in a dense
+// shared-memory array instead of the hash table, every candidate (x >= the
+// value threshold) gathered once and ordered by the large-row tail's bucket
+// sort (pairwise ranking up to 256 candidates), then the same resolution.
+// No cluster, no bulk copies, no general path: a handful of block-wide steps.
+constexpr int SMALL_V = 4096;
+constexpr int SMALL_EPT = SMALL_V / NT;  // ids per thread
+// counts (later the tail's positions) | biased-id bitmap | keys, weights,
+// ranked keys, ranked weights, prefixes | bucket counts, masses | bias list
+constexpr int SMALL_OFF_BMARK = SMALL_V * 4;
+constexpr int SMALL_OFF_K = SMALL_OFF_BMARK + SMALL_V / 8;
+constexpr int SMALL_OFF_BC = SMALL_OFF_K + 5 * SMALL_V * 8;
+constexpr int SMALL_OFF_BIAS = SMALL_OFF_BC + NBK * 12;
+constexpr int SMALL_SMEM = SMALL_OFF_BIAS + BIAS_SMEM * 8;
+static_assert(SMALL_V % NT == 0, "small rows: whole ids per thread");
+static_assert(SMALL_V <= 65536 && NBK % NT == 0, "small rows: tail positions and bucket scan");
+
+// Value-bucket sort of a small row's n <= SMALL_V gathered candidates:
+// SMALL_NBUC buckets uniform in x over the A range below the row max (as
+// tail_bucket_sort, eight times finer: a row of SMALL_V Gaussian values puts
+// a handful in each), a counting pass, a block scan of the counts, a scatter
+// into bucket order and a rank inside each bucket.  Leaves keys, weights and
+// exclusive weight prefixes in rank order in K / W / RS (the gathered
+// arrays are dead after the scatter; RK / RW hold the bucket order, RS the
+// bucket counts and starts until the prefix pass).  Returns false, having
+// sorted nothing, when a bucket of A holds more than BUCKET_MAX candidates
+// (runs of exact ties).  Block-wide; ends with a barrier.
+constexpr int SMALL_NBUC = 2048;
+static_assert(SMALL_NBUC % NT == 0 && SMALL_NBUC * 8 <= SMALL_V * 8, "small rows: bucket scan and counts");
+__device__ bool small_bucket_sort(const Row &r, uint32_t km, int n, const TailScr &s, CtaSh &sh) {
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const float m = okey_inv(km);
+  const float span = fmaxf(r.minp ? fminf(23.5f, __fadd_rn(-r.lnMp, 0.25f)) : 23.5f, 1e-3f);
+  const float sc = (float)SMALL_NBUC / span;
+  constexpr uint32_t LAST = SMALL_NBUC - 1;  // x at or below m - span * LAST / NBUC: outside A
+  auto bucket_of = [&](uint64_t key) {       // monotone in the key
+    const float x = okey_inv(km - (uint32_t)(key >> 32));
+    const float g = __fmul_rn(__fsub_rn(m, x), sc);
+    return g >= (float)LAST ? LAST : (g > 0.0f ? (uint32_t)g : 0u);
+  };
+  uint32_t *cnt = reinterpret_cast<uint32_t *>(s.RS), *start = cnt + SMALL_NBUC;
+  uint64_t *BK = s.RK, *BW = s.RW;
+  for (int b = t; b < SMALL_NBUC; b += NT) cnt[b] = 0u;
+  __syncthreads();
+  for (int i = t; i < n; i += NT) {
+    const uint32_t b = bucket_of(s.K[i]);
+    s.P[i] = (b << 16) | atomicAdd(&cnt[b], 1u);
+  }
+  __syncthreads();
+  constexpr int PER = SMALL_NBUC / NT;
+  uint32_t c[PER], tot = 0, big = 0;
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    c[q] = cnt[t * PER + q];
+    tot += c[q];
+    big |= (t * PER + q < (int)LAST && c[q] > BUCKET_MAX) ? 1u : 0u;
+  }
+  uint32_t inc = tot;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(~0u, inc, o);
+    if (lane >= o) inc += v;
+  }
+  if (lane == 31) sh.red_u32[wid] = inc;
+  if (__syncthreads_or((int)big)) return false;  // uniform
+  uint32_t run = inc - tot;
+  for (int w = 0; w < wid; ++w) run += sh.red_u32[w];
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    start[t * PER + q] = run;
+    run += c[q];
+  }
+  __syncthreads();
+  // with top_k only the first K ranks are read: buckets starting at or past
+  // rank K are neither placed nor ranked
+  const uint32_t lim = r.topk ? (uint32_t)r.K : 0xFFFFFFFFu;
+  for (int i = t; i < n; i += NT) {
+    const uint32_t pb = s.P[i];
+    if (start[pb >> 16] >= lim) continue;
+    const uint32_t dst = start[pb >> 16] + (pb & 0xFFFFu);
+    BK[dst] = s.K[i];
+    BW[dst] = s.W[i];
+  }
+  __syncthreads();
+  uint32_t placed = (uint32_t)n;
+  if (lim < (uint32_t)n) {
+    int lo = 0, hi = (int)LAST;  // the last bucket whose start is < lim (starts are non-decreasing)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (start[mid] < lim) lo = mid;
+      else hi = mid - 1;
+    }
+    placed = start[lo] + cnt[lo];
+  }
+  for (int q = t; q < (int)placed; q += NT) {  // rank inside the bucket
+    const uint64_t key = BK[q];
+    const uint32_t b = bucket_of(key);
+    const uint32_t st = start[b], en = st + cnt[b];
+    uint32_t rk = (uint32_t)q - st;  // outside A: any order
+    if (b < LAST) {
+      rk = 0;
+      for (uint32_t j = st; j < en; ++j) rk += BK[j] < key ? 1u : 0u;
+    }
+    s.K[st + rk] = key;
+    s.W[st + rk] = BW[q];
+  }
+  __syncthreads();
+  {  // exclusive prefix of the weights in rank order, a segment per thread
+    const int seg = (int)((placed + NT - 1) / NT);
+    const int a0 = min((int)placed, t * seg), a1 = min((int)placed, a0 + seg);
+    uint64_t loc = 0;
+    for (int j = a0; j < a1; ++j) loc += s.W[j];
+    uint64_t tot64;
+    uint64_t run64 = block_exscan_u64(loc, tot64, sh);
+    for (int j = a0; j < a1; ++j) {
+      s.RS[j] = run64;
+      run64 += s.W[j];
+    }
+  }
+  __syncthreads();
+  return true;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NT, 1) small_kernel(const mstar_sampler_params_t p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ CtaSh sh;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  const int V = p.V;
+  const int64_t gbase = p.vocab_offset;
+  uint32_t *cnt = reinterpret_cast<uint32_t *>(smem);
+  uint32_t *bmark = reinterpret_cast<uint32_t *>(smem + SMALL_OFF_BMARK);  // ids with a bias entry
+  int32_t *bid = reinterpret_cast<int32_t *>(smem + SMALL_OFF_BIAS);
+  float *bval = reinterpret_cast<float *>(bid + BIAS_SMEM);
+  TailScr ts;
+  ts.K = reinterpret_cast<uint64_t *>(smem + SMALL_OFF_K);
+  ts.W = ts.K + SMALL_V;
+  ts.RK = ts.W + SMALL_V;
+  ts.RW = ts.RK + SMALL_V;
+  ts.RS = ts.RW + SMALL_V;
+  ts.P = cnt;  // the counts are dead once the transformed values are in registers
+  ts.bc = reinterpret_cast<uint32_t *>(smem + SMALL_OFF_BC);
+  ts.bm = reinterpret_cast<uint64_t *>(smem + SMALL_OFF_BC + NBK * 4);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int slot = p.slot_idx ? p.slot_idx[row] : row;
+  const bool debug = p.out_x || p.out_kept || p.out_probs;
+  if (slot < 0) {
+    if (tid == 0) {
+      if (p.out_ids) p.out_ids[row] = gbase;
+      if (p.out_ids32) p.out_ids32[row] = (int32_t)gbase;
+      if (p.out_status) p.out_status[row] = 0;
+    }
+    for (int i = tid; debug && i < V; i += NT) {
+      const int64_t o = (int64_t)row * V + i;
+      if (p.out_x) p.out_x[o] = -INFINITY;
+      if (p.out_kept) p.out_kept[o] = 0;
+      if (p.out_probs) p.out_probs[o] = 0.0f;
+    }
+    return;
+  }
+  // the row (id i = tid + NT * j), the parameters, the draw
+  const uint8_t *rowp = static_cast<const uint8_t *>(p.logits) + (int64_t)row * p.ld * sizeof(T);
+  float raw[SMALL_EPT];
+#pragma unroll
+  for (int j = 0; j < SMALL_EPT; ++j) {
+    const int i = tid + NT * j;
+    raw[j] = i < V ? Elem<T>::load(rowp, i) : -INFINITY;
+  }
+  if (tid == 0) {
+    sh.n_spec = 0;
+    sh.npass = 0;
+    sh.cnt_k = 0;
+    sh.best = 0xFFFFFFFFu;
+    sh.cmax = okey(-INFINITY);
+    sh.kmin = ~0ull;
+    sh.kmax = 0ull;
+    sh.res.token = 0;
+    sh.res.WK = 0;
+    sh.res.ckK = 0;
+  } else if (tid == 64) {
+    row_init(sh.row, p, row, slot, V);
+  } else if (tid == 32) {
+    sh.u = p.uniforms ? p.uniforms[row]
+                      : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
+  }
+  for (int i = tid; i < SMALL_V; i += NT) cnt[i] = 0u;
+  for (int i = tid; i < SMALL_V / 32; i += NT) bmark[i] = 0u;
+  const bool bias = p.bias_ids && p.bias_vals;
+  const bool bias_smem = bias && p.NB <= BIAS_SMEM;
+  for (int j = tid; bias_smem && j < p.NB; j += NT) {
+    bid[j] = p.bias_ids[(int64_t)slot * p.NB + j];
+    bval[j] = p.bias_vals[(int64_t)slot * p.NB + j];
+  }
+  __syncthreads();
+  // occurrence counts (history ring) and each biased id's first bias entry
+  if (p.hist_ids && p.hist_len) {
+    const int32_t *h = p.hist_ids + (int64_t)slot * p.H;
+    const int hl = min(p.hist_len[slot], p.H);
+    for (int j = tid; j < hl; j += NT) {
+      const int64_t e = (int64_t)h[j] - gbase;
+      if (e >= 0 && e < V) atomicAdd(&cnt[e], 1u);
+    }
+  }
+  if (bias) {
+    const int32_t *bi = p.bias_ids + (int64_t)slot * p.NB;
+    for (int j = tid; j < p.NB; j += NT) {
+      const int32_t id = bias_smem ? bid[j] : bi[j];
+      const int64_t e = (int64_t)id - gbase;
+      if (id >= 0 && e >= 0 && e < V) atomicOr(&bmark[e >> 5], 1u << (e & 31));
+    }
+  }
+  __syncthreads();
+  const Row r = sh.row;
+  const uint32_t *sw = p.seen_bits ? p.seen_bits + (int64_t)slot * p.seen_words : nullptr;
+  const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)slot * p.allowed_words : nullptr;
+  float x[SMALL_EPT];
+  float tmax = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < SMALL_EPT; ++j) {
+    const int i = tid + NT * j;
+    float v = raw[j];
+    x[j] = -INFINITY;
+    if (i >= V) continue;
+    const int64_t g = gbase + i;
+    if (bias && ((bmark[i >> 5] >> (i & 31)) & 1u)) {
+      const int32_t *bi = p.bias_ids + (int64_t)slot * p.NB;
+      const float *bv = p.bias_vals + (int64_t)slot * p.NB;
+      for (int q = 0; q < p.NB; ++q) {  // bias entries in list order
+        const int32_t id = bias_smem ? bid[q] : bi[q];
+        if (id == (int32_t)g) v = __fadd_rn(v, bias_smem ? bval[q] : bv[q]);
+      }
+    }
+    const int c = sw ? (int)((sw[g >> 5] >> (g & 31)) & 1u) : (int)cnt[i];
+    if (c > 0) {
+      v = (v > 0.0f) ? __fdiv_rn(v, r.R) : __fmul_rn(v, r.R);
+      v = __fsub_rn(v, __fmul_rn(r.F, (float)c));
+      v = __fsub_rn(v, r.Pp);
+    }
+    const bool allowed = !aw || ((aw[g >> 5] >> (g & 31)) & 1u);
+    if (v != v) x[j] = v;
+    else if (!allowed) x[j] = -INFINITY;
+    else x[j] = xform(r, v);
+    tmax = fmaxf(tmax, x[j]);
+  }
+  // row max; greedy / top-1: the lowest id at the max
+  for (int o = 16; o; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(~0u, tmax, o));
+  if (lane == 0 && tmax > -INFINITY) atomicMax(&sh.cmax, okey(tmax));
+  __syncthreads();
+  const float m = okey_inv(sh.cmax);
+  const bool empty = !(m > -INFINITY);
+  const bool one = r.greedy || r.K == 1;
+  uint32_t token = (uint32_t)gbase, status = 0;
+  if (empty) {
+    status = MSTAR_STATUS_EMPTY;
+  } else if (one) {
+    uint32_t best = 0xFFFFFFFFu;
+#pragma unroll
+    for (int j = 0; j < SMALL_EPT; ++j)
+      if (x[j] == m) best = min(best, (uint32_t)(gbase + tid + NT * j));
+    best = __reduce_min_sync(~0u, best);
+    if (lane == 0) atomicMin(&sh.best, best);
+    __syncthreads();
+    token = sh.best;
+    if (tid == 0) {
+      sh.res.token = token;
+      sh.res.WK = 4294967296ull;
+      sh.res.ckK = (uint64_t)token;
+    }
+  } else {
+    if (tid < 32) {
+      const float t = choose_theta(r, m);
+      if (lane == 0) sh.theta = t;
+    }
+    __syncthreads();
+    const float theta = sh.theta;
+    const uint32_t km = okey(m);
+    // candidates (x >= theta): order keys and weights, compacted
+    uint32_t mine = 0;
+#pragma unroll
+    for (int j = 0; j < SMALL_EPT; ++j) mine += (x[j] >= theta) ? 1u : 0u;
+    const uint32_t o = warp_reserve(&sh.n_spec, mine);
+    uint64_t kmn = ~0ull, kmx = 0ull;
+    uint32_t np = 0;
+    {
+      uint32_t q = o;
+#pragma unroll
+      for (int j = 0; j < SMALL_EPT; ++j)
+        if (x[j] >= theta) {
+          const uint64_t k = ckey(km, x[j], (uint32_t)(gbase + tid + NT * j));
+          const uint64_t w = weight_A(r, x[j], m);
+          ts.K[q] = k;
+          ts.W[q] = w;
+          ++q;
+          kmn = u64min(kmn, k);
+          kmx = u64max(kmx, k);
+          np += w != 0;
+        }
+    }
+    np = __reduce_add_sync(~0u, np);
+    if (lane == 0 && np) atomicAdd(&sh.npass, np);
+    __syncthreads();  // keys, weights and the pass count complete
+    const int n = (int)sh.n_spec;
+    TailScr rs = ts;  // where the rank-ordered keys / weights / prefixes end up
+    if (n <= RANK_SMALL) {
+      tail_rank_sort(n, ts);
+    } else if (small_bucket_sort(r, km, n, ts, sh)) {
+      rs.RK = ts.K;
+      rs.RW = ts.W;
+    } else {  // long runs of ties: buckets of the order key
+      tail_gather_end(kmn, kmx, 0u, ts, sh);
+      tail_sort(n, ts, sh);
+    }
+    if (n <= NT) {
+      if (tid < 32) tail_resolve_warp(r, sh.u, rs, sh);
+      __syncthreads();
+    } else {
+      tail_resolve(r, sh.u, rs, sh);
+    }
+    token = sh.res.token;
+  }
+  if (tid == 0) {
+    sh.res.m = m;
+    sh.res.greedy = r.greedy;
+    sh.res.empty = empty;
+    write_row_outputs(p, row, slot, token, status);
+  }
+  if (debug) {
+    __syncthreads();
+    const Result res = sh.res;
+    const uint32_t kmm = okey(res.m);
+#pragma unroll
+    for (int j = 0; j < SMALL_EPT; ++j) {
+      const int i = tid + NT * j;
+      if (i >= V) continue;
+      const int64_t o = (int64_t)row * V + i;
+      const uint32_t gid = (uint32_t)(gbase + i);
+      const float xv = x[j];
+      bool kept = false;
+      float prob = 0.0f;
+      if (!empty && xv == xv) {
+        if (one) {
+          kept = gid == token;
+          prob = kept ? 1.0f : 0.0f;
+        } else if (xv > -INFINITY && ckey(kmm, xv, gid) <= res.ckK && weight_A(r, xv, res.m) != 0) {
+          kept = true;
+          prob = (float)__ddiv_rn((double)spec_w_from_e(spec_e(xv, res.m)), (double)res.WK);
+        }
+      }
+      if (p.out_x) p.out_x[o] = xv;
+      if (p.out_kept) p.out_kept[o] = kept ? 1 : 0;
+      if (p.out_probs) p.out_probs[o] = prob;
+    }
+  }
+}
+
 // ------------------------------------------------------------ commit
 
 // State updates for ids chosen elsewhere: one thread per row.  Ids outside
@@ -3067,7 +3427,36 @@ static int launch_T(const mstar_sampler_params_t *p, const Plan &pl, uint32_t *s
   return MSTAR_OK;
 }
 
+// Small rows (V <= SMALL_V, automatic width, no testing flags): the
+// one-CTA-per-row kernel.
+static bool use_small(const mstar_sampler_params_t *p, int mode) {
+  return mode == 0 && p->V <= SMALL_V && p->cluster_size == 0 &&
+         !(p->flags & (MSTAR_FLAG_FORCE_GENERAL | MSTAR_FLAG_TEST_WITHHOLD));
+}
+
+template <typename T>
+static int launch_small(const mstar_sampler_params_t *p, cudaStream_t st) {
+  auto kern = small_kernel<T>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMALL_SMEM);
+  if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p->B, 1, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
+  cfg.dynamicSmemBytes = SMALL_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, *p);
+  if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return MSTAR_OK;
+}
+
 static int launch(const mstar_sampler_params_t *p, int mode, int tp_cap, uint32_t *send, cudaStream_t st) {
+  if (use_small(p, mode))
+    return p->dtype == MSTAR_DTYPE_BF16 ? launch_small<__nv_bfloat16>(p, st) : launch_small<float>(p, st);
   Plan pl;
   int rc = plan_launch(p, mode, tp_cap, pl);
   if (rc) return rc;
@@ -3089,6 +3478,11 @@ const char *mstar_sampler_last_error(void) { return g_last_error.c_str(); }
 int mstar_sampler_plan(const mstar_sampler_params_t *p, int32_t *cluster_size, int64_t *smem_bytes) {
   int rc = validate(p);
   if (rc) return rc;
+  if (use_small(p, 0)) {
+    if (cluster_size) *cluster_size = 1;
+    if (smem_bytes) *smem_bytes = SMALL_SMEM;
+    return MSTAR_OK;
+  }
   Plan pl;
   rc = plan_launch(p, 0, 0, pl);
   if (rc) return rc;

@@ -59,10 +59,14 @@ class SamplingConfig:
     stop_token_ids: tuple | list | None = None
     _owner: object = field(default=None, repr=False, compare=False)
 
+    def __setattr__(self, name, value) -> None:
+        object.__setattr__(self, name, value)
+        owner = self.__dict__.get("_owner")
+        if owner is not None and not name.startswith("_"):  # the sampler re-reads this config
+            owner._mark_dirty()
+
     def set_seed(self, seed) -> None:
         self.seed = None if seed is None else int(seed)
-        if self._owner is not None:
-            self._owner._mark_dirty()
 
     @property
     def greedy(self) -> bool:
@@ -254,10 +258,16 @@ class Sampler:
         self._free = list(range(max_requests - 1, -1, -1))
         self._sampling_config: dict = {}
         self._idx_cache: dict = {}
+        self._dirty = False
 
     def _mark_dirty(self) -> None:
-        for rid, cfg in self._sampling_config.items():
-            self.params.write(self._slot[rid], cfg)
+        self._dirty = True  # a request's config changed: its row is rewritten before the next step
+
+    def _flush(self) -> None:
+        if self._dirty:
+            for rid, cfg in self._sampling_config.items():
+                self.params.write(self._slot[rid], cfg)
+            self._dirty = False
 
     def add_request(self, rid) -> None:
         if rid in self._slot:
@@ -322,6 +332,7 @@ class Sampler:
             logits = logits.unsqueeze(0)
         if logits.shape[0] != n:
             raise ValueError(f"{n} request ids for {logits.shape[0]} logits rows")
+        self._flush()
         self.params.upload()
         out = torch.empty(n, dtype=torch.int64, device=self.device)
         idx = self._index(rids)
@@ -442,6 +453,7 @@ class SamplerBuffers:
         self._row_mask: list = [None] * max_bs  # the mask bound to a row
         self._rows: list = []
         self._cfg: dict = {}
+        self._cfg_dirty = True
         self._samplers: dict = {}
 
     @classmethod
@@ -449,10 +461,13 @@ class SamplerBuffers:
         return cls(max_bs, device, tp_group=tp_group, vocab_size=vocab_size)
 
     def _mark_dirty(self) -> None:
-        pass  # parameters are compared row by row at every gather
+        self._cfg_dirty = True  # a registered config changed: rows are compared at the next gather
 
     def register_request(self, rid, cfg: SamplingConfig) -> None:
+        if cfg._owner is None:
+            object.__setattr__(cfg, "_owner", self)
         self._cfg[rid] = cfg
+        self._cfg_dirty = True
         if rid not in self._req_slot:
             if not self._free:
                 raise RuntimeError(f"SamplerBuffers full ({self.max_requests} requests)")
@@ -480,6 +495,9 @@ class SamplerBuffers:
             self._row_mask[j] = None
 
     def stage_seen_token_masks(self, rids, masks) -> None:
+        masks = list(masks)
+        if masks == self._row_mask[: len(masks)]:  # every mask already lives in its row
+            return
         rows = self.seen_tokens.buf
         moving = [j for j, m in enumerate(masks) if self._row_mask[j] is not m]
         if not moving:
@@ -500,6 +518,9 @@ class SamplerBuffers:
             self._row_mask[j] = m
 
     def _sync_masks(self, rids, masks) -> None:
+        masks = list(masks)
+        if masks == self._row_mask[: len(masks)]:
+            return
         rows = self.seen_tokens.buf
         for j, m in enumerate(masks):
             if self._row_mask[j] is not m:  # not staged here: copy the row back
@@ -508,10 +529,14 @@ class SamplerBuffers:
     def gather_for_request_ids(self, rids, n: int, gather_seen_tokens: bool = True) -> CudaGraphableSampler:
         if len(rids) != n or n > self.max_bs:
             raise ValueError(f"gather of {len(rids)} ids into {n} rows (max {self.max_bs})")
-        for j, rid in enumerate(rids):
-            self.params.write(j, self._cfg[rid])
-        self.params.upload()
-        moved = [j for j, rid in enumerate(rids) if self._row_rid[j] != rid]
+        rids = list(rids)
+        same = rids == self._rows
+        if not same or self._cfg_dirty:
+            for j, rid in enumerate(rids):
+                self.params.write(j, self._cfg[rid])
+            self.params.upload()
+            self._cfg_dirty = False
+        moved = [] if same else [j for j, rid in enumerate(rids) if self._row_rid[j] != rid]
         if moved:
             # RNG offsets: a row's previous request keeps its offset in the
             # per-request table, the arriving request brings its own
@@ -535,12 +560,12 @@ class SamplerBuffers:
             for j in range(n):
                 self._release_row(j)
             self.seen_tokens.buf[:n].zero_()
-        self._rows = list(rids)
+        self._rows = rids
         s = self._samplers.get(n)
         if s is None:
             s = CudaGraphableSampler(self, n)
             self._samplers[n] = s
-        s._rids = list(rids)
+        s._rids = rids
         return s
 
     def stopped(self, rids) -> list:

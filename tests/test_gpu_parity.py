@@ -174,3 +174,43 @@ def test_general_value_bins(oracle_lib, seed):
         assert_parity(g, o, case)
         g = run_gpu(case, cluster_size=cl, flags=N.FLAG_FORCE_GENERAL)
         assert_parity(g, o, case)
+
+
+@pytest.mark.parametrize("B,V,K,P,dtype", [(1, 4096, 0, 1.0, "bf16"), (16, 4096, 0, 1.0, "f32"), (1, 2048, 50, 0.9, "bf16"),
+                                            (8, 3072, 0, 0.8, "f32"), (4, 4096, 1, 1.0, "bf16")])
+def test_small_vocab_rows(oracle_lib, B, V, K, P, dtype):
+    """Talker-shaped rows (a codec vocabulary of at most 4096 ids: one CTA
+    per row; temperature 1, repetition 1.1 over seen ids, top_k off and
+    top_p 1 by default, so every id is a candidate) against the oracle, with
+    history and seen-bit penalties, bias and a mask."""
+    for penalty in ("seen", "hist"):
+        case = random_case(400 + B + V, B=B, V=V, dtype=dtype, penalty=penalty, specials=False, greedy_frac=0.0,
+                           scale=1.0)
+        case.temperature[:] = 1.0
+        case.top_k[:] = K
+        case.top_p[:] = P
+        case.min_p[:] = 0.0
+        case.rep_pen[:] = 1.1
+        o = oracle_lib.run(case, debug=True)
+        g = run_gpu(case)
+        assert_parity(g, o, case)
+
+
+@pytest.mark.parametrize("K,dtype", [(0, "f32"), (20, "bf16"), (0, "bf16")])
+def test_small_vocab_ties(oracle_lib, K, dtype):
+    """Small rows whose logits take a dozen distinct values (long runs of
+    exact ties, ordered by id): the value buckets overflow and the kernel
+    sorts by order key instead."""
+    from mstar_rs_b200.workloads import f32_to_bf16_bits
+
+    case = random_case(77 + K, B=4, V=4096, dtype="f32", penalty="seen", specials=False, greedy_frac=0.0, scale=1.0)
+    q = (np.round(case.logits * 2.0) / 2.0).astype(np.float32)
+    case.logits = f32_to_bf16_bits(q) if dtype == "bf16" else q
+    case.dtype = dtype
+    case.temperature[:] = 1.0
+    case.top_k[:] = K
+    case.top_p[:] = 0.95
+    case.min_p[:] = 0.0
+    o = oracle_lib.run(case, debug=True)
+    g = run_gpu(case)
+    assert_parity(g, o, case)
