@@ -18,7 +18,9 @@ ours:       K steps replayed from CUDA graphs over rotating logits buffers whose
             api_graph: the drop-in CudaGraphableSampler replayed with the
             engine's stage / gather / sync around every replay, device logits.
             per_config (one GPU): every other workload the sampler is measured
-            on, each with its roofline and CPU baseline.
+            on, each with its roofline and CPU baseline.  lmhead (one GPU): the
+            tensor-core LM-head projection + sampling call against cuBLAS + the
+            same sampler step.
             More GPUs (torchrun): the line is data-parallel (each rank its own
             batch, weak scaling); `tp` is the vocabulary-sharded workload over
             the ranks (shard records, NCCL all-gather, merge, captured in one
@@ -441,6 +443,7 @@ def run_ours(args, world, rank, local):
         line["cpu_spec_oracle"] = c_oracle_baseline(case)
     if world == 1 and not args.no_per_config and args.workload == "qwen_mixed":
         line["per_config"] = run_per_config(args, dev, stream, no_cpu=args.no_cpu_baseline)
+        line["lmhead"] = run_lmhead(dev)
     print(json.dumps(line), flush=True)
 
 
@@ -470,6 +473,89 @@ def run_per_config(args, dev, stream, no_cpu=False):
     if not no_cpu:
         tp1["cpu_baseline"] = torch_cpu_baseline(make_case("tp", 0, args.seed), budget_s=3.0, max_rows=8)
     out[tp1.pop("name")] = tp1
+    return out
+
+
+def _graph_us(fn, dev, reps=10, replays=5):
+    """Mean µs of one fn() call, fn captured `reps` times in a CUDA graph."""
+    import torch
+
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(replays):
+            g.replay()
+        e1.record(s)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / (reps * replays)
+    del g
+    return ms * 1e3
+
+
+def run_lmhead(dev, B=64, V=151936, d=2048):
+    """The LM-head projection feeding the sampler (one GPU, the mixed
+    workload's rows and histories, operands whose projection has the mixed
+    workload's logits): the tensor-core projection + sampling call against
+    cuBLAS's bf16 GEMM followed by the same sampler step.  Weights stream
+    from HBM every call (V * d * 2 bytes > L2); the logits stay in L2."""
+    import torch
+
+    from mstar_rs_b200 import kernel
+    from mstar_rs_b200 import workloads as W
+
+    case = W.qwen_mixed(seed=5, B=B, V=V)
+    kw = W.to_device(case, device=dev)
+    kw.pop("logits")
+    hidden, weight = W.lmhead_operands(B, V, d, seed=7, device=dev)
+    logits = torch.empty(B, V, dtype=torch.bfloat16, device=dev)
+    ids = torch.zeros(B, dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    p = kernel.build_params(logits, **kw, out_ids=ids)
+
+    def fused():
+        kernel.lmhead_step(hidden, weight, logits, status=status, **kw, out_ids=ids)
+
+    def gemm():
+        kernel.lmhead_logits(hidden, weight, out=logits, status=status)
+
+    def sampler():
+        kernel.launch_step(p, dev)
+
+    def cublas():
+        torch.matmul(hidden, weight.T, out=logits)
+
+    def cublas_then_sampler():
+        cublas()
+        sampler()
+
+    r = {name: _graph_us(fn, dev) for name, fn in (("fused_us", fused), ("gemm_us", gemm),
+                                                   ("sampler_l2_resident_us", sampler), ("cublas_gemm_us", cublas),
+                                                   ("cublas_then_sampler_us", cublas_then_sampler))}
+    torch.cuda.synchronize(dev)
+    wbytes = V * d * 2
+    alg = wbytes + hidden.numel() * 2 + algorithmic_bytes(case) - B * V * 2  # the logits stay on chip
+    peak, peak_src = _peak()
+    ach = alg / (r["fused_us"] * 1e-6) / 1e9
+    out = {"config": {"B": B, "V": V, "d": d, "dtype": "bf16", "workload": "qwen_mixed rows, projected logits"},
+           **{k: round(v, 2) for k, v in r.items()},
+           "gemm_weights_gbs": wbytes / (r["gemm_us"] * 1e-6) / 1e9,
+           "cublas_weights_gbs": wbytes / (r["cublas_gemm_us"] * 1e-6) / 1e9,
+           "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                        "peak_source": peak_src, "algorithmic_bytes": alg},
+           "status": int(status.item())}
+    del hidden, weight, logits
+    torch.cuda.empty_cache()
     return out
 
 

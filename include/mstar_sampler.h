@@ -176,6 +176,36 @@ int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int3
  * fields named here; logits may be NULL.  ids: [B] int64 (device). */
 int mstar_sampler_commit(const mstar_sampler_params_t *p, const int64_t *ids, void *stream);
 
+/* LM-head projection on the tensor cores: logits[b * ld + v] = sum_k
+ * hidden[b * d + k] * weight[v * d + k] for b < B, v < V; hidden [B, d] and
+ * weight [V, d] bf16 row-major (a Linear's weight), fp32 accumulation,
+ * stored as dtype (MSTAR_DTYPE_F32, or MSTAR_DTYPE_BF16 rounded to nearest
+ * even).  Replaces the `self.lm_head(hidden)` that precedes each sampler
+ * call (python/mstar_rs/models/orpheus.py:349, qwen3_omni.py:517).
+ * B <= 256, d a multiple of 8, both pointers 16-byte aligned.
+ * workspace: NULL, or device scratch of at least
+ * mstar_lmhead_workspace_bytes(B) bytes (256-byte aligned; its contents
+ * need not be preserved between calls, and calls that share it must not
+ * overlap on the GPU).  With it every SM gets an equal share of the weight
+ * stream (split vocabulary tiles are summed through it); without it the
+ * shares are whole 128-id tiles.  status: NULL or a device word that gets
+ * bit 1 if a bounded in-kernel wait ran out. */
+int64_t mstar_lmhead_workspace_bytes(int32_t B);
+int mstar_lmhead_logits(const void *hidden, const void *weight, int32_t B, int32_t V, int32_t d,
+                        void *logits, int32_t dtype, int64_t ld, void *workspace,
+                        int64_t workspace_bytes, uint32_t *status, void *stream);
+
+/* Projection and sampling in one call: mstar_lmhead_logits into p->logits
+ * (which must be writable, [B, ld] of p->dtype, weight [p->V, d] being this
+ * shard's rows), then mstar_sampler_step on it as a programmatic dependent
+ * launch.  The logits are stored with an L2 evict-last policy and the
+ * weight stream is read evict-first, so the step's logits are read back
+ * from L2 rather than from HBM.  Results are those of the two calls made in
+ * turn.  workspace, status: as for mstar_lmhead_logits. */
+int mstar_sampler_lmhead_step(const mstar_sampler_params_t *p, const void *hidden, const void *weight,
+                              int32_t d, void *workspace, int64_t workspace_bytes, uint32_t *status,
+                              void *stream);
+
 /* The sampler's Philox4x32-10 uniform for (seed, offset), computed on the
  * host; lets callers reproduce a draw without a device. */
 float mstar_sampler_philox_uniform(uint64_t seed, uint64_t offset);

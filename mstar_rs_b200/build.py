@@ -15,7 +15,7 @@ import sys
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 SRC = [os.path.join(PKG, "csrc", "sampler.cu")]
-DEPS = SRC + [os.path.join(PKG, "csrc", "spec.cuh"), os.path.join(ROOT, "include", "mstar_sampler.h")]
+DEPS = SRC + [os.path.join(PKG, "csrc", "spec.cuh"), os.path.join(PKG, "csrc", "lmhead.cuh"), os.path.join(ROOT, "include", "mstar_sampler.h")]
 OUT = os.path.join(PKG, "_lib", "libmstar_sampler.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

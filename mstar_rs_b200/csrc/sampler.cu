@@ -34,6 +34,7 @@
 // python/mstar_rs/models/orpheus.py:350 and qwen3_omni.py:518 (batched,
 // in-graph), Sampler.sample in orpheus.py:517 / qwen3_omni.py:483 (eager).
 #include <cooperative_groups.h>
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -3465,6 +3466,8 @@ static int launch(const mstar_sampler_params_t *p, int mode, int tp_cap, uint32_
   return mode == 0 ? launch_T<float, 0>(p, pl, send, st) : launch_T<float, 1>(p, pl, send, st);
 }
 
+#include "lmhead.cuh"
+
 }  // namespace mstar
 
 using namespace mstar;
@@ -3511,6 +3514,29 @@ int mstar_sampler_tp_local(const mstar_sampler_params_t *p, int32_t tp_cap, uint
     return fail(MSTAR_ERR_UNSUPPORTED, "dense debug outputs are single-shard only");
   q.flags &= ~(MSTAR_FLAG_UPDATE_HISTORY | MSTAR_FLAG_UPDATE_SEEN | MSTAR_FLAG_ADVANCE_OFFSET);
   return launch(&q, 1, tp_cap, send, static_cast<cudaStream_t>(stream));
+}
+
+int64_t mstar_lmhead_workspace_bytes(int32_t B) {
+  if (B < 1 || B > lmh::MAX_N) return -1;
+  return lmh::workspace_bytes(B);
+}
+
+int mstar_lmhead_logits(const void *hidden, const void *weight, int32_t B, int32_t V, int32_t d, void *logits,
+                        int32_t dtype, int64_t ld, void *workspace, int64_t workspace_bytes, uint32_t *status,
+                        void *stream) {
+  return lmh::logits(hidden, weight, B, V, d, logits, dtype, ld, workspace, workspace_bytes, status,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int mstar_sampler_lmhead_step(const mstar_sampler_params_t *p, const void *hidden, const void *weight, int32_t d,
+                              void *workspace, int64_t workspace_bytes, uint32_t *status, void *stream) {
+  int rc = validate(p);
+  if (rc) return rc;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = lmh::logits(hidden, weight, p->B, p->V, d, const_cast<void *>(p->logits), p->dtype, p->ld, workspace,
+                   workspace_bytes, status, st);
+  if (rc) return rc;
+  return launch(p, 0, 0, nullptr, st);
 }
 
 int mstar_sampler_commit(const mstar_sampler_params_t *p, const int64_t *ids, void *stream) {

@@ -130,6 +130,20 @@ def sampler_step(logits: torch.Tensor, **kw) -> N.Params:
     return p
 
 
+def sampler_step_heads(logits: torch.Tensor, **kw) -> N.Params:
+    """One launch for H heads of n rows each (logits [H, n, V], e.g. the
+    codebook heads of a multi-codebook decoder sampled together): row h * n + i
+    of the flattened [H * n, V] batch is head h's row i, and slot_idx [H * n]
+    (or the row number) picks its parameters and per-slot state, so each
+    (head, request) pair keeps its own history, seen mask and RNG offset."""
+    if logits.dim() != 3:
+        raise ValueError("logits must be [H, n, V]")
+    H, n, V = logits.shape
+    if logits.stride(2) != 1 or logits.stride(0) != n * logits.stride(1):
+        raise ValueError("logits heads must be stacked rows of one [H * n, V] matrix")
+    return sampler_step(logits.reshape(H * n, V), **kw)
+
+
 def plan(logits: torch.Tensor, **kw):
     p = build_params(logits, **kw)
     cs, sm = N.I32(), N.I64()
@@ -196,3 +210,91 @@ def commit(ids: torch.Tensor, *, V: int, num_slots: int, slot_idx=None, hist_ids
         stream = torch.cuda.current_stream(dev).cuda_stream
         N.check(N.lib().mstar_sampler_commit(ctypes.byref(p), ctypes.c_void_p(ids.data_ptr()),
                                              ctypes.c_void_p(stream)), "mstar_sampler_commit")
+
+
+def _check_lmhead(hidden: torch.Tensor, weight: torch.Tensor):
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("hidden and weight must be bfloat16")
+    if not hidden.is_cuda or weight.device != hidden.device:
+        raise ValueError("hidden and weight must be CUDA tensors on one device")
+    if hidden.dim() != 2 or weight.dim() != 2 or hidden.shape[1] != weight.shape[1]:
+        raise ValueError("hidden must be [B, d] and weight [V, d]")
+    if not hidden.is_contiguous() or not weight.is_contiguous():
+        raise ValueError("hidden and weight must be contiguous")
+    return hidden.shape[0], weight.shape[0], hidden.shape[1]
+
+
+_WS: dict = {}
+
+
+def lmhead_workspace(B: int, device: torch.device) -> torch.Tensor:
+    """Scratch for projections of up to B rows on `device`
+    (mstar_lmhead_workspace_bytes), kept per device and reused: calls on one
+    stream share it; give each concurrent stream its own."""
+    dev = torch.device(device)
+    with torch.cuda.device(dev):
+        n = int(N.lib().mstar_lmhead_workspace_bytes(B))
+    if n <= 0:
+        raise ValueError(f"B={B} is outside [1, 256]")
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < n:
+        ws = torch.empty(n, dtype=torch.uint8, device=dev)
+        _WS[key] = ws
+    return ws
+
+
+def _check_ws(ws, dev):
+    if ws is None:
+        return None, 0
+    if ws.dtype != torch.uint8 or ws.device != dev or not ws.is_contiguous():
+        raise ValueError("workspace must be a contiguous uint8 tensor on the hidden device")
+    return _ptr(ws), ws.numel()
+
+
+def lmhead_logits(hidden: torch.Tensor, weight: torch.Tensor, *, out: torch.Tensor | None = None,
+                  dtype=torch.float32, status: torch.Tensor | None = None, workspace="auto") -> torch.Tensor:
+    """hidden [B, d] @ weight[V, d]^T on the tensor cores (mstar_lmhead_logits),
+    fp32 accumulation, stored as float32 or bfloat16.  workspace: "auto" (the
+    device's cached lmhead_workspace), a uint8 tensor, or None (whole-tile
+    shares, no scratch)."""
+    B, V, d = _check_lmhead(hidden, weight)
+    dev = hidden.device
+    if out is None:
+        out = torch.empty(B, V, dtype=dtype, device=dev)
+    if out.dtype not in _DT or out.device != dev or out.dim() != 2 or out.shape[0] != B or out.shape[1] < V \
+            or out.stride(1) != 1:
+        raise ValueError("out must be [B, >= V] float32 / bfloat16 with contiguous rows on the hidden device")
+    if status is not None and (status.dtype != torch.int32 or status.device != dev or status.numel() < 1):
+        raise ValueError("status must be an int32 tensor on the hidden device")
+    if isinstance(workspace, str):
+        workspace = lmhead_workspace(B, dev)
+    wp, wn = _check_ws(workspace, dev)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        N.check(N.lib().mstar_lmhead_logits(_ptr(hidden), _ptr(weight), B, V, d, _ptr(out), _DT[out.dtype],
+                                            out.stride(0), wp, wn, _ptr(status), ctypes.c_void_p(stream)),
+                "mstar_lmhead_logits")
+    return out
+
+
+def lmhead_step(hidden: torch.Tensor, weight: torch.Tensor, logits: torch.Tensor, *, status=None,
+                workspace="auto", **kw) -> N.Params:
+    """Project hidden [B, d] by weight [V, d] into `logits` [B, V] (float32 or
+    bfloat16, written) and sample from it (mstar_sampler_lmhead_step).  The
+    sampling keywords are sampler_step's; workspace as for lmhead_logits."""
+    B, V, d = _check_lmhead(hidden, weight)
+    if logits.shape[0] != B or logits.dim() != 2 or logits.shape[1] != V:
+        raise ValueError("logits must be [B, V] for hidden [B, d] and weight [V, d]")
+    if status is not None and (status.dtype != torch.int32 or status.device != hidden.device or status.numel() < 1):
+        raise ValueError("status must be an int32 tensor on the hidden device")
+    p = build_params(logits, **kw)
+    if isinstance(workspace, str):
+        workspace = lmhead_workspace(B, hidden.device)
+    wp, wn = _check_ws(workspace, hidden.device)
+    with torch.cuda.device(logits.device):
+        stream = torch.cuda.current_stream(logits.device).cuda_stream
+        N.check(N.lib().mstar_sampler_lmhead_step(ctypes.byref(p), _ptr(hidden), _ptr(weight), d, wp, wn,
+                                                  _ptr(status), ctypes.c_void_p(stream)),
+                "mstar_sampler_lmhead_step")
+    return p

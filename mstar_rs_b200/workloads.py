@@ -226,3 +226,28 @@ def to_device(b: Batch, device="cuda", with_uniforms: bool = True) -> dict:
         uniforms=t(b.uniforms, np.float32) if with_uniforms else None,
         seed=t(b.seed, np.int64), offset=t(b.offset, np.int64), vocab_offset=b.vocab_offset)
     return {"logits": logits, **kw}
+
+
+def lmhead_operands(B: int = 64, V: int = 151936, d: int = 2048, seed: int = 0, device="cuda",
+                    spike_frac: float = 0.005):
+    """Seeded bf16 LM-head operands whose projection hidden @ weight.T has the
+    mixed workload's logits: N(0, 3^2) per entry plus, for each row, a spike
+    of U(4, 10) on spike_frac of the ids.  Dimensions [0, B) of hidden are
+    one-hot row markers and weight's columns [0, B) carry the row spikes, so
+    the spikes ride the projection itself; the rest is Gaussian (built on the
+    device: the weight is V * d * 2 bytes)."""
+    import torch
+
+    if d < B + 64:
+        raise ValueError("d must leave room for one marker dimension per row")
+    g = torch.Generator(device=device).manual_seed(seed)
+    hidden = torch.randn(B, d, generator=g, device=device)
+    hidden[:, :B] = 0.0
+    hidden[torch.arange(B, device=device), torch.arange(B, device=device)] = 1.0
+    weight = torch.randn(V, d, generator=g, device=device).mul_(3.0 / (d - B) ** 0.5)
+    weight[:, :B] = 0.0
+    nspike = max(1, int(round(spike_frac * V)))
+    for r in range(B):
+        ids = torch.randperm(V, generator=g, device=device)[:nspike]
+        weight[ids, r] = torch.empty(nspike, device=device).uniform_(4.0, 10.0, generator=g)
+    return hidden.to(torch.bfloat16), weight.to(torch.bfloat16)

@@ -214,3 +214,25 @@ def test_small_vocab_ties(oracle_lib, K, dtype):
     o = oracle_lib.run(case, debug=True)
     g = run_gpu(case)
     assert_parity(g, o, case)
+
+
+def test_multi_head_step(oracle_lib):
+    """Four codebook heads of three requests in one launch ([H, n, V] with a
+    slot per (head, request), each slot with its own seen ids), against the
+    oracle on the flattened rows."""
+    import torch
+
+    from mstar_rs_b200 import kernel
+    from mstar_rs_b200.workloads import to_device
+
+    H, n, V = 4, 3, 2048
+    case = random_case(91, B=H * n, V=V, dtype="bf16", penalty="seen", specials=False, greedy_frac=0.0, scale=1.0)
+    case.top_k[:] = 0
+    case.top_p[:] = 1.0
+    case.min_p[:] = 0.0
+    o = oracle_lib.run(case)
+    d = to_device(case)
+    logits = d.pop("logits").reshape(H, n, V)
+    ids = torch.zeros(H * n, dtype=torch.int64, device="cuda")
+    kernel.sampler_step_heads(logits, **d, out_ids=ids)
+    assert np.array_equal(ids.cpu().numpy(), o["ids"])
