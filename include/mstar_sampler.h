@@ -195,6 +195,24 @@ int mstar_lmhead_logits(const void *hidden, const void *weight, int32_t B, int32
                         void *logits, int32_t dtype, int64_t ld, void *workspace,
                         int64_t workspace_bytes, uint32_t *status, void *stream);
 
+/* mstar_lmhead_logits for callers that cannot allocate device memory: no
+ * counterpart in the reference.  Engines that give all of HBM to their own
+ * pool at start-up (a raw cudaMalloc then fails or fragments it), code that
+ * runs during a global-mode stream capture (where cudaMalloc is not
+ * allowed) and native callers without a device allocator pass only inputs
+ * and outputs; the projection's scratch is a static device array of 8 MiB
+ * inside the library, held on every GPU that loads the library until the
+ * process exits.  The call allocates and frees nothing.  B is limited to
+ * what fits that array (96 rows on a 148-SM GPU); larger B is refused with
+ * MSTAR_ERR_INVALID.  The first call on a device looks the array's address
+ * up (which may load the library's device code there): make it before any
+ * stream capture.  All calls on a device share the array and leave their
+ * contents in it (each call clears what it needs cleared); calls that
+ * overlap on the GPU, from two streams or two threads, race on it. */
+int mstar_lmhead_logits_static(const void *hidden, const void *weight, int32_t B, int32_t V,
+                               int32_t d, void *logits, int32_t dtype, int64_t ld, uint32_t *status,
+                               void *stream);
+
 /* Projection and sampling in one call: mstar_lmhead_logits into p->logits
  * (which must be writable, [B, ld] of p->dtype, weight [p->V, d] being this
  * shard's rows), then mstar_sampler_step on it as a programmatic dependent

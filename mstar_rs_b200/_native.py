@@ -64,6 +64,7 @@ EXPORTS = (
     "mstar_sampler_step", "mstar_sampler_tp_record_words", "mstar_sampler_tp_local",
     "mstar_sampler_tp_merge", "mstar_sampler_philox_uniform", "mstar_sampler_commit",
     "mstar_lmhead_workspace_bytes", "mstar_lmhead_logits", "mstar_sampler_lmhead_step",
+    "mstar_lmhead_logits_static",
 )
 
 
@@ -100,6 +101,8 @@ def lib() -> ctypes.CDLL:
         L.mstar_lmhead_logits.restype = ctypes.c_int
         L.mstar_sampler_lmhead_step.argtypes = [ctypes.POINTER(Params), P, P, I32, P, I64, P, P]
         L.mstar_sampler_lmhead_step.restype = ctypes.c_int
+        L.mstar_lmhead_logits_static.argtypes = [P, P, I32, I32, I32, P, I32, I64, P, P]
+        L.mstar_lmhead_logits_static.restype = ctypes.c_int
         L.mstar_sampler_philox_uniform.argtypes = [ctypes.c_uint64, ctypes.c_uint64]
         L.mstar_sampler_philox_uniform.restype = ctypes.c_float
         if L.mstar_sampler_abi_version() != ABI_VERSION:

@@ -534,4 +534,51 @@ static int logits(const void *hidden, const void *weight, int B, int V, int d, v
   return MSTAR_OK;
 }
 
+// Projection scratch for callers that cannot allocate device memory: engines
+// that hand all of HBM to their own pool at start-up (a raw cudaMalloc then
+// fails or fragments the pool), code that runs while a stream is being
+// captured in global mode (where cudaMalloc is not allowed), and native
+// callers with no device allocator of their own.  The stream-K workspace of
+// mstar_lmhead_logits_static lives here instead: a file-scope device array of
+// STATIC_WS_BYTES (8 MiB), which every GPU that loads the library holds until
+// the process exits.  All calls on a device share it and it keeps the last
+// call's contents; each call clears the ready flags it relies on, and calls
+// that overlap on the GPU (two streams, two threads) race on it.
+constexpr int64_t STATIC_WS_BYTES = 8ll << 20;
+static __device__ __align__(256) uint8_t g_static_ws[STATIC_WS_BYTES];
+
+// Device address of g_static_ws on the current device, looked up once per
+// device with that device current (g_static_ws itself is only a host-side
+// stand-in for the symbol).  The lookup may load the module on the device,
+// so the first call on a device should come before any stream capture.
+static void *static_ws(int &rc) {
+  static void *addr[kMaxDevices] = {};
+  const int dev = current_device();
+  std::lock_guard<std::mutex> g(g_dev_mu);
+  if (!addr[dev]) {
+    void *a = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&a, g_static_ws);
+    if (e != cudaSuccess || !a) {
+      rc = fail(MSTAR_ERR_CUDA, std::string("cudaGetSymbolAddress(static workspace): ") + cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = a;
+  }
+  rc = MSTAR_OK;
+  return addr[dev];
+}
+
+static int logits_static(const void *hidden, const void *weight, int B, int V, int d, void *out, int dtype,
+                         int64_t ld, uint32_t *err, cudaStream_t st) {
+  if (B >= 1 && B <= MAX_N && workspace_bytes(B) > STATIC_WS_BYTES)
+    return fail(MSTAR_ERR_INVALID, "B = " + std::to_string(B) + " needs " + std::to_string(workspace_bytes(B)) +
+                                       " bytes of scratch; the static workspace holds " +
+                                       std::to_string(STATIC_WS_BYTES) + " (at most 96 rows on 148 SMs)");
+  int rc = check_operands(hidden, weight, B, V, d);
+  if (rc) return rc;
+  void *ws = static_ws(rc);
+  if (rc) return rc;
+  return logits(hidden, weight, B, V, d, out, dtype, ld, ws, STATIC_WS_BYTES, err, st);
+}
+
 }  // namespace lmh

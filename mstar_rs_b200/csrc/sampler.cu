@@ -3528,6 +3528,11 @@ int mstar_lmhead_logits(const void *hidden, const void *weight, int32_t B, int32
                      static_cast<cudaStream_t>(stream));
 }
 
+int mstar_lmhead_logits_static(const void *hidden, const void *weight, int32_t B, int32_t V, int32_t d,
+                               void *logits, int32_t dtype, int64_t ld, uint32_t *status, void *stream) {
+  return lmh::logits_static(hidden, weight, B, V, d, logits, dtype, ld, status, static_cast<cudaStream_t>(stream));
+}
+
 int mstar_sampler_lmhead_step(const mstar_sampler_params_t *p, const void *hidden, const void *weight, int32_t d,
                               void *workspace, int64_t workspace_bytes, uint32_t *status, void *stream) {
   int rc = validate(p);
