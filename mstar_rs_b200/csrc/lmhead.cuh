@@ -10,17 +10,19 @@
 // (V * d * 2 bytes, each byte read once), so the kernel is built around
 // keeping that stream at HBM rate on every SM until the end.  One persistent
 // CTA per SM takes an equal, contiguous share of the (vocabulary tile of BM
-// ids, k-block of 64) units (stream-K): 151936 ids make 1187 tiles, which
+// ids, k-block of BK) units (stream-K): 151936 ids make 1187 tiles, which
 // whole-tile shares would spread as 9 or 8 per SM.  A tile split between
 // CTAs is finished by the CTA holding its first k-blocks, which adds the
 // fp32 partial sums the later CTAs left in the workspace (one slot and one
 // ready flag per CTA; a CTA's only partial tile is its first segment, which
 // it finishes first, so the owner, which reaches the tile last, rarely
 // waits).  Without a workspace the shares are whole tiles.  Roles:
-//   warp 0    TMA producer: 2-D tensor copies of a weight tile [LM_BM x 64]
-//             and the hidden tile [N x 64] per k-block into a ring of stages
-//             (128-byte swizzled rows, the layout the MMA descriptors name);
-//   warp 1    MMA issuer: tcgen05.mma kind::f16 (M = LM_BM vocabulary ids,
+//   warp 0    TMA producer: 2-D tensor copies of the weight tile [BM x BK]
+//             and the hidden tile [N x BK] of each k-block, as 64-wide
+//             boxes, into a ring of stages (128-byte swizzled rows, the
+//             layout the MMA descriptors name); the first ring is issued
+//             before the CTA's set-up barrier;
+//   warp 1    MMA issuer: tcgen05.mma kind::f16 (M = BM vocabulary ids,
 //             N = batch rows padded to 16, K = 16 per instruction) into one
 //             of two TMEM accumulators, so the epilogue of tile t overlaps
 //             the MMAs of tile t + grid; owns the TMEM allocation;
@@ -32,12 +34,19 @@
 namespace lmh {
 
 constexpr int BM = 128;          // vocabulary ids per tile (MMA M, TMEM lanes)
-constexpr int BK = 64;           // hidden elements per k-block: one 128-byte swizzle row
+constexpr int BOX_K = 64;        // hidden elements per TMA box: one 128-byte swizzle row
+// A k-block (one pipeline stage) is two adjacent boxes: 256 contiguous bytes
+// of every weight row, one L2 256-byte promotion, so each DRAM access the
+// stream makes serves a whole stage instead of half of it (one box per
+// stage streamed at 5.5 TB/s, two at 6.1 TB/s; B=64, V=151936, d=2048).
+constexpr int KBOXES = 2;
+constexpr int BK = BOX_K * KBOXES;  // hidden elements per k-block
 constexpr int THREADS = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr int MAX_STAGES = 8;
+constexpr int MAX_STAGES = 12;
 constexpr int MAX_N = 256;       // batch rows per launch (MMA N limit)
-constexpr int A_BYTES = BM * BK * 2;  // 16 KB weight tile per stage
-constexpr int SMEM_BUDGET = 200 * 1024;
+constexpr int A_BYTES = BM * BK * 2;  // 32 KB of weight rows per stage
+constexpr int A_BOX = BM * BOX_K * 2;  // one weight box (16 KB)
+constexpr int SMEM_BUDGET = 220 * 1024;
 
 // Error word bits (the epilogue reports them per launch).
 constexpr uint32_t ERR_TIMEOUT = 1u;
@@ -220,32 +229,53 @@ __device__ __forceinline__ void raise(const Gemm &g, Sh &sh, uint32_t bits) {
 
 // Producer: one thread.  k-block `it` (counted across this CTA's share) uses
 // stage it % stages; its fill waits for the MMA commit that released the
-// stage's previous use.
+// stage's previous use.  Resumable: the first `stages` k-blocks are issued
+// before the CTA's set-up barrier (no stage has been used yet, so no wait),
+// the rest after it.
+struct Producer {
+  Work w;
+  int tile = 0, kb = 0, k1 = 0;
+  uint32_t it = 0, armed = 0, armed_par = 0;
+  __device__ explicit Producer(const Gemm &g) : w(g) {}
+  __device__ bool next(const Gemm &g) {  // the next k-block to load, if any
+    if (kb >= k1) {
+      if (!w.next(g)) return false;
+      tile = w.tile;
+      kb = w.k0;
+      k1 = w.k1;
+    }
+    return true;
+  }
+};
+
 __device__ void produce(const Gemm &g, Sh &sh, uint8_t *sA, uint8_t *sB, const CUtensorMap *tw,
-                        const CUtensorMap *th) {
+                        const CUtensorMap *th, Producer &P, uint32_t limit) {
   const uint32_t bbytes = (uint32_t)g.N * BK * 2;
   const uint64_t pw = policy_evict_first(), ph = policy_evict_last();
-  uint32_t it = 0, armed = 0, armed_par = 0;
-  Work w(g);
-  while (!aborted(sh) && w.next(g)) {
-    const int tile = w.tile;
-    for (int kb = w.k0; kb < w.k1; ++kb, ++it) {
-      const uint32_t s = it % (uint32_t)g.stages, use = it / (uint32_t)g.stages;
-      if (use > 0 && !mbar_wait(&sh.empty[s], (use - 1) & 1u)) {
-        raise(g, sh, ERR_TIMEOUT);
-        break;
-      }
-      mbar_expect_tx(&sh.full[s], (uint32_t)A_BYTES + bbytes);
-      tma_load_2d(sA + (size_t)s * A_BYTES, tw, kb * BK, tile * BM, &sh.full[s], pw);
-      tma_load_2d(sB + (size_t)s * bbytes, th, kb * BK, 0, &sh.full[s], ph);
-      armed |= 1u << s;
-      armed_par = (armed_par & ~(1u << s)) | ((use & 1u) << s);
+  while (P.it < limit && !aborted(sh) && P.next(g)) {
+    const uint32_t s = P.it % (uint32_t)g.stages, use = P.it / (uint32_t)g.stages;
+    if (use > 0 && !mbar_wait(&sh.empty[s], (use - 1) & 1u)) {
+      raise(g, sh, ERR_TIMEOUT);
+      break;
     }
+    mbar_expect_tx(&sh.full[s], (uint32_t)A_BYTES + bbytes);
+#pragma unroll
+    for (int j = 0; j < KBOXES; ++j) {
+      tma_load_2d(sA + (size_t)s * A_BYTES + j * A_BOX, tw, P.kb * BK + j * BOX_K, P.tile * BM, &sh.full[s], pw);
+      tma_load_2d(sB + (size_t)s * bbytes + j * (bbytes / KBOXES), th, P.kb * BK + j * BOX_K, 0, &sh.full[s], ph);
+    }
+    P.armed |= 1u << s;
+    P.armed_par = (P.armed_par & ~(1u << s)) | ((use & 1u) << s);
+    ++P.kb;
+    ++P.it;
   }
-  // every copy issued lands before the CTA may exit (normally long done)
+}
+
+// Every copy issued lands before the CTA may exit (normally long done).
+__device__ void produce_drain(const Gemm &g, Sh &sh, const Producer &P) {
   for (int s = 0; s < g.stages; ++s)
-    if ((armed >> s) & 1u)
-      if (!mbar_wait(&sh.full[s], (armed_par >> s) & 1u)) raise(g, sh, ERR_TIMEOUT);
+    if ((P.armed >> s) & 1u)
+      if (!mbar_wait(&sh.full[s], (P.armed_par >> s) & 1u)) raise(g, sh, ERR_TIMEOUT);
 }
 
 // MMA issuer: one thread.  Segment number sl of this CTA accumulates into
@@ -275,8 +305,11 @@ __device__ void mma_issue(const Gemm &g, Sh &sh, uint8_t *sA, uint8_t *sB, uint3
       tc_fence_after();
       const uint32_t as = a0 + s * (uint32_t)A_BYTES, bs = b0 + s * bbytes;
 #pragma unroll
-      for (int k = 0; k < BK / 16; ++k)  // K = 16 bf16 = 32 bytes per instruction
-        mma_bf16(dcol, sw128_desc(as + 32u * k), sw128_desc(bs + 32u * k), idesc, (kb != w.k0 || k) ? 1u : 0u);
+      for (int j = 0; j < KBOXES; ++j)
+#pragma unroll
+        for (int k = 0; k < BOX_K / 16; ++k)  // K = 16 bf16 = 32 bytes per instruction
+          mma_bf16(dcol, sw128_desc(as + j * A_BOX + 32u * k), sw128_desc(bs + j * (bbytes / KBOXES) + 32u * k),
+                   idesc, (kb != w.k0 || j || k) ? 1u : 0u);
       mma_commit(&sh.empty[s]);
     }
     if (!ok) break;
@@ -304,7 +337,10 @@ __global__ void __launch_bounds__(lmh::THREADS, 1)
   // a dependent launch (the sampler step) may be scheduled as CTAs finish;
   // its griddepcontrol.wait still waits for this whole grid and its writes
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  Producer P(g);
   if (threadIdx.x == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tw)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&th)) : "memory");
     for (int s = 0; s < g.stages; ++s) {
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
@@ -316,6 +352,7 @@ __global__ void __launch_bounds__(lmh::THREADS, 1)
     mbar_init(&sh.mma_done, 1);
     sh.abort = 0;
     fence_barrier_init();
+    produce(g, sh, sA, sB, &tw, &th, P, (uint32_t)g.stages);  // the first ring, while TMEM is allocated
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sh.tmem_base)),
@@ -328,7 +365,10 @@ __global__ void __launch_bounds__(lmh::THREADS, 1)
   tc_fence_after();
   const uint32_t tbase = sh.tmem_base;
   if (warp == 0) {
-    if (lane == 0) produce(g, sh, sA, sB, &tw, &th);
+    if (lane == 0) {
+      produce(g, sh, sA, sB, &tw, &th, P, 0xFFFFFFFFu);
+      produce_drain(g, sh, P);
+    }
   } else if (warp == 1) {
     if (lane == 0) mma_issue(g, sh, sA, sB, tbase);
   } else {
@@ -449,14 +489,14 @@ static EncodeTiled encode_fn() {
 }
 
 // Tensor map of a K-major bf16 matrix [rows, d] (row stride d) read as
-// boxes of BK x box_rows with the 128-byte swizzle; rows past the end read
-// as zeros.
+// boxes of BOX_K x box_rows with the 128-byte swizzle; rows and columns past
+// the end read as zeros.
 static int make_map(CUtensorMap *m, const void *ptr, int64_t rows, int d, int box_rows) {
   const EncodeTiled enc = encode_fn();
   if (!enc) return fail(MSTAR_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)d * 2u};
-  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  const cuuint32_t box[2] = {(cuuint32_t)BOX_K, (cuuint32_t)box_rows};
   const cuuint32_t es[2] = {1u, 1u};
   const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, es,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

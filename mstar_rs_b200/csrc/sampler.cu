@@ -1,34 +1,45 @@
 // B200 batched token sampler: logits [B, V] -> token ids [B].
 //
-// One thread-block cluster of S CTAs samples one row.  Each CTA owns a
-// contiguous slice of the row, pulls it into shared memory with 1-D bulk
-// copies (cp.async.bulk + mbarrier, one barrier per 32 KB chunk, all issued
-// by one thread before anything else) and keeps it resident for the whole
-// step, so HBM is read exactly once:
+// One thread-block cluster of S CTAs (512 threads each) samples one row;
+// each CTA owns a contiguous slice of it and reads every byte of the slice
+// exactly once from HBM:
 //
-//   setup     while the copies fly: the slice's penalised / biased ids go
-//             into a small hash table and a bitmap, disallowed ids into a
-//             second bitmap.
-//   pass A    per chunk as it lands: disallowed ids -> -inf, penalised /
-//             biased ids ("specials") -> NaN after their raw value is saved
-//             in the hash table, running max of the raw values.  The
-//             specials' final values are then computed from the table.
-//   cluster   row max m = max over the CTAs (DSMEM).  A conservative value
-//             threshold theta <= x_A (x_A = smallest value with positive
-//             weight passing min_p) is picked from m and checked with the
-//             spec's exponential.
-//   pass C    vectors whose transformed max is below theta are skipped after
-//             one compare; the few survivors pass the exact predicate and go
-//             into a CTA-local candidate list.
-//   tail      the leader pulls every list over DSMEM, counts candidates and
-//             weight mass into 2048 buckets of the order key, scans the
-//             buckets, ranks each candidate inside its bucket, and resolves
-//             top_k / top_p / the inverse-CDF draw from exact u64 prefix sums
-//             of the fixed-point weights.
-//   general   rows whose candidate set exceeds the tail capacity run a
-//             leader-driven loop of histogram (count + mass) and compaction
-//             rounds over the still-resident slices until every boundary is
-//             pinned to a bin small enough to sort.
+//   loads     the small per-row inputs are issued first (history length and
+//             words, parameter words, the slice's unaligned fringe, bias
+//             entries), then the slice: up to 152 KB as streaming 128-bit
+//             loads into a register tile (19 vectors per thread), larger
+//             slices as 1-D bulk copies into shared memory (32 KB per
+//             mbarrier; every wait is bounded in time).
+//   setup     while the loads fly: a skip bitmap of the slice's special ids
+//             (history / bias ids, allowed-mask holes), a seen map for
+//             seen-bit penalties, the row's parameters and Philox uniform,
+//             then a hash table of the specials with occurrence counts.
+//   pass A    raw maximum per vector, specials masked out by a taint mask;
+//             the register tile is stored to shared memory and each vector's
+//             raw maximum kept in registers.  The specials' final values
+//             (bias, penalties, mask, temperature) come from the table and,
+//             for seen ids, straight from the resident data.
+//   threshold theta(cm) from the CTA's own maximum: below it no value can
+//             carry weight or pass min_p for any row maximum m >= cm, so no
+//             cluster exchange is needed before candidates are chosen.
+//   push      vectors whose raw maximum reaches theta are rescanned; their
+//             candidates go straight into the leader CTA's shared memory
+//             (one reservation per warp), cut at the CTA's local top_k value
+//             when a top_k row has more than it may push; the CTA's maximum,
+//             count, status and lowest id at its maximum go to every peer.
+//             One cluster barrier per step.
+//   tail      (leader) rank sort, value-bucket sort or key-bucket sort of the
+//             candidates, then top_k / top_p / the inverse-CDF draw from
+//             exact u64 prefix sums of the fixed-point weights.  Rows with
+//             more than 2048 candidates run the general path instead:
+//             histogram (count + mass) and compaction rounds over the
+//             still-resident slices until every boundary is pinned.
+//   epilogue  id, status, stop flag, in-graph state updates (history ring,
+//             seen bit, RNG offset).  MODE 1 (a vocabulary shard) emits the
+//             shard's candidate record instead, merged by tp_merge_kernel.
+//
+// Rows of at most 4096 ids take small_kernel (one CTA, no cluster).  The
+// LM-head projection that produces the logits is in lmhead.cuh.
 //
 // Reference call sites this kernel serves: CudaGraphableSampler.sample in
 // python/mstar_rs/models/orpheus.py:350 and qwen3_omni.py:518 (batched,
