@@ -61,6 +61,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-per-config", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--only", choices=["lmhead"], default=None,
+                    help="print only the LM-head report (projection + sampling against cuBLAS + sampler)")
+    ap.add_argument("--lmhead-profile", type=int, default=0, metavar="N",
+                    help="run N plain projection + sampling calls (no graphs, no timing) for a profiler")
     return ap.parse_args()
 
 
@@ -886,8 +890,37 @@ def run_tp_line(args, world, rank, local):
     }), flush=True)
 
 
+def lmhead_profile(n, B=64, V=151936, d=2048):
+    """n plain projection + sampling calls of the LM-head report's workload,
+    one launch pair each, for ncu launch lists and captures."""
+    import torch
+
+    from mstar_rs_b200 import kernel
+    from mstar_rs_b200 import workloads as W
+
+    dev = torch.device("cuda", 0)
+    case = W.qwen_mixed(seed=5, B=B, V=V)
+    kw = W.to_device(case, device=dev)
+    kw.pop("logits")
+    hidden, weight = W.lmhead_operands(B, V, d, seed=7, device=dev)
+    logits = torch.empty(B, V, dtype=torch.bfloat16, device=dev)
+    ids = torch.zeros(B, dtype=torch.int64, device=dev)
+    for _ in range(n):
+        kernel.lmhead_step(hidden, weight, logits, **kw, out_ids=ids)
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"lmhead_profile_calls": n, "ids": ids[:8].tolist()}))
+
+
 def main():
     args = parse()
+    if args.lmhead_profile:
+        lmhead_profile(args.lmhead_profile)
+        return
+    if args.only == "lmhead":
+        import torch
+
+        print(json.dumps(run_lmhead(torch.device("cuda", 0))), flush=True)
+        return
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":
