@@ -163,6 +163,33 @@ int mstar_sampler_tp_local(const mstar_sampler_params_t *p, int32_t tp_cap, uint
 int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world,
                            int64_t V_global, const uint32_t *recv, void *stream);
 
+/* Two-round tensor-parallel sampling, for rows without top_k (or with one
+ * above tp_cap): the reference's Thinker samples with top_k 0 whenever a
+ * temperature is given (python/mstar_rs/models/qwen3_omni.py:440-443).
+ *   1. tp_local2: as tp_local, but such a row sends the first tp_cap members
+ *      of its shard A set (record word 3, bit 0: possibly partial) and
+ *      leaves the shard's final values in xbuf [B, V] (f32).
+ *   2. all-gather the records; tp_merge1 on every rank: rows with no partial
+ *      shard are decided as by tp_merge; the others are deferred, and pend
+ *      [B, 2] (uint32: flag, bits of the row max M) records them.
+ *   3. tp_mass: the shard's exact A mass against M for every deferred row
+ *      into send2 [B, 2] (uint32 pairs, a little-endian u64 each; 0 for the
+ *      rest).
+ *   4. all-gather send2 into recv2 [tp_world, B, 2]; tp_merge2 on every rank
+ *      decides the deferred rows exactly when their kept set (top_p) or draw
+ *      point (no top_p) lies among the members every shard sent, and flags
+ *      the rest MSTAR_STATUS_TP_OVERFLOW (id: the row's leading member).
+ * Every rank gets the same ids and state updates.  tp_world <= 16. */
+int mstar_sampler_tp_local2(const mstar_sampler_params_t *p, int32_t tp_cap, uint32_t *send,
+                            float *xbuf, void *stream);
+int mstar_sampler_tp_merge1(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world,
+                            int64_t V_global, const uint32_t *recv, uint32_t *pend, void *stream);
+int mstar_sampler_tp_mass(const mstar_sampler_params_t *p, const float *xbuf, const uint32_t *pend,
+                          uint32_t *send2, void *stream);
+int mstar_sampler_tp_merge2(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world,
+                            int64_t V_global, const uint32_t *recv, const uint32_t *recv2,
+                            const uint32_t *pend, void *stream);
+
 /* State updates for ids chosen elsewhere: for every row r of [0, p->B)
  * whose slot (slot_idx[r], or r) is >= 0 and whose id ids[r] lies in
  * [vocab_offset, vocab_offset + V): append the id to the slot's history ring

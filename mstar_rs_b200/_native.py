@@ -64,7 +64,8 @@ EXPORTS = (
     "mstar_sampler_step", "mstar_sampler_tp_record_words", "mstar_sampler_tp_local",
     "mstar_sampler_tp_merge", "mstar_sampler_philox_uniform", "mstar_sampler_commit",
     "mstar_lmhead_workspace_bytes", "mstar_lmhead_logits", "mstar_sampler_lmhead_step",
-    "mstar_lmhead_logits_static",
+    "mstar_lmhead_logits_static", "mstar_sampler_tp_local2", "mstar_sampler_tp_merge1", "mstar_sampler_tp_mass",
+    "mstar_sampler_tp_merge2",
 )
 
 
@@ -95,6 +96,14 @@ def lib() -> ctypes.CDLL:
         L.mstar_sampler_tp_merge.restype = ctypes.c_int
         L.mstar_sampler_commit.argtypes = [ctypes.POINTER(Params), P, P]
         L.mstar_sampler_commit.restype = ctypes.c_int
+        L.mstar_sampler_tp_local2.argtypes = [ctypes.POINTER(Params), I32, P, P, P]
+        L.mstar_sampler_tp_local2.restype = ctypes.c_int
+        L.mstar_sampler_tp_merge1.argtypes = [ctypes.POINTER(Params), I32, I32, I64, P, P, P]
+        L.mstar_sampler_tp_merge1.restype = ctypes.c_int
+        L.mstar_sampler_tp_mass.argtypes = [ctypes.POINTER(Params), P, P, P, P]
+        L.mstar_sampler_tp_mass.restype = ctypes.c_int
+        L.mstar_sampler_tp_merge2.argtypes = [ctypes.POINTER(Params), I32, I32, I64, P, P, P, P]
+        L.mstar_sampler_tp_merge2.restype = ctypes.c_int
         L.mstar_lmhead_workspace_bytes.argtypes = [I32]
         L.mstar_lmhead_workspace_bytes.restype = I64
         L.mstar_lmhead_logits.argtypes = [P, P, I32, I32, I32, P, I32, I64, P, I64, P, P]

@@ -117,6 +117,7 @@ struct Plan {
   int32_t smem_bytes;
   int32_t mode;        // 0 = step, 1 = TP local
   int32_t tp_cap, rec_words;
+  float *xdump;        // TP local, two rounds: shard values [B, V] of rows without a usable top_k
 };
 
 enum : int { OP_DONE = 0, OP_HIST = 1, OP_COMPACT = 2 };
@@ -202,6 +203,8 @@ struct CtaSh {
   int kcut_bin;         // candidates: value bin of this CTA's K-th largest (top_k cut)
   Row row;
   int tp_ovf;
+  int pseudo;           // TP two rounds: the row's top_k is the record capacity
+  int dumpx;            // TP two rounds: the shard values go to the value buffer
   int bcast_i;
   uint64_t bcast_u64;
   uint32_t pw[NPARAM];  // the row's parameter words, staged for row_init
@@ -1454,12 +1457,10 @@ __device__ bool tail_bucket_sort(const Row &r, uint32_t km, int n, const TailScr
 }
 
 // Sort the n gathered candidates (tail_put, every thread's kmn / kmx / np)
-// and resolve them (MODE 0: res.token / WK / ckK) or emit the shard record
-// (MODE 1).  Block-wide; a small set is resolved by warp 0 alone, so callers
-// read sh.res after a barrier.
-template <int MODE>
-__device__ void tail_finish(const Row &r, float u, uint32_t km, int n, uint64_t kmn, uint64_t kmx, uint32_t np,
-                            int tp_cap, uint32_t *rec, const TailScr &ts, CtaSh &sh) {
+// into RK / RW / RS rank order; sh.npass counts those passing the value-A
+// predicate.  Block-wide; ends with a barrier.
+__device__ void tail_sort_gathered(const Row &r, uint32_t km, int n, uint64_t kmn, uint64_t kmx, uint32_t np,
+                                   const TailScr &ts, CtaSh &sh) {
   np = __reduce_add_sync(~0u, np);
   if ((threadIdx.x & 31) == 0 && np) atomicAdd(&sh.npass, np);
   __syncthreads();  // keys, weights and the pass count complete
@@ -1470,6 +1471,15 @@ __device__ void tail_finish(const Row &r, float u, uint32_t km, int n, uint64_t 
     tail_gather_end(kmn, kmx, 0u, ts, sh);
     tail_sort(n, ts, sh);
   }
+}
+
+// Sort the n gathered candidates and resolve them (MODE 0: res.token / WK /
+// ckK) or emit the shard record (MODE 1).  Block-wide; a small set is
+// resolved by warp 0 alone, so callers read sh.res after a barrier.
+template <int MODE>
+__device__ void tail_finish(const Row &r, float u, uint32_t km, int n, uint64_t kmn, uint64_t kmx, uint32_t np,
+                            int tp_cap, uint32_t *rec, const TailScr &ts, CtaSh &sh) {
+  tail_sort_gathered(r, km, n, kmn, kmx, np, ts, sh);
   if (MODE == 0) {
     if (n <= NT) {
       if (threadIdx.x < 32) tail_resolve_warp(r, u, ts, sh);
@@ -1973,8 +1983,34 @@ __device__ __forceinline__ void general_path(const RowCtx &c, CtaSh &sh) {
   }
 }
 
-// Dense debug outputs (processed logits, kept mask, probabilities),
-// recomputed from global memory.  Every CTA of the cluster, after a cluster
+// Every position of the slice once through emit(e, x): the final value of
+// each id (the resident logits transformed, then the specials' and seen ids'
+// final values over them).  Block-wide (one barrier between the two).
+template <typename T, typename Emit>
+__device__ __forceinline__ void dense_values(const RowCtx &c, Emit &&emit) {
+  const mstar_sampler_params_t &p = *c.p;
+  const Row &r = c.r;
+  const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)c.slot * p.allowed_words : nullptr;
+  for (int64_t e = c.c0 + threadIdx.x; e < c.c1; e += NT) {
+    const float v = Elem<T>::load(c.rowp, e);
+    const int64_t g = e + c.gbase;
+    const bool allowed = !aw || ((aw[g >> 5] >> (g & 31)) & 1u);
+    float x;
+    if (v != v) x = v;
+    else if (!allowed) x = -INFINITY;
+    else x = xform(r, v);
+    emit(e, x);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < c.nspec; i += NT) emit((int64_t)c.L.spec[i].gid - c.gbase, c.L.spec[i].x);
+  // seen-mask ids from global memory (the leader's resident slice may hold
+  // the tail's scratch by now)
+  for_each_seen<T>(c.sl, r, true, threadIdx.x, NT, [&](const Cand &cd, bool valid) {
+    if (valid) emit((int64_t)cd.gid - c.gbase, cd.x);
+  });
+}
+
+// Dense debug outputs (x, kept, probs) of this CTA's slice, after the
 // barrier that published the leader's result.
 template <typename T>
 __device__ __forceinline__ void debug_dense(const RowCtx &c, CtaSh &sh) {
@@ -1983,8 +2019,7 @@ __device__ __forceinline__ void debug_dense(const RowCtx &c, CtaSh &sh) {
   const Row &r = c.r;
   const Result res = cluster.map_shared_rank(&sh, 0)->res;
   const uint32_t kmm = okey(res.m);
-  const uint32_t *aw = p.allowed_bits ? p.allowed_bits + (int64_t)c.slot * p.allowed_words : nullptr;
-  auto emit = [&](int64_t e, float x) {
+  dense_values<T>(c, [&](int64_t e, float x) {
     const int64_t o = (int64_t)c.row * p.V + e;
     const uint32_t gid = (uint32_t)(e + c.gbase);
     bool kept = false;
@@ -2004,23 +2039,6 @@ __device__ __forceinline__ void debug_dense(const RowCtx &c, CtaSh &sh) {
     if (p.out_x) p.out_x[o] = x;
     if (p.out_kept) p.out_kept[o] = kept ? 1 : 0;
     if (p.out_probs) p.out_probs[o] = prob;
-  };
-  for (int64_t e = c.c0 + threadIdx.x; e < c.c1; e += NT) {
-    const float v = Elem<T>::load(c.rowp, e);
-    const int64_t g = e + c.gbase;
-    const bool allowed = !aw || ((aw[g >> 5] >> (g & 31)) & 1u);
-    float x;
-    if (v != v) x = v;
-    else if (!allowed) x = -INFINITY;
-    else x = xform(r, v);
-    emit(e, x);
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < c.nspec; i += NT) emit((int64_t)c.L.spec[i].gid - c.gbase, c.L.spec[i].x);
-  // seen-mask ids from global memory (the leader's resident slice may hold
-  // the tail's scratch by now)
-  for_each_seen<T>(c.sl, r, true, threadIdx.x, NT, [&](const Cand &cd, bool valid) {
-    if (valid) emit((int64_t)cd.gid - c.gbase, cd.x);
   });
 }
 
@@ -2182,6 +2200,8 @@ __global__ void __launch_bounds__(NT, 1)
     sh.n_spec = 0;
     sh.ht_fail = 0;
     sh.tp_ovf = 0;
+    sh.pseudo = 0;
+    sh.dumpx = 0;
     sh.nemit = 0;
     sh.cmax = okey(-INFINITY);
     sh.best = 0xFFFFFFFFu;
@@ -2226,6 +2246,18 @@ __global__ void __launch_bounds__(NT, 1)
   __syncthreads();  // skip words written, table cleared, small values staged
   if (tid == 64) {
     row_init(sh.row, sh.pw, p, row, p.V);
+    // two-round TP: a row without top_k (or with one above the record's
+    // capacity) leaves its shard values for the second round and, when the
+    // shard has more ids than a record holds, sends the first tp_cap members
+    // of its shard A set, marked as possibly partial
+    if (MODE == 1 && pl.xdump && !sh.row.greedy && (!sh.row.topk || sh.row.K > pl.tp_cap)) {
+      sh.dumpx = 1;
+      if ((int64_t)pl.tp_cap < p.V) {
+        sh.row.topk = true;
+        sh.row.K = pl.tp_cap;
+        sh.pseudo = 1;
+      }
+    }
   } else if (MODE == 0 && tid == 32) {
     sh.u = p.uniforms ? __uint_as_float((uint32_t)sh.rng[0]) : philox_uniform(sh.rng[0], sh.rng[1]);
   }
@@ -2409,6 +2441,22 @@ __global__ void __launch_bounds__(NT, 1)
     __syncthreads();
   }
   const int nspec = min((int)sh.n_spec, pl.spec_cap);
+  if (MODE == 1 && pl.xdump && sh.dumpx) {  // uniform: the shard values for the second round
+    RowCtx dc;
+    dc.p = &p;
+    dc.L = L;
+    dc.sl = sl;
+    dc.r = r;
+    dc.rowp = rowp;
+    dc.nspec = nspec;
+    dc.row = row;
+    dc.slot = slot;
+    dc.c0 = c0;
+    dc.c1 = c1;
+    dc.gbase = gbase;
+    float *xo = pl.xdump + (int64_t)row * p.V;
+    dense_values<T>(dc, [&](int64_t e, float x) { xo[e] = x; });
+  }
   const float theta_l = sh.theta;
   const int capq = TAIL_CAP / S;  // candidates each CTA may push to the leader
   cluster_wait();                 // every CTA of the cluster runs: remote stores are safe
@@ -2717,7 +2765,7 @@ __global__ void __launch_bounds__(NT, 1)
           rec[1] = ovf ? 0u : (uint32_t)nemit;
         }
         rec[2] = st;
-        rec[3] = 0;
+        rec[3] = sh.pseudo ? 1u : 0u;  // bit 0: the record holds at most the first tp_cap members
       }
     }
   }
@@ -3111,7 +3159,7 @@ __global__ void __launch_bounds__(128) commit_kernel(const mstar_sampler_params_
 // One CTA per row: merge tp_world candidate records and sample.
 __global__ void __launch_bounds__(NT, 1)
     tp_merge_kernel(const mstar_sampler_params_t p, int tp_cap, int tp_world, int rec_words, int64_t V_global,
-                    const uint32_t *recv) {
+                    const uint32_t *recv, uint32_t *pend) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ CtaSh sh;
   const int row = blockIdx.x, tid = threadIdx.x;
@@ -3121,6 +3169,7 @@ __global__ void __launch_bounds__(NT, 1)
       if (p.out_ids) p.out_ids[row] = 0;
       if (p.out_ids32) p.out_ids32[row] = 0;
       if (p.out_status) p.out_status[row] = 0;
+      if (pend) pend[2 * row] = 0u;
     }
     return;
   }
@@ -3129,12 +3178,25 @@ __global__ void __launch_bounds__(NT, 1)
   const TailScr ts = tail_scratch(smem);
   float m = -INFINITY;
   uint32_t status = 0;
+  bool partial = false;  // some shard sent only the first tp_cap members of its A set
   for (int q = 0; q < tp_world; ++q) {
     const uint32_t *rec = recv + ((int64_t)q * p.B + row) * rec_words;
     m = fmaxf(m, __uint_as_float(rec[0]));
     status |= rec[2];
+    partial |= (rec[3] & 1u) && rec[1] >= (uint32_t)tp_cap;
   }
   status &= ~(uint32_t)MSTAR_STATUS_EMPTY;
+  if (partial && !(r.greedy || r.K == 1) && m > -INFINITY) {
+    if (pend) {  // decided by the second round: no output and no state update here
+      if (tid == 0) {
+        pend[2 * row] = 1u;
+        pend[2 * row + 1] = __float_as_uint(m);
+      }
+      return;
+    }
+    status |= MSTAR_STATUS_TP_OVERFLOW;
+  }
+  if (pend && tid == 0) pend[2 * row] = 0u;
   if (tid == 0) {
     sh.nloc = 0;
     sh.best = 0xFFFFFFFFu;
@@ -3193,6 +3255,177 @@ __global__ void __launch_bounds__(NT, 1)
       status |= MSTAR_STATUS_EMPTY;
       token = 0;
     }
+    write_row_outputs(p, row, slot, token, status);
+  }
+}
+
+// ------------------------------------------------------------ TP, second round
+//
+// Rows whose shards sent only the first tp_cap members of their A sets
+// (top_k off, or above the record capacity) are decided with one more
+// exchange.  tp_mass_kernel: each shard's exact A mass against the row max M
+// the first merge found (one CTA per deferred row, over the shard values
+// its record kernel left in xbuf).  tp_merge2_kernel: with W_A = the sum of
+// those masses, the rank-ordered union of the records is exact up to k*,
+// the smallest last-sent key among the partial shards (every key up to it
+// was sent); the row is decided when its kept set ends there (top_p) or its
+// draw point falls there (top_p off), and flagged MSTAR_STATUS_TP_OVERFLOW
+// otherwise.  Rows with top_k above the capacity are decided when their
+// first K members are all known.
+
+__global__ void __launch_bounds__(NT)
+    tp_mass_kernel(const mstar_sampler_params_t p, const float *xbuf, const uint32_t *pend, uint32_t *send2) {
+  __shared__ uint64_t part[NWARP];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  if (!pend[2 * row]) {
+    if (tid == 0) {
+      send2[2 * row] = 0u;
+      send2[2 * row + 1] = 0u;
+    }
+    return;
+  }
+  const int slot = p.slot_idx ? p.slot_idx[row] : row;
+  Row r;
+  row_init(r, p, row, slot, p.V);
+  const float M = __uint_as_float(pend[2 * row + 1]);
+  const float *x = xbuf + (int64_t)row * p.V;
+  uint64_t acc = 0;
+  for (int64_t e = tid; e < p.V; e += NT) {
+    const float v = x[e];
+    if (v == v && v > -INFINITY) acc += weight_A(r, v, M);
+  }
+  for (int o = 16; o; o >>= 1) acc += (uint64_t)__shfl_xor_sync(~0u, (unsigned long long)acc, o);
+  if ((tid & 31) == 0) part[tid >> 5] = acc;
+  __syncthreads();
+  if (tid == 0) {
+    uint64_t t = 0;
+    for (int w = 0; w < NWARP; ++w) t += part[w];
+    send2[2 * row] = (uint32_t)t;
+    send2[2 * row + 1] = (uint32_t)(t >> 32);
+  }
+}
+
+__global__ void __launch_bounds__(NT, 1)
+    tp_merge2_kernel(const mstar_sampler_params_t p, int tp_cap, int tp_world, int rec_words, int64_t V_global,
+                     const uint32_t *recv, const uint32_t *recv2, const uint32_t *pend) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ CtaSh sh;
+  __shared__ unsigned long long kstar;  // smallest last-sent key among the partial shards
+  __shared__ unsigned long long kq[16];
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  if (!pend[2 * row]) return;  // decided by the first merge (or a padding row)
+  const int slot = p.slot_idx ? p.slot_idx[row] : row;
+  Row r;
+  row_init(r, p, row, slot, V_global);
+  const TailScr ts = tail_scratch(smem);
+  const float m = __uint_as_float(pend[2 * row + 1]);
+  const uint32_t km = okey(m);
+  uint32_t status = 0;
+  for (int q = 0; q < tp_world; ++q) status |= recv[((int64_t)q * p.B + row) * rec_words + 2];
+  status &= ~(uint32_t)MSTAR_STATUS_EMPTY;
+  if (tid == 0) {
+    sh.nloc = 0;
+    sh.status = 0;
+    sh.theta = 0.0f;
+    sh.res.token = 0;
+    sh.u = p.uniforms ? p.uniforms[row]
+                      : philox_uniform(p.seed ? p.seed[slot] : 0ull, p.offset ? p.offset[slot] : 0ull);
+    kstar = ~0ull;
+    tail_reset(sh);
+  }
+  if (tid < 16) kq[tid] = 0ull;
+  if (tid < 32) {
+    const float t = choose_theta(r, m);
+    if (tid == 0) sh.theta = t;
+  }
+  __syncthreads();
+  const float theta = sh.theta;
+  uint64_t kmn = ~0ull, kmx = 0ull;
+  uint32_t np = 0;
+  for (int q = 0; q < tp_world; ++q) {
+    const uint32_t *rec = recv + ((int64_t)q * p.B + row) * rec_words;
+    const bool part = (rec[3] & 1u) && rec[1] >= (uint32_t)tp_cap;
+    const int n = (int)min(rec[1], (uint32_t)tp_cap);
+    unsigned long long lastk = 0ull;
+    for (int j = tid; j < n; j += NT) {
+      const float x = __uint_as_float(rec[4 + 2 * j]);
+      const uint32_t gid = rec[5 + 2 * j];
+      if ((int64_t)gid >= V_global) {
+        atomicOr(&sh.status, MSTAR_STATUS_BAD_RECORD);
+        continue;
+      }
+      if (part) lastk = u64max(lastk, ckey(km, x, gid));
+      if (x >= theta) {
+        const uint32_t idx = atomicAdd(&sh.nloc, 1u);
+        if (idx < (uint32_t)TAIL_CAP) tail_put(r, m, km, Cand{x, gid}, (int)idx, ts, kmn, kmx, np);
+      }
+    }
+    if (part) {
+      for (int o = 16; o; o >>= 1) lastk = u64max(lastk, (uint64_t)__shfl_xor_sync(~0u, lastk, o));
+      if (lane == 0 && q < 16) atomicMax(&kq[q], lastk);
+    }
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int q = 0; q < tp_world && q < 16; ++q) {
+      const uint32_t *rec = recv + ((int64_t)q * p.B + row) * rec_words;
+      if ((rec[3] & 1u) && rec[1] >= (uint32_t)tp_cap) kstar = u64min(kstar, kq[q]);
+    }
+  const int n = (int)min(sh.nloc, (uint32_t)TAIL_CAP);
+  tail_sort_gathered(r, km, n, kmn, kmx, np, ts, sh);
+  if (tid == 0) {
+    const int npass = (int)sh.npass;
+    // known members of A: a prefix of the rank order (keys up to k*)
+    int nk = 0;
+    while (nk < npass && ts.RK[nk] <= kstar) ++nk;
+    const uint64_t G = nk ? ts.RS[nk - 1] + ts.RW[nk - 1] : 0ull;
+    auto S = [&](int j) -> uint64_t { return j < nk ? ts.RS[j] : G; };  // exclusive prefix, j <= nk
+    bool ok = nk > 0;
+    int nA = nk;
+    uint64_t WA = 0;
+    if (ok && r.topk) {  // the first K members must all be known
+      ok = r.K <= nk;
+      nA = r.K;
+      if (ok) WA = S(nA);
+    } else if (ok) {
+      for (int q = 0; q < tp_world; ++q)
+        WA += (uint64_t)recv2[2 * ((int64_t)q * p.B + row)] |
+              ((uint64_t)recv2[2 * ((int64_t)q * p.B + row) + 1] << 32);
+      nA = -1;  // all of A (its end may lie past k*)
+    }
+    int nK = 0;
+    uint64_t WK = 0;
+    if (ok && r.topp) {  // kept: j == 0 or S_j < P * W_A; the first j >= 1 with S_j >= thr must be known
+      const double thr = __dmul_rn((double)r.P, (double)WA);
+      const int lim = nA >= 0 ? nA : nk;
+      nK = 0;
+      for (int j = 1; j <= lim; ++j)
+        if (!((double)S(j) < thr)) {
+          nK = j;
+          break;
+        }
+      if (nK == 0 && nA >= 0) nK = nA;  // every one of the first K is kept
+      ok = nK > 0;
+      if (ok) WK = S(nK);
+    } else if (ok) {
+      nK = nA >= 0 ? nA : nk;
+      WK = nA >= 0 ? S(nA) : WA;
+    }
+    uint32_t token = (uint32_t)(ts.RK[0] & 0xFFFFFFFFu);
+    if (ok && WK > 0) {
+      const uint64_t rr = draw_point(sh.u, WK);
+      ok = false;
+      for (int j = 0; j < nK && j < nk; ++j)
+        if (S(j) <= rr && rr < S(j) + ts.RW[j]) {
+          token = (uint32_t)(ts.RK[j] & 0xFFFFFFFFu);
+          ok = true;
+          break;
+        }
+    } else if (ok) {  // no weight anywhere: the leading member stands
+      ok = true;
+    }
+    status |= sh.status;
+    if (!ok) status |= MSTAR_STATUS_TP_OVERFLOW;
     write_row_outputs(p, row, slot, token, status);
   }
 }
@@ -3466,12 +3699,14 @@ static int launch_small(const mstar_sampler_params_t *p, cudaStream_t st) {
   return MSTAR_OK;
 }
 
-static int launch(const mstar_sampler_params_t *p, int mode, int tp_cap, uint32_t *send, cudaStream_t st) {
+static int launch(const mstar_sampler_params_t *p, int mode, int tp_cap, uint32_t *send, cudaStream_t st,
+                  float *xdump = nullptr) {
   if (use_small(p, mode))
     return p->dtype == MSTAR_DTYPE_BF16 ? launch_small<__nv_bfloat16>(p, st) : launch_small<float>(p, st);
-  Plan pl;
+  Plan pl{};
   int rc = plan_launch(p, mode, tp_cap, pl);
   if (rc) return rc;
+  pl.xdump = xdump;
   if (p->dtype == MSTAR_DTYPE_BF16)
     return mode == 0 ? launch_T<__nv_bfloat16, 0>(p, pl, send, st) : launch_T<__nv_bfloat16, 1>(p, pl, send, st);
   return mode == 0 ? launch_T<float, 0>(p, pl, send, st) : launch_T<float, 1>(p, pl, send, st);
@@ -3497,7 +3732,7 @@ int mstar_sampler_plan(const mstar_sampler_params_t *p, int32_t *cluster_size, i
     if (smem_bytes) *smem_bytes = SMALL_SMEM;
     return MSTAR_OK;
   }
-  Plan pl;
+  Plan pl{};
   rc = plan_launch(p, 0, 0, pl);
   if (rc) return rc;
   if (cluster_size) *cluster_size = pl.S;
@@ -3513,7 +3748,8 @@ int mstar_sampler_step(const mstar_sampler_params_t *p, void *stream) {
 
 int32_t mstar_sampler_tp_record_words(int32_t tp_cap) { return 4 + 2 * tp_cap; }
 
-int mstar_sampler_tp_local(const mstar_sampler_params_t *p, int32_t tp_cap, uint32_t *send, void *stream) {
+static int tp_local_impl(const mstar_sampler_params_t *p, int32_t tp_cap, uint32_t *send, float *xbuf,
+                         void *stream) {
   if (!p) return fail(MSTAR_ERR_INVALID, "params is NULL");
   mstar_sampler_params_t q = *p;
   if (!q.out_ids && !q.out_ids32) q.out_ids32 = reinterpret_cast<int32_t *>(send);  // not written in TP mode
@@ -3524,7 +3760,17 @@ int mstar_sampler_tp_local(const mstar_sampler_params_t *p, int32_t tp_cap, uint
   if (q.out_x || q.out_kept || q.out_probs)
     return fail(MSTAR_ERR_UNSUPPORTED, "dense debug outputs are single-shard only");
   q.flags &= ~(MSTAR_FLAG_UPDATE_HISTORY | MSTAR_FLAG_UPDATE_SEEN | MSTAR_FLAG_ADVANCE_OFFSET);
-  return launch(&q, 1, tp_cap, send, static_cast<cudaStream_t>(stream));
+  return launch(&q, 1, tp_cap, send, static_cast<cudaStream_t>(stream), xbuf);
+}
+
+int mstar_sampler_tp_local(const mstar_sampler_params_t *p, int32_t tp_cap, uint32_t *send, void *stream) {
+  return tp_local_impl(p, tp_cap, send, nullptr, stream);
+}
+
+int mstar_sampler_tp_local2(const mstar_sampler_params_t *p, int32_t tp_cap, uint32_t *send, float *xbuf,
+                            void *stream) {
+  if (!xbuf) return fail(MSTAR_ERR_INVALID, "xbuf is NULL");
+  return tp_local_impl(p, tp_cap, send, xbuf, stream);
 }
 
 int64_t mstar_lmhead_workspace_bytes(int32_t B) {
@@ -3577,8 +3823,8 @@ int mstar_sampler_commit(const mstar_sampler_params_t *p, const int64_t *ids, vo
   return MSTAR_OK;
 }
 
-int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world, int64_t V_global,
-                           const uint32_t *recv, void *stream) {
+static int tp_merge_check(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world, int64_t V_global,
+                          const void *recv) {
   int rc = validate(p);
   if (rc) return rc;
   if (!recv) return fail(MSTAR_ERR_INVALID, "recv is NULL");
@@ -3590,11 +3836,60 @@ int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int3
   // the global id must cover the whole vocabulary
   if (p->seen_bits && p->seen_words * 32 < V_global)
     return fail(MSTAR_ERR_INVALID, "seen_words too small for V_global");
+  return MSTAR_OK;
+}
+
+static int tp_merge_impl(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world, int64_t V_global,
+                         const uint32_t *recv, uint32_t *pend, void *stream) {
+  int rc = tp_merge_check(p, tp_cap, tp_world, V_global, recv);
+  if (rc) return rc;
   const int smem = LEAN_SCRATCH;
   cudaError_t e = cudaFuncSetAttribute(tp_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   tp_merge_kernel<<<p->B, NT, smem, static_cast<cudaStream_t>(stream)>>>(*p, tp_cap, tp_world, 4 + 2 * tp_cap,
-                                                                         V_global, recv);
+                                                                         V_global, recv, pend);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return MSTAR_OK;
+}
+
+int mstar_sampler_tp_merge(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world, int64_t V_global,
+                           const uint32_t *recv, void *stream) {
+  return tp_merge_impl(p, tp_cap, tp_world, V_global, recv, nullptr, stream);
+}
+
+int mstar_sampler_tp_merge1(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world, int64_t V_global,
+                            const uint32_t *recv, uint32_t *pend, void *stream) {
+  if (!pend) return fail(MSTAR_ERR_INVALID, "pend is NULL");
+  if (tp_world > 16) return fail(MSTAR_ERR_INVALID, "the two-round exchange takes at most 16 ranks");
+  return tp_merge_impl(p, tp_cap, tp_world, V_global, recv, pend, stream);
+}
+
+int mstar_sampler_tp_mass(const mstar_sampler_params_t *p, const float *xbuf, const uint32_t *pend, uint32_t *send2,
+                          void *stream) {
+  if (!p) return fail(MSTAR_ERR_INVALID, "params is NULL");
+  if (!xbuf || !pend || !send2) return fail(MSTAR_ERR_INVALID, "xbuf, pend and send2 must not be NULL");
+  mstar_sampler_params_t q = *p;
+  if (!q.out_ids && !q.out_ids32) q.out_ids32 = reinterpret_cast<int32_t *>(send2);  // (no id is written)
+  const int rc = validate(&q);
+  if (rc) return rc;
+  tp_mass_kernel<<<p->B, NT, 0, static_cast<cudaStream_t>(stream)>>>(q, xbuf, pend, send2);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+  return MSTAR_OK;
+}
+
+int mstar_sampler_tp_merge2(const mstar_sampler_params_t *p, int32_t tp_cap, int32_t tp_world, int64_t V_global,
+                            const uint32_t *recv, const uint32_t *recv2, const uint32_t *pend, void *stream) {
+  int rc = tp_merge_check(p, tp_cap, tp_world, V_global, recv);
+  if (rc) return rc;
+  if (!recv2 || !pend) return fail(MSTAR_ERR_INVALID, "recv2 and pend must not be NULL");
+  if (tp_world > 16) return fail(MSTAR_ERR_INVALID, "the two-round exchange takes at most 16 ranks");
+  const int smem = LEAN_SCRATCH;
+  cudaError_t e = cudaFuncSetAttribute(tp_merge2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  tp_merge2_kernel<<<p->B, NT, smem, static_cast<cudaStream_t>(stream)>>>(*p, tp_cap, tp_world, 4 + 2 * tp_cap,
+                                                                          V_global, recv, recv2, pend);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(MSTAR_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
   return MSTAR_OK;

@@ -180,6 +180,71 @@ def tp_merge(logits: torch.Tensor, tp_cap: int, tp_world: int, V_global: int, re
                 "mstar_sampler_tp_merge")
 
 
+def _u32(t, name, dev, n):
+    if t.dtype != torch.int32 or t.device != dev or not t.is_contiguous() or t.numel() < n:
+        raise ValueError(f"{name} must be a contiguous int32 tensor of >= {n} words on {dev}")
+
+
+def tp_local2(logits: torch.Tensor, tp_cap: int, send: torch.Tensor, xbuf: torch.Tensor, **kw) -> None:
+    """Two-round shard records (mstar_sampler_tp_local2): rows without a
+    usable top_k send their first tp_cap members and leave their shard
+    values in xbuf [B, V] float32."""
+    p = build_params(logits, **kw)
+    dev = logits.device
+    _u32(send, "send", dev, logits.shape[0] * tp_record_words(tp_cap))
+    if xbuf.dtype != torch.float32 or xbuf.device != dev or not xbuf.is_contiguous() or \
+            xbuf.numel() < logits.shape[0] * logits.shape[1]:
+        raise ValueError("xbuf must be a contiguous float32 [B, V] tensor on the logits device")
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        N.check(N.lib().mstar_sampler_tp_local2(ctypes.byref(p), tp_cap, _ptr(send), _ptr(xbuf),
+                                                ctypes.c_void_p(stream)), "mstar_sampler_tp_local2")
+
+
+def tp_merge1(logits: torch.Tensor, tp_cap: int, tp_world: int, V_global: int, recv: torch.Tensor,
+              pend: torch.Tensor, **kw) -> None:
+    """First merge of the two-round exchange (mstar_sampler_tp_merge1): decides
+    the rows no shard cut short, defers the others into pend [B, 2] int32."""
+    p = build_params(logits, **kw)
+    dev = logits.device
+    B = logits.shape[0]
+    _u32(recv, "recv", dev, tp_world * B * tp_record_words(tp_cap))
+    _u32(pend, "pend", dev, 2 * B)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        N.check(N.lib().mstar_sampler_tp_merge1(ctypes.byref(p), tp_cap, tp_world, V_global, _ptr(recv), _ptr(pend),
+                                                ctypes.c_void_p(stream)), "mstar_sampler_tp_merge1")
+
+
+def tp_mass(logits: torch.Tensor, xbuf: torch.Tensor, pend: torch.Tensor, send2: torch.Tensor, **kw) -> None:
+    """The shard's exact A mass of every deferred row (mstar_sampler_tp_mass)
+    into send2 [B, 2] int32 (a little-endian u64 per row)."""
+    p = build_params(logits, **kw)
+    dev = logits.device
+    B = logits.shape[0]
+    _u32(pend, "pend", dev, 2 * B)
+    _u32(send2, "send2", dev, 2 * B)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        N.check(N.lib().mstar_sampler_tp_mass(ctypes.byref(p), _ptr(xbuf), _ptr(pend), _ptr(send2),
+                                              ctypes.c_void_p(stream)), "mstar_sampler_tp_mass")
+
+
+def tp_merge2(logits: torch.Tensor, tp_cap: int, tp_world: int, V_global: int, recv: torch.Tensor,
+              recv2: torch.Tensor, pend: torch.Tensor, **kw) -> None:
+    """Second merge of the two-round exchange (mstar_sampler_tp_merge2)."""
+    p = build_params(logits, **kw)
+    dev = logits.device
+    B = logits.shape[0]
+    _u32(recv, "recv", dev, tp_world * B * tp_record_words(tp_cap))
+    _u32(recv2, "recv2", dev, tp_world * 2 * B)
+    _u32(pend, "pend", dev, 2 * B)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        N.check(N.lib().mstar_sampler_tp_merge2(ctypes.byref(p), tp_cap, tp_world, V_global, _ptr(recv), _ptr(recv2),
+                                                _ptr(pend), ctypes.c_void_p(stream)), "mstar_sampler_tp_merge2")
+
+
 def commit(ids: torch.Tensor, *, V: int, num_slots: int, slot_idx=None, hist_ids=None, hist_len=None,
            seen_bits=None, stop_ids=None, stop_flags=None, offset=None, flags=0, vocab_offset=0) -> None:
     """Per-slot state updates for ids chosen elsewhere (mstar_sampler_commit):

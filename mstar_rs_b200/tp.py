@@ -14,9 +14,16 @@ Each rank holds the logits of a contiguous vocabulary range (ids
 This replaces the reference's token broadcast across Thinker ranks
 (python/mstar_rs/models/qwen3_omni.py:401-404, :408, :431).  All buffers are
 allocated once, so a step can be captured in a CUDA graph together with the
-NCCL all-gather.  Rows whose shard set exceeds ``tp_cap`` (top_k off over a
-flat shard) report ``STATUS_TP_OVERFLOW``; size ``tp_cap`` to the largest
-top_k in use.
+NCCL all-gather.
+
+With ``two_round=True`` rows without top_k (the Thinker's default whenever a
+temperature is given, qwen3_omni.py:440-443) are sampled too: such a row's
+shards send their first ``tp_cap`` members; rows with a shard cut short are
+deferred by the first merge, every shard sends its exact A mass against the
+row max (a second, 8-byte-per-row all-gather), and the second merge decides
+them whenever the kept set or the draw lies among the members every shard
+sent.  Rows it cannot decide report ``STATUS_TP_OVERFLOW``; with one round,
+so does every row whose shard set exceeds ``tp_cap``.
 """
 from __future__ import annotations
 
@@ -50,9 +57,12 @@ class VocabParallelSampler:
     """
 
     def __init__(self, max_bs: int, V_global: int, world: int, rank: int, device, tp_cap: int = 64,
-                 group=None, gather: Callable[[torch.Tensor, torch.Tensor], None] | None = None):
+                 group=None, gather: Callable[[torch.Tensor, torch.Tensor], None] | None = None,
+                 two_round: bool = False, V_shard: int | None = None):
         if tp_cap < 1:
             raise ValueError("tp_cap must be >= 1")
+        if two_round and world > 16:
+            raise ValueError("the two-round exchange takes at most 16 ranks")
         self.max_bs, self.V_global, self.world, self.rank = max_bs, V_global, world, rank
         self.tp_cap = tp_cap
         self.device = torch.device(device)
@@ -60,6 +70,13 @@ class VocabParallelSampler:
         self.send = torch.zeros(max_bs * self.words, dtype=torch.int32, device=self.device)
         self.recv = torch.zeros(world * max_bs * self.words, dtype=torch.int32, device=self.device)
         self.gather = gather if gather is not None else _default_gather(group)
+        self.two_round = two_round
+        if two_round:
+            vs = V_shard if V_shard is not None else -(-V_global // world)
+            self.xbuf = torch.empty(max_bs * vs, dtype=torch.float32, device=self.device)
+            self.pend = torch.zeros(2 * max_bs, dtype=torch.int32, device=self.device)
+            self.send2 = torch.zeros(2 * max_bs, dtype=torch.int32, device=self.device)
+            self.recv2 = torch.zeros(world * 2 * max_bs, dtype=torch.int32, device=self.device)
 
     def local(self, logits: torch.Tensor, vocab_offset: int, **params) -> torch.Tensor:
         """Step 1: this shard's records for the rows of ``logits``."""
@@ -79,10 +96,32 @@ class VocabParallelSampler:
         state of ``kernel.sampler_step`` (temperature, top_k, ..., seed/offset
         or uniforms, history, flags)."""
         B = logits.shape[0]
-        send = self.local(logits, vocab_offset, **{k: v for k, v in params.items() if k != "flags"})
-        recv = self.recv[: self.world * B * self.words]  # contiguous [world, B * words]
+        local = {k: v for k, v in params.items() if k not in ("flags", "out_status", "stop_ids", "stop_flags")}
+        if not self.two_round:
+            send = self.local(logits, vocab_offset, **local)
+            recv = self.recv[: self.world * B * self.words]  # contiguous [world, B * words]
+            self.gather(recv, send)
+            self.merge(logits, vocab_offset, recv, out_ids=out_ids, **params)
+            return out_ids
+        if B > self.max_bs:
+            raise ValueError(f"batch {B} exceeds max_bs {self.max_bs}")
+        V = logits.shape[1]
+        if self.xbuf.numel() < B * V:
+            raise ValueError(f"shard of {V} ids exceeds the V_shard the sampler was built for")
+        send = self.send[: B * self.words]
+        xbuf = self.xbuf[: B * V]
+        kernel.tp_local2(logits, self.tp_cap, send, xbuf, vocab_offset=vocab_offset, **local)
+        recv = self.recv[: self.world * B * self.words]
         self.gather(recv, send)
-        self.merge(logits, vocab_offset, recv, out_ids=out_ids, **params)
+        pend = self.pend[: 2 * B]
+        kernel.tp_merge1(logits, self.tp_cap, self.world, self.V_global, recv, pend, vocab_offset=vocab_offset,
+                         out_ids=out_ids, **params)
+        send2 = self.send2[: 2 * B]
+        kernel.tp_mass(logits, xbuf, pend, send2, vocab_offset=vocab_offset, **local)
+        recv2 = self.recv2[: self.world * 2 * B]
+        self.gather(recv2, send2)
+        kernel.tp_merge2(logits, self.tp_cap, self.world, self.V_global, recv, recv2, pend,
+                         vocab_offset=vocab_offset, out_ids=out_ids, **params)
         return out_ids
 
 

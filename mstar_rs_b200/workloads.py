@@ -177,6 +177,36 @@ def tp_sharded(tp: int, seed: int = 0, B: int = 128, V: int = 152064, H: int = 5
     return shards
 
 
+def tp_topk_off(tp: int, seed: int = 0, B: int = 32, V: int = 48000, H: int = 128, spike_frac: float = 0.003,
+                top_p: tuple = (0.9, 1.0)) -> list[Batch]:
+    """Vocab-sharded rows with top_k off, as the Thinker samples whenever a
+    temperature is given (python/mstar_rs/models/qwen3_omni.py:440-443):
+    bf16 N(0, 1) logits with spike_frac of each shard's ids spiked by
+    +U(6, 10) (a peaked distribution), T 0.7, top_k 0, top_p cycling through
+    `top_p` by row, repetition 1.05 over a uniform history."""
+    assert V % tp == 0
+    Vs = V // tp
+    prm = np.random.default_rng(seed + 104729)
+    common = dict(
+        temperature=np.full(B, 0.7, np.float32), top_k=np.zeros(B, np.int32),
+        top_p=np.array([top_p[r % len(top_p)] for r in range(B)], np.float32), min_p=np.zeros(B, np.float32),
+        rep_pen=np.full(B, 1.05, np.float32), pres_pen=np.zeros(B, np.float32),
+        freq_pen=np.zeros(B, np.float32),
+        hist_ids=prm.integers(0, V, (B, H), dtype=np.int32), hist_len=np.full(B, H, np.int32),
+        uniforms=prm.random(B, dtype=np.float32))
+    shards = []
+    nspike = max(1, int(round(spike_frac * Vs)))
+    for q in range(tp):
+        rng = np.random.default_rng(seed + 31 * q + 1)
+        x = rng.standard_normal((B, Vs), dtype=np.float32)
+        for r in range(B):
+            ids = rng.choice(Vs, nspike, replace=False)
+            x[r, ids] += rng.uniform(6.0, 10.0, nspike).astype(np.float32)
+        shards.append(Batch(logits=f32_to_bf16_bits(x), dtype="bf16", vocab_offset=q * Vs,
+                            name=f"tpk0_{tp}_shard{q}_b{B}_v{V}_bf16", **common))
+    return shards
+
+
 def tp_full(shards: list[Batch]) -> Batch:
     s0 = shards[0]
     b = Batch(**{f.name: getattr(s0, f.name) for f in fields(s0)})
