@@ -4,19 +4,20 @@
 // each CTA owns a contiguous slice of it and reads every byte of the slice
 // exactly once from HBM:
 //
-//   loads     the small per-row inputs are issued first (history length and
-//             words, parameter words, the slice's unaligned fringe, bias
-//             entries), then the slice: up to 152 KB as streaming 128-bit
-//             loads into a register tile (19 vectors per thread), larger
-//             slices as 1-D bulk copies into shared memory (32 KB per
-//             mbarrier; every wait is bounded in time).
-//   setup     while the loads fly: a skip bitmap of the slice's special ids
+//   loads     the small per-row inputs first (history length and words,
+//             parameter words, the slice's unaligned fringe, bias entries),
+//             staged in shared memory before the slice is requested: issued
+//             behind the slice they would wait for most of the 19 MB stream
+//             of all rows.  Then the slice, as 1-D bulk copies into shared
+//             memory (32 KB per mbarrier; every wait is bounded in time).
+//   setup     while the copies land: a skip bitmap of the slice's special ids
 //             (history / bias ids, allowed-mask holes), a seen map for
 //             seen-bit penalties, the row's parameters and Philox uniform,
-//             then a hash table of the specials with occurrence counts.
-//   pass A    raw maximum per vector, specials masked out by a taint mask;
-//             the register tile is stored to shared memory and each vector's
-//             raw maximum kept in registers.  The specials' final values
+//             and a hash table of the specials with occurrence counts.
+//   pass A    raw maximum per vector as each chunk lands, specials masked out
+//             by a taint mask; a slice of at most 152 KB keeps each vector's
+//             raw maximum in registers (19 vectors per thread, thread t
+//             owning vectors t, t + 512, ...).  The specials' final values
 //             (bias, penalties, mask, temperature) come from the table and,
 //             for seen ids, straight from the resident data.
 //   threshold theta(cm) from the CTA's own maximum: below it no value can
@@ -24,12 +25,15 @@
 //             cluster exchange is needed before candidates are chosen.
 //   push      vectors whose raw maximum reaches theta are rescanned; their
 //             candidates go straight into the leader CTA's shared memory
-//             (one reservation per warp), cut at the CTA's local top_k value
-//             when a top_k row has more than it may push; the CTA's maximum,
+//             (one reservation per warp and step); a top_k row whose vectors above theta are many
+//             times K is first cut below the value bin holding the K-th
+//             largest vector maximum, and one that still holds more than it
+//             may push is cut at its K-th largest value; the CTA's maximum,
 //             count, status and lowest id at its maximum go to every peer.
 //             One cluster barrier per step.
-//   tail      (leader) rank sort, value-bucket sort or key-bucket sort of the
-//             candidates, then top_k / top_p / the inverse-CDF draw from
+//   tail      (leader) rank sort, value-bucket sort (one atomic pass of
+//             bucket counts and masses up to 512 candidates) or key-bucket
+//             sort of the candidates, then top_k / top_p / the inverse-CDF draw from
 //             exact u64 prefix sums of the fixed-point weights.  Rows with
 //             more than 2048 candidates run the general path instead:
 //             histogram (count + mass) and compaction rounds over the
@@ -79,7 +83,8 @@ constexpr int MAX_CHUNKS = 8;       // slice data <= 256 KB
 constexpr int MAX_ROUNDS = 96;      // bound on general-path rounds
 constexpr int BIAS_SMEM = 256;      // bias entries staged in shared memory
 constexpr int NPARAM = 7;           // per-row sampling parameter words
-constexpr int NVR = 19;             // vectors per thread in the register tile (152 KB per CTA)
+constexpr int PRECUT_FACTOR = 4;   // pre-cut a top_k row when more than this many times K vectors pass
+constexpr int NVR = 19;             // vectors per thread whose maxima stay in registers (152 KB per CTA)
 constexpr int HIST_BYTES = NBIN * 16;  // per histogram: counts + three 11-bit mass parts
 constexpr int GEN_BYTES = 2 * HIST_BYTES + GCAP * 8;  // L1 | REF (aliased by the sort scratch) | sort input
 static_assert(NBIN * 8 <= NBIN * 12, "64-bit mass prefixes fit over the part arrays");
@@ -201,6 +206,7 @@ struct CtaSh {
   uint32_t min_all;
   int nemit;
   int kcut_bin;         // candidates: value bin of this CTA's K-th largest (top_k cut)
+  uint32_t vcount;      // candidates: untainted vectors reaching theta (pre-cut)
   Row row;
   int tp_ovf;
   int pseudo;           // TP two rounds: the row's top_k is the record capacity
@@ -525,6 +531,7 @@ __device__ __forceinline__ void block_exscan2_u64(uint64_t a, uint64_t b, uint64
 
 
 
+
 // The row's sampling parameters as raw 32-bit words, in the order
 // temperature, top_k, min_p, top_p, repetition, frequency, presence
 // (defaults for absent arrays); word j is loaded by one thread.
@@ -568,19 +575,6 @@ __device__ __forceinline__ void row_init(Row &r, const mstar_sampler_params_t &p
 #pragma unroll
   for (int j = 0; j < NPARAM; ++j) w[j] = param_word(p, j, slot);
   row_init(r, w, p, row, V);
-}
-
-// A 16-byte streaming load (read once) issued exactly where it stands: the
-// asm is volatile and clobbers memory, so the compiler neither sinks it
-// below the setup that follows nor hoists the smaller loads above it behind
-// it; its registers are waited for only where they are first used.
-__device__ __forceinline__ uint4 ld_stream(const uint4 *g) {
-  uint4 v;
-  asm volatile("ld.global.cs.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(g)
-               : "memory");
-  return v;
 }
 
 // value-A predicate of x given the row max m (positive weight and min_p).
@@ -1361,6 +1355,7 @@ __device__ void tail_emit(const Row &r, uint32_t km, int tp_cap, uint32_t *rec, 
 // BUCKET_MAX candidates (runs of exact ties: the caller then sorts by order
 // key, whose buckets split ties by id).  Block-wide; ends with a barrier.
 constexpr int RANK_SMALL = 128;
+constexpr int RESOLVE_WARP_MAX = 64;  // candidates one warp resolves faster than the whole block
 constexpr uint32_t BUCKET_MAX = 64;
 __device__ bool tail_bucket_sort(const Row &r, uint32_t km, int n, const TailScr &s, CtaSh &sh) {
   const int t = threadIdx.x, lane = t & 31;
@@ -1481,7 +1476,7 @@ __device__ void tail_finish(const Row &r, float u, uint32_t km, int n, uint64_t 
                             int tp_cap, uint32_t *rec, const TailScr &ts, CtaSh &sh) {
   tail_sort_gathered(r, km, n, kmn, kmx, np, ts, sh);
   if (MODE == 0) {
-    if (n <= NT) {
+    if (n <= RESOLVE_WARP_MAX) {  // a few ranks: one warp, no block barrier
       if (threadIdx.x < 32) tail_resolve_warp(r, u, ts, sh);
     } else {
       tail_resolve(r, u, ts, sh);
@@ -1491,6 +1486,123 @@ __device__ void tail_finish(const Row &r, float u, uint32_t km, int n, uint64_t 
   }
 }
 
+
+// Clears the per-bucket counts and masses tail_finish1 accumulates into;
+// called by the leader's threads t0, t0 + stride, ... before a barrier that
+// precedes tail_finish1.
+__device__ __forceinline__ void tail_clear1(const TailScr &s, int t0, int stride) {
+  uint32_t *w = s.bc;  // counts [256]
+  for (int i = t0; i < 256; i += stride) w[i] = 0u;
+  uint32_t *mw = reinterpret_cast<uint32_t *>(s.bm);  // mass words: lo [256], hi [256]
+  for (int i = t0; i < 512; i += stride) mw[i] = 0u;
+}
+
+// tail_finish for RANK_SMALL < n <= NT candidates, candidate i held by
+// thread i (key, weight; valid = i < n), sorted by value bucket with fewer
+// block-wide steps than tail_bucket_sort: each candidate's bucket count and
+// weight go into per-bucket counts and masses in one atomic pass (counters
+// cleared by tail_clear1 beforehand), one warp scan gives every bucket's
+// first rank and exclusive mass, a scatter into bucket order, and a rank
+// inside the bucket that also sums the weights of the bucket's smaller keys,
+// so each candidate's exclusive weight prefix is its bucket's exclusive
+// mass plus that sum: no block-wide prefix scan.  Same outputs and buckets
+// as tail_bucket_sort; runs of ties (a bucket of A with more than
+// BUCKET_MAX candidates) fall back to the order-key sort.  Block-wide.
+template <int MODE>
+__device__ void tail_finish1(const Row &r, float u, uint32_t km, int n, bool valid, uint64_t key, uint64_t w,
+                             uint64_t kmn, uint64_t kmx, int tp_cap, uint32_t *rec, const TailScr &s, CtaSh &sh) {
+  const int t = threadIdx.x, lane = t & 31;
+  const float m = okey_inv(km);
+  const float span = fmaxf(r.minp ? fminf(23.5f, __fadd_rn(-r.lnMp, 0.25f)) : 23.5f, 1e-3f);
+  const float sc = 256.0f / span;
+  uint32_t *cnt = s.bc, *start = s.bc + 256;
+  uint32_t *mlo = reinterpret_cast<uint32_t *>(s.bm), *mhi = mlo + 256;
+  uint64_t *mst = s.bm + 256;       // exclusive bucket masses
+  uint64_t *BK = s.K, *BW = s.W;    // bucket order (each key and weight is in its thread's registers)
+  uint32_t b = 255u, pos = 0u;
+  if (valid) {
+    const float x = okey_inv(km - (uint32_t)(key >> 32));
+    const float g = __fmul_rn(__fsub_rn(m, x), sc);
+    b = g >= 255.0f ? 255u : (g > 0.0f ? (uint32_t)g : 0u);
+    pos = atomicAdd(&cnt[b], 1u);
+    if (w) add_u64_split(&mlo[b], &mhi[b], w);
+  }
+  const uint32_t np = __reduce_add_sync(~0u, (valid && w != 0) ? 1u : 0u);
+  if (lane == 0 && np) atomicAdd(&sh.npass, np);
+  __syncthreads();  // counts, masses and the pass count complete
+  if (t < 32) {  // exclusive scans of the counts and masses, 8 buckets per lane
+    uint32_t c[8], tot = 0;
+    uint64_t ms[8], mt = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int bq = lane * 8 + q;
+      c[q] = cnt[bq];
+      ms[q] = get_u64_split(&mlo[bq], &mhi[bq]);
+      tot += c[q];
+      mt += ms[q];
+    }
+    uint32_t inc = tot;
+    uint64_t minc = mt;
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(~0u, inc, o);
+      const uint64_t mv = __shfl_up_sync(~0u, (unsigned long long)minc, o);
+      if (lane >= o) {
+        inc += v;
+        minc += mv;
+      }
+    }
+    uint32_t run = inc - tot, big = 0;
+    uint64_t mrun = minc - mt;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      start[lane * 8 + q] = run;
+      mst[lane * 8 + q] = mrun;
+      run += c[q];
+      mrun += ms[q];
+      big |= (lane * 8 + q < 255 && c[q] > BUCKET_MAX) ? 1u : 0u;
+    }
+    big = __reduce_or_sync(~0u, big);
+    if (lane == 0) sh.bcast_i = (int)big;
+  }
+  __syncthreads();  // bucket starts and masses
+  if (sh.bcast_i) {  // uniform: long runs of ties, the order-key sort (keys and weights gathered by the caller)
+    tail_gather_end(kmn, kmx, 0u, s, sh);
+    tail_sort(n, s, sh);
+  } else {
+    // with top_k only the first K ranks are read: buckets starting at or
+    // past rank K are neither placed nor ranked
+    const uint32_t lim = r.topk ? (uint32_t)r.K : 0xFFFFFFFFu;
+    const uint32_t st = start[b];
+    const bool placed = valid && st < lim;
+    if (placed) {
+      BK[st + pos] = key;
+      BW[st + pos] = w;
+    }
+    __syncthreads();  // bucket order
+    if (placed) {
+      uint32_t rk = pos;  // outside A: any order
+      uint64_t before = 0;
+      if (b < 255u) {
+        rk = 0;
+        const uint32_t en = st + cnt[b];
+        for (uint32_t j = st; j < en; ++j) {
+          const bool lt = BK[j] < key;
+          rk += lt ? 1u : 0u;
+          before += lt ? BW[j] : 0ull;
+        }
+      }
+      s.RK[st + rk] = key;
+      s.RW[st + rk] = w;
+      s.RS[st + rk] = mst[b] + before;
+    }
+    __syncthreads();  // rank order
+  }
+  if (MODE == 0) {
+    tail_resolve(r, u, s, sh);  // (more than RANK_SMALL candidates: one rank per thread)
+  } else {
+    tail_emit(r, km, tp_cap, rec, s, sh);
+  }
+}
 
 // ------------------------------------------------------------ the kernel
 
@@ -1530,6 +1642,35 @@ __device__ __forceinline__ int vb_bin(const VBins &v, float x) {
   while (b < NBIN - 1 && !(x > vb_edge(v, b + 1))) ++b;
   return b;
 }
+// The first of NBIN bins (counts in hist, from the top) at which the count
+// from the top reaches K, or NBIN - 1 if none does.  One full warp; every
+// lane returns the same bin.
+__device__ __forceinline__ int vb_kbin(const uint32_t *hist, uint32_t K) {
+  static_assert(NBIN == 32 * 32, "32 chunks of 32 bins");
+  const int lane = threadIdx.x & 31;
+  // lane l sums chunk l (bins 32 l .. 32 l + 31), reading them in a rotated
+  // order so that the 32 lanes hit 32 different banks at every step
+  uint32_t s = 0;
+#pragma unroll 8
+  for (int i = 0; i < 32; ++i) s += hist[lane * 32 + ((i + lane) & 31)];
+  uint32_t inc = s;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(~0u, inc, o);
+    if (lane >= o) inc += t;
+  }
+  const unsigned reach = __ballot_sync(~0u, inc >= K);
+  if (!reach) return NBIN - 1;
+  const int ch = __ffs(reach) - 1;  // the chunk where the count reaches K
+  const uint32_t before = __shfl_sync(~0u, inc - s, ch);
+  uint32_t ci = hist[ch * 32 + lane];  // then its bins, one per lane
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(~0u, ci, o);
+    if (lane >= o) ci += t;
+  }
+  const unsigned rb = __ballot_sync(~0u, before + ci >= K);
+  return ch * 32 + (__ffs(rb) - 1);
+}
+
 // Order-key range [lo, hi] of value bin b (clipped to the A range's keys <= kmax).
 __device__ __forceinline__ void vb_range(const VBins &v, uint32_t km, int b, uint64_t kmax, uint64_t &lo,
                                          uint64_t &hi) {
@@ -2085,12 +2226,13 @@ __global__ void __launch_bounds__(NT, 1)
   // may have written the logits or the per-slot state) has completed
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // ---- loads.  A slice whose aligned interior fits one register tile (NVR
-  // vectors per thread) is loaded straight into registers: every thread
-  // issues all of its loads at once, which lands a 152 KB slice about 1.5 us
-  // sooner than bulk copies into shared memory do; the registers are copied
-  // to shared memory once the skip bitmap is known.  A larger slice is
-  // bulk-copied in 32 KB chunks (one mbarrier each), all issued by thread 0.
+  // ---- loads.  The small per-row inputs are loaded and staged first; the
+  // slice follows as bulk copies of 32 KB chunks (one mbarrier each, all
+  // issued by thread 0) once they are staged.  Requested behind the slice,
+  // the small loads wait in the same memory queues as every row's stream
+  // (measured: staged at ~3.3 us instead of ~1.9 us), and the setup that
+  // needs them would wait with them.  A slice whose aligned interior maps
+  // onto NVR vectors per thread keeps each vector's maximum in registers.
   const bool rt = nbv <= NT * NVR;  // uniform
   const bool has_hist = p.hist_ids && p.hist_len;
   // slot_idx costs one round trip before anything that depends on the slot
@@ -2159,27 +2301,10 @@ __global__ void __launch_bounds__(NT, 1)
     bid = p.bias_ids[(int64_t)slot * p.NB + tid];
     bval = p.bias_vals[(int64_t)slot * p.NB + tid];
   }
-  // ---- the slice: a register tile, or bulk copies
-  uint4 rv[NVR];
-  if (rt) {
-    const uint4 *src = reinterpret_cast<const uint4 *>(b0);
-#pragma unroll
-    for (int i = 0; i < NVR; ++i) {
-      const int q = i * NT + tid;
-      rv[i] = q < nbv ? ld_stream(src + q) : make_uint4(0u, 0u, 0u, 0u);
-    }
-  } else if (tid == 0) {
+  // ---- the slice's chunk barriers (the copies start after the staging)
+  if (tid == 0) {
     for (int j = 0; j < nchunk; ++j) mbar_init(&sh.mbar[j], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    // (testing: with MSTAR_FLAG_TEST_WITHHOLD the last copy is never issued
-    // and its barrier never completes, so its waits run out)
-    const int nissue = (p.flags & MSTAR_FLAG_TEST_WITHHOLD) ? nchunk - 1 : nchunk;
-    for (int j = 0; j < nissue; ++j) {
-      const uint32_t bytes = (uint32_t)min((int64_t)CHUNK_BYTES, nbulk - (int64_t)j * CHUNK_BYTES);
-      mbar_expect_tx(&sh.mbar[j], bytes);
-      bulk_g2s(L.data + (b0 - a_al) + (int64_t)j * CHUNK_BYTES,
-               reinterpret_cast<const void *>(b0 + (uintptr_t)j * CHUNK_BYTES), bytes, &sh.mbar[j]);
-    }
   }
   // ---- staging of the small values in shared memory
   if (tid >= 64 && tid < 64 + NPARAM) sh.pw[tid - 64] = (uint32_t)pword;
@@ -2205,6 +2330,7 @@ __global__ void __launch_bounds__(NT, 1)
     sh.nemit = 0;
     sh.cmax = okey(-INFINITY);
     sh.best = 0xFFFFFFFFu;
+    sh.vcount = 0;
     tail_reset(sh);
   }
 
@@ -2219,6 +2345,7 @@ __global__ void __launch_bounds__(NT, 1)
   uint32_t *skip32 = reinterpret_cast<uint32_t *>(L.skip);
   if (has_spec)
     for (int i = tid; i < pl.ht_cap; i += NT) L.ht[i] = make_int2(-1, 0);
+  for (int i = tid; i < NBIN; i += NT) L.queue[i] = 0;  // the top_k pre-cut's histogram
   if (p.allowed_bits || p.seen_bits) {
     // word by word: disallowed positions, and (seen-bit mode) the seen ones,
     // which also go into the seen map unless disallowed
@@ -2244,6 +2371,17 @@ __global__ void __launch_bounds__(NT, 1)
     for (int i = tid; i < map_words / 4; i += NT) s4[i] = make_uint4(0u, 0u, 0u, 0u);
   }
   __syncthreads();  // skip words written, table cleared, small values staged
+  if (tid == 0) {  // the slice, chunk by chunk
+    // (testing: with MSTAR_FLAG_TEST_WITHHOLD the last copy is never issued
+    // and its barrier never completes, so its waits run out)
+    const int nissue = (p.flags & MSTAR_FLAG_TEST_WITHHOLD) ? nchunk - 1 : nchunk;
+    for (int j = 0; j < nissue; ++j) {
+      const uint32_t bytes = (uint32_t)min((int64_t)CHUNK_BYTES, nbulk - (int64_t)j * CHUNK_BYTES);
+      mbar_expect_tx(&sh.mbar[j], bytes);
+      bulk_g2s(L.data + (b0 - a_al) + (int64_t)j * CHUNK_BYTES,
+               reinterpret_cast<const void *>(b0 + (uintptr_t)j * CHUNK_BYTES), bytes, &sh.mbar[j]);
+    }
+  }
   if (tid == 64) {
     row_init(sh.row, sh.pw, p, row, p.V);
     // two-round TP: a row without top_k (or with one above the record's
@@ -2331,9 +2469,10 @@ __global__ void __launch_bounds__(NT, 1)
   const bool one = r.greedy || r.K == 1;
 
   // ---- max pass: the masked raw max of the slice (specials and disallowed
-  // positions left out), then the specials' final values.  The register
-  // tile keeps each vector's masked max for the candidate pass and is copied
-  // to shared memory, where the slice stays resident for the later passes.
+  // positions left out), then the specials' final values.  A slice of at
+  // most NVR vectors per thread keeps each vector's raw max in registers for
+  // the candidate pass; the slice stays resident in shared memory for the
+  // later passes.
   Acc racc = Elem<T>::acc_init();
   float spec_max = -INFINITY;
   bool timed_out = false;
@@ -2375,12 +2514,16 @@ __global__ void __launch_bounds__(NT, 1)
       if (valid) spec_max = fmaxf(spec_max, c.x);
     });
   };
-  uint32_t taint = 0;  // register tile: the vectors holding a skipped position
+  uint32_t taint = 0;  // the thread's vectors (of gm) holding a skipped position
   if (rt) {
-    // each vector's raw max (a few instructions) and its copy to shared
-    // memory; vectors with a skipped position (special or disallowed; rare
-    // without an allowed mask) are then reduced again, masked, from shared
-    // memory, and always rescanned by the candidate pass
+    // each vector's raw max (a few instructions) as its chunk lands, kept in
+    // registers for the candidate pass; vectors with a skipped position
+    // (special or disallowed; rare without an allowed mask) are then reduced
+    // again, masked, and always rescanned by the candidate pass.  Row i of
+    // the thread's vectors (NT consecutive vectors) lies in chunk i * NT * 16
+    // / CHUNK_BYTES.
+    static_assert(CHUNK_BYTES % (NT * 16) == 0, "a row of vectors lies in one chunk");
+    constexpr int RPC = CHUNK_BYTES / (NT * 16);  // rows of vectors per chunk
 #pragma unroll
     for (int i = 0; i < NVR; ++i) {
       const int q = i * NT + tid;
@@ -2389,10 +2532,10 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
     for (int i = 0; i < NVR; ++i) {
       const int q = i * NT + tid;
+      if (i % RPC == 0 && i / RPC < nchunk && !mbar_wait(&sh.mbar[i / RPC], 0)) timed_out = true;
       gm[i] = Elem<T>::acc_init();
       if (q < nbv) {
-        gm[i] = Elem<T>::vred(rv[i]);
-        data4[hv + q] = rv[i];
+        gm[i] = Elem<T>::vred(data4[hv + q]);
         if (!((taint >> i) & 1u)) racc = Elem<T>::acc_max(racc, gm[i]);
       }
     }
@@ -2422,6 +2565,18 @@ __global__ void __launch_bounds__(NT, 1)
   // it from the non-special max while the other warps finalize the specials;
   // it is redone only when a special holds the CTA max.
   const float cm_ns = okey_inv(sh.cmax);
+  if (rt && r.topk && !one && (int)r.K <= TAIL_CAP / S) {
+    // the top_k pre-cut's trigger: the untainted vectors within the usual
+    // threshold span of the non-special max (an estimate: the cut itself is
+    // taken against the exact theta)
+    const float ta = fmaxf(__fsub_rn(cm_ns, 23.5f), r.minp ? __fadd_rn(cm_ns, __fsub_rn(r.lnMp, 0.01f)) : -INFINITY);
+    uint32_t c = 0;
+#pragma unroll
+    for (int i = 0; i < NVR; ++i)
+      c += (i * NT + tid < nbv && !((taint >> i) & 1u) && xform(r, Elem<T>::acc_f(gm[i])) >= ta) ? 1u : 0u;
+    c = __reduce_add_sync(~0u, c);
+    if (lane == 0 && c) atomicAdd(&sh.vcount, c);
+  }
   if (tid < 32) {
     const float t = cm_ns > -INFINITY ? choose_theta(r, cm_ns) : INFINITY;
     if (lane == 0) sh.theta = t;
@@ -2462,7 +2617,7 @@ __global__ void __launch_bounds__(NT, 1)
   cluster_wait();                 // every CTA of the cluster runs: remote stores are safe
 
   // ---- candidates: x >= theta(cm) (or x == cm for greedy / top-1),
-  // pushed into the leader's region: the register tile's vectors whose max
+  // pushed into the leader's region: the vectors whose max (kept in registers)
   // reaches the cut (a bulk-copied slice: every vector), the fringe vectors
   // and the specials.  Once this CTA holds more candidates than it may push
   // the scan stops and the row takes the general path (which scans again) --
@@ -2526,15 +2681,17 @@ __global__ void __launch_bounds__(NT, 1)
         return __shfl_sync(~0u, *reinterpret_cast<volatile uint32_t *>(&sh.nloc), 0) > (uint32_t)capq;
       };
       if (rt) {
-        // the tile's vectors whose max reaches the cut, as a bit mask (one
+        // the thread's vectors whose max reaches the cut, as a bit mask (one
         // compact unrolled test), then one rolled loop over the set bits:
         // the scan's code is instantiated once, not once per vector
         // (a vector's raw max bounds its masked max: tainted vectors pass
         // the same test)
         uint32_t pm = 0;
 #pragma unroll
-        for (int i = 0; i < NVR; ++i)
-          pm |= (i * NT + tid < nbv && xform(r, Elem<T>::acc_f(gm[i])) >= tcut) ? 1u << i : 0u;
+        for (int i = 0; i < NVR; ++i) {
+          const float gx = xform(r, Elem<T>::acc_f(gm[i]));
+          pm |= (i * NT + tid < nbv && gx >= tcut && (!kcut || gx > kcut_x)) ? 1u << i : 0u;
+        }
         int steps = 0;
         while (__any_sync(~0u, pm != 0u)) {  // warp-uniform
           if (held_over()) {
@@ -2564,9 +2721,44 @@ __global__ void __launch_bounds__(NT, 1)
       }
       for_each_seen<T>(sl, r, false, tid, NT, push_special);
     };
+    // Pre-cut of a top_k row from the vector maxima kept in registers: if at
+    // least K untainted vectors have a max in value bins 0..b, this CTA's K-th
+    // largest value is > E(b + 1), so nothing at or below E(b + 1) is among
+    // its K largest (nor the row's).  Taken when the vectors reaching theta
+    // are many times K; it keeps the push and the leader's sort near K
+    // candidates per CTA instead of every value above theta.
+    if (rt && !one && r.topk && r.K <= capq && sh.vcount > (uint32_t)(PRECUT_FACTOR * r.K)) {  // CTA-uniform
+      uint32_t pv = 0;  // untainted vectors reaching theta
+#pragma unroll
+      for (int i = 0; i < NVR; ++i)
+        pv |= (i * NT + tid < nbv && !((taint >> i) & 1u) && xform(r, Elem<T>::acc_f(gm[i])) >= theta_l) ? 1u << i
+                                                                                                           : 0u;
+      VBins vb;
+      vb.m = cm;
+      vb.w = __fmul_rn(__fsub_rn(cm, theta_l), 1.0f / NBIN);
+      vb.iw = 1.0f / vb.w;
+      if (vb.w > 0.0f && vb.w < INFINITY && vb.iw < INFINITY) {  // CTA-uniform
+        uint32_t *hist = reinterpret_cast<uint32_t *>(L.queue);  // cleared in the setup
+        for (uint32_t t = pv; t; t &= t - 1u) {
+          const int k = hv + (__ffs(t) - 1) * NT + tid;
+          atomicAdd(&hist[vb_bin(vb, xform(r, Elem<T>::vmax(data4[k])))], 1u);
+        }
+        __syncthreads();
+        if (tid < 32) {
+          const int bk = vb_kbin(hist, (uint32_t)r.K);
+          if (lane == 0) sh.kcut_bin = bk;
+        }
+        __syncthreads();
+        const int bk = sh.kcut_bin;
+        if (bk < NBIN - 1) {
+          kcut = true;
+          kcut_x = vb_edge(vb, bk + 1);
+        }
+      }
+    }
     push_all();
     __syncthreads();
-    if (!one && r.topk && r.K <= capq && sh.nloc > (uint32_t)capq) {  // CTA-uniform: a top_k row overflowed
+    if (!kcut && !one && r.topk && r.K <= capq && sh.nloc > (uint32_t)capq) {  // CTA-uniform: a top_k row overflowed
       VBins vb;
       vb.m = cm;
       vb.w = __fmul_rn(__fsub_rn(cm, theta_l), 1.0f / NBIN);
@@ -2593,25 +2785,8 @@ __global__ void __launch_bounds__(NT, 1)
         });
         __syncthreads();
         if (tid < 32) {  // the first bin where the count from the top reaches K
-          constexpr int PER = NBIN / 32;
-          uint32_t s = 0;
-          for (int i = 0; i < PER; ++i) s += hist[lane * PER + i];
-          uint32_t inc = s;
-          for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t t = __shfl_up_sync(~0u, inc, o);
-            if (lane >= o) inc += t;
-          }
-          const unsigned reach = __ballot_sync(~0u, inc >= (uint32_t)r.K);
-          int bk = NBIN - 1;
-          if (reach && lane == __ffs(reach) - 1) {
-            uint32_t c = inc - s;
-            for (bk = lane * PER; bk < (lane + 1) * PER - 1; ++bk) {
-              c += hist[bk];
-              if (c >= (uint32_t)r.K) break;
-            }
-          }
-          bk = __shfl_sync(~0u, bk, reach ? __ffs(reach) - 1 : 0);
-          if (lane == 0) sh.kcut_bin = reach ? bk : NBIN - 1;
+          const int bk = vb_kbin(hist, (uint32_t)r.K);
+          if (lane == 0) sh.kcut_bin = bk;
         }
         __syncthreads();
         const int bk = sh.kcut_bin;
@@ -2681,6 +2856,8 @@ __global__ void __launch_bounds__(NT, 1)
       sh.res.ckK = 0;
       sh.res.status = st;
     }
+  } else if (fast && rank == 0) {  // the leader's slice data is dead: clear the one-pass tail's counters
+    tail_clear1(tail_scratch(L.data), tid - 32, NT - 32);
   }
   __syncthreads();
   const float theta = sh.theta;
@@ -2724,12 +2901,25 @@ __global__ void __launch_bounds__(NT, 1)
         const int n = (int)sh.ncand;
         uint64_t kmn = ~0ull, kmx = 0ull;
         uint32_t np = 0;
-        for (int i = tid; i < n; i += NT) {  // one candidate per thread
-          int q = 0;
-          while (q + 1 < S && i >= (int)sh.goff[q + 1]) ++q;
-          tail_put(r, m, km, L.lcand[q * capq + (i - (int)sh.goff[q])], i, ts, kmn, kmx, np);
+        if (n > RANK_SMALL && n <= NT) {  // one candidate per thread, kept in registers
+          const bool valid = tid < n;
+          uint64_t key = 0, w = 0;
+          if (valid) {
+            int q = 0;
+            while (q + 1 < S && tid >= (int)sh.goff[q + 1]) ++q;
+            tail_put(r, m, km, L.lcand[q * capq + (tid - (int)sh.goff[q])], tid, ts, kmn, kmx, np);
+            key = ts.K[tid];
+            w = ts.W[tid];
+          }
+          tail_finish1<MODE>(r, MODE == 0 ? sh.u : 0.0f, km, n, valid, key, w, kmn, kmx, pl.tp_cap, rec, ts, sh);
+        } else {
+          for (int i = tid; i < n; i += NT) {  // one candidate per thread
+            int q = 0;
+            while (q + 1 < S && i >= (int)sh.goff[q + 1]) ++q;
+            tail_put(r, m, km, L.lcand[q * capq + (i - (int)sh.goff[q])], i, ts, kmn, kmx, np);
+          }
+          tail_finish<MODE>(r, MODE == 0 ? sh.u : 0.0f, km, n, kmn, kmx, np, pl.tp_cap, rec, ts, sh);
         }
-        tail_finish<MODE>(r, MODE == 0 ? sh.u : 0.0f, km, n, kmn, kmx, np, pl.tp_cap, rec, ts, sh);
       }
     }
   } else {
@@ -3602,8 +3792,8 @@ static int plan_launch(const mstar_sampler_params_t *p, int mode, int tp_cap, Pl
     if (!need(p->cluster_size, pl)) return fail(MSTAR_ERR_UNSUPPORTED, "row does not fit the requested cluster size");
     return MSTAR_OK;
   }
-  // the smallest cluster the row fits with slices that fit the register
-  // tile (else the smallest it fits at all), widened while the grid leaves
+  // the smallest cluster the row fits with slices of at most NVR vectors
+  // per thread (else the smallest it fits at all), widened while the grid leaves
   // SMs idle (small batches: each row's slice is then streamed by more SMs),
   // up to the portable cluster size and keeping slices >= 8192 elements
   auto in_tile = [&](int s) {
