@@ -407,6 +407,7 @@ def run_ours(args, world, rank, local):
     extra = {}
     if world > 1:
         extra["tp"] = run_tp_multi(args, world, rank, local)
+        extra["tp_topk_off"] = run_tp_topk_off(args, world, rank, local)
         extra["dp_split"] = run_dp_split(args, world, rank, local)
     plan, nbuf, step_bytes = t["plan"], t["nbuf"], t["step_bytes"]
     del t
@@ -841,6 +842,63 @@ def run_tp_multi(args, world, rank, local):
             "rows_per_s": B / (ms / 1e3), "allgather_us": ag_ms * 1e3, "allgather_share": ag_ms / ms,
             "record_bytes_per_rank": B * smp.words * 4, "ids_identical_on_every_rank": bool(ids_ok.item()),
             "scaling": "strong", "launch": "one CUDA graph per cycle: tp_local, NCCL all-gather, tp_merge"}
+
+
+def run_tp_topk_off(args, world, rank, local, B=128, V=152064):
+    """Rows without top_k over the ranks (two rounds: records, NCCL
+    all-gather, first merge, exact shard masses, a second 8-byte-per-row
+    all-gather, second merge), the whole step captured in one CUDA graph.
+    Reported: µs per step (max over ranks), the rows the two rounds decided,
+    and whether every rank drew the same ids."""
+    import torch
+    import torch.distributed as dist
+
+    from mstar_rs_b200 import _native as N
+    from mstar_rs_b200 import tp as TP
+    from mstar_rs_b200 import workloads as W
+
+    dev = torch.device("cuda", local)
+    shard = W.tp_topk_off(world, seed=args.seed, B=B, V=V, H=512)[rank]
+    d = W.to_device(shard, device=dev)
+    logits = d.pop("logits")
+    off = d.pop("vocab_offset")
+    smp = TP.VocabParallelSampler(B, V, world, rank, dev, tp_cap=64, group=dist.group.WORLD, two_round=True,
+                                  V_shard=shard.V)
+    out = torch.zeros(B, dtype=torch.int64, device=dev)
+    st = torch.zeros(B, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            smp.sample(logits, off, out, out_status=st, **d)
+    torch.cuda.synchronize(dev)
+    reps = 20
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(reps):
+            smp.sample(logits, off, out, out_status=st, **d)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(5):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / (5 * reps)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    decided = int(((st & N.STATUS_TP_OVERFLOW) == 0).sum().item())
+    ref = out.clone()
+    dist.broadcast(ref, src=0)
+    ok = torch.tensor([int(torch.equal(ref, out))], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    del graph
+    return {"workload": f"tp{world}_topk_off_b{B}_v{V}_bf16", "us_per_step": ms * 1e3, "rows_per_s": B / (ms / 1e3),
+            "rows_decided": decided, "rows": B, "ids_identical_on_every_rank": bool(ok.item()), "scaling": "strong",
+            "launch": "one CUDA graph: tp_local2, all-gather, tp_merge1, tp_mass, all-gather, tp_merge2"}
 
 
 def run_dp_split(args, world, rank, local):
