@@ -84,6 +84,7 @@ constexpr int MAX_ROUNDS = 96;      // bound on general-path rounds
 constexpr int BIAS_SMEM = 256;      // bias entries staged in shared memory
 constexpr int NPARAM = 7;           // per-row sampling parameter words
 constexpr int PRECUT_FACTOR = 4;   // pre-cut a top_k row when more than this many times K vectors pass
+constexpr int GCUT_MAX_K = TAIL_CAP * 3 / 4;  // cluster-wide top_k cut up to this K (the cut's spill must fit the tail)
 constexpr int NVR = 19;             // vectors per thread whose maxima stay in registers (152 KB per CTA)
 constexpr int HIST_BYTES = NBIN * 16;  // per histogram: counts + three 11-bit mass parts
 constexpr int GEN_BYTES = 2 * HIST_BYTES + GCAP * 8;  // L1 | REF (aliased by the sort scratch) | sort input
@@ -2616,6 +2617,57 @@ __global__ void __launch_bounds__(NT, 1)
   const int capq = TAIL_CAP / S;  // candidates each CTA may push to the leader
   cluster_wait();                 // every CTA of the cluster runs: remote stores are safe
 
+  // ---- cluster-wide top_k cut, for a top_k row whose K exceeds what one CTA
+  // may push (its K largest could then not be cut CTA by CTA): the CTAs
+  // exchange their maxima, add histograms of their untainted vector maxima
+  // and their specials' values over common value bins [theta(m), m] into the
+  // leader's shared memory, and each reads the first bin from the top where
+  // the count reaches K.  K items (distinct values of the row) lie above that
+  // bin's lower edge, so no value at or below it is among the row's K
+  // largest.  Two cluster barriers instead of the general path's rounds;
+  // taken by every CTA of the cluster or by none (it depends on the row's
+  // parameters and the plan only).
+  bool gk = false;
+  float gk_x = -INFINITY;
+  if (MODE == 0 && !one && r.topk && r.K > capq && r.K <= GCUT_MAX_K &&
+      pl.slice * es <= (int64_t)NT * NVR * 16) {  // cluster-uniform; every CTA keeps its maxima in registers
+    if (tid < S) cluster.map_shared_rank(&sh, tid)->maxes[rank] = cm;
+    cluster.sync();  // maxima delivered; every histogram cleared in the setup
+    float mq = lane < S ? sh.maxes[lane] : -INFINITY;
+    for (int o = 16; o; o >>= 1) mq = fmaxf(mq, __shfl_xor_sync(~0u, mq, o));
+    const float mg = mq;  // the row max
+    const float tg = mg > -INFINITY ? choose_theta(r, mg) : INFINITY;  // every warp: same value
+    VBins vb;
+    vb.m = mg;
+    vb.w = __fmul_rn(__fsub_rn(mg, tg), 1.0f / NBIN);
+    vb.iw = 1.0f / vb.w;
+    const bool ok = mg > -INFINITY && vb.w > 0.0f && vb.w < INFINITY && vb.iw < INFINITY;  // cluster-uniform
+    uint32_t *lhist = cluster.map_shared_rank(reinterpret_cast<uint32_t *>(L.queue), 0);
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < NVR; ++i) {
+        const float gx = xform(r, Elem<T>::acc_f(gm[i]));
+        if (i * NT + tid < nbv && !((taint >> i) & 1u) && gx >= tg) atomicAdd(&lhist[vb_bin(vb, gx)], 1u);
+      }
+      for (int i = tid; i < nspec; i += NT) {
+        const float x = L.spec[i].x;
+        if (x >= tg) atomicAdd(&lhist[vb_bin(vb, x)], 1u);
+      }
+    }
+    cluster.sync();  // the leader's histogram complete
+    if (ok) {
+      if (tid < 32) {
+        const int bk = vb_kbin(lhist, (uint32_t)r.K);
+        if (lane == 0) sh.kcut_bin = bk;
+      }
+      __syncthreads();
+      if (sh.kcut_bin < NBIN - 1) {
+        gk = true;
+        gk_x = vb_edge(vb, sh.kcut_bin + 1);
+      }
+    }
+  }
+
   // ---- candidates: x >= theta(cm) (or x == cm for greedy / top-1),
   // pushed into the leader's region: the vectors whose max (kept in registers)
   // reaches the cut (a bulk-copied slice: every vector), the fringe vectors
@@ -2631,8 +2683,8 @@ __global__ void __launch_bounds__(NT, 1)
     const float tcut = one ? cm : theta_l;
     Cand *const lead = cluster.map_shared_rank(L.lcand, 0) + rank * capq;
     uint32_t best = 0xFFFFFFFFu;
-    bool kcut = false;
-    float kcut_x = -INFINITY;  // pushed: x > kcut_x (with kcut)
+    bool kcut = gk;
+    float kcut_x = gk_x;  // pushed: x > kcut_x (with kcut)
     // one vector per lane per step (warp-uniform step count); the passing
     // values are appended with one atomic per warp
     auto scan_vec = [&](int k, bool valid) {

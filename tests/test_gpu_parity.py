@@ -50,6 +50,29 @@ def test_large_flat_rows(oracle_lib, seed):
         assert (g["status"] & 2).any(), "expected the general path"
 
 
+@pytest.mark.parametrize("seed", range(4))
+@pytest.mark.parametrize("cluster", [4, 8])
+def test_cluster_topk_cut(oracle_lib, seed, cluster):
+    """top_k rows whose K exceeds what one CTA may push (2048 / cluster) on
+    flat rows where every id is a candidate: the CTAs cut at a value bin
+    found from a histogram of all CTAs' vector maxima and specials summed in
+    the leader, instead of taking the general path.  History penalties put
+    specials into the histogram; odd seeds add the NaN / inf / -0 values."""
+    case = random_case(400 + seed, B=6, V=60000, dtype=["f32", "bf16"][seed % 2], scale=1.0,
+                       specials=bool(seed % 2), greedy_frac=0.0, mask=False)
+    cap = 2048 // cluster
+    case.temperature[:] = 1.0
+    case.top_k[:] = [cap + 1, cap + 300, 900, 1200, 1536, cap + 60]
+    case.top_p[:] = [1.0, 0.9, 0.95, 0.5, 1.0, 0.99]
+    case.min_p[:] = 0.0
+    o = oracle_lib.run(case, debug=True)
+    g = run_gpu(case, cluster_size=cluster)
+    assert_parity(g, o, case)
+    if not seed % 2:  # finite rows take the cut, not the general path (a CTA holding
+        # far more than its share of the cut's values may still overflow: at most one row)
+        assert int(((g["status"] & 2) != 0).sum()) <= 1
+
+
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("cluster", [1, 2])
 @pytest.mark.parametrize("mask", [False, True])
