@@ -862,8 +862,7 @@ def run_tp_topk_off(args, world, rank, local, B=128, V=152064):
     d = W.to_device(shard, device=dev)
     logits = d.pop("logits")
     off = d.pop("vocab_offset")
-    smp = TP.VocabParallelSampler(B, V, world, rank, dev, tp_cap=64, group=dist.group.WORLD, two_round=True,
-                                  V_shard=shard.V)
+    smp = TP.VocabParallelSampler(B, V, world, rank, dev, group=dist.group.WORLD, two_round=True, V_shard=shard.V)
     out = torch.zeros(B, dtype=torch.int64, device=dev)
     st = torch.zeros(B, dtype=torch.int32, device=dev)
     stream = torch.cuda.Stream(device=dev)

@@ -35,6 +35,16 @@ from . import _native as N
 from . import kernel
 
 
+# Default record capacities (members per shard and row).  One round: a row's
+# top_k members must fit, and the Thinker's top_k rarely exceeds 64.  Two
+# rounds: rows without top_k send their first members in order; 256 decide
+# every row of a peaked 152k-vocabulary batch at tp 2 where 64 leave about one
+# in ten to the overflow flag (the numpy restatement and the GPU agree on
+# which rows), and the record stays under 2 KB per row.
+TP_CAP = 64
+TWO_ROUND_TP_CAP = 256
+
+
 def _default_gather(group) -> Callable[[torch.Tensor, torch.Tensor], None]:
     import torch.distributed as dist
 
@@ -51,14 +61,17 @@ def _default_gather(group) -> Callable[[torch.Tensor, torch.Tensor], None]:
 class VocabParallelSampler:
     """Fixed-shape vocab-parallel sampler for up to ``max_bs`` rows.
 
-    ``gather(recv, send)`` all-gathers ``send`` ([B * words] int32) from every
+    ``tp_cap`` defaults to TP_CAP (one round) or TWO_ROUND_TP_CAP (two
+    rounds); world * tp_cap must not exceed 2048.  ``gather(recv, send)`` all-gathers ``send`` ([B * words] int32) from every
     rank into ``recv`` ([world, B * words], rank-major); by default it is a
     torch.distributed all-gather over ``group``.
     """
 
-    def __init__(self, max_bs: int, V_global: int, world: int, rank: int, device, tp_cap: int = 64,
+    def __init__(self, max_bs: int, V_global: int, world: int, rank: int, device, tp_cap: int | None = None,
                  group=None, gather: Callable[[torch.Tensor, torch.Tensor], None] | None = None,
                  two_round: bool = False, V_shard: int | None = None):
+        if tp_cap is None:
+            tp_cap = TWO_ROUND_TP_CAP if two_round else TP_CAP
         if tp_cap < 1:
             raise ValueError("tp_cap must be >= 1")
         if two_round and world > 16:

@@ -211,3 +211,49 @@ def test_two_round_sampler_one_rank(oracle_lib):
     decided = (st.cpu().numpy() & N.STATUS_TP_OVERFLOW) == 0
     assert decided.all()
     np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+def test_two_round_full_size(oracle_lib, tp):
+    """The two rounds at the vocab-parallel workload's full size (B=128,
+    V=152064, peaked rows without top_k) with the sampler's default record
+    capacity, shards emulated on one device (the exchange concatenates the
+    shards' sends): every row is decided and every shard's ids equal the
+    full row's oracle ids."""
+    import torch
+
+    from mstar_rs_b200 import _native as N
+    from mstar_rs_b200 import tp as TP
+
+    B, V = 128, 152064
+    shards = W.tp_topk_off(tp, seed=0, B=B, V=V, H=512)
+    full = W.tp_full(shards)
+    ref = oracle_lib.run(full)["ids"]
+    devs = [W.to_device(s) for s in shards]
+    logits = [d.pop("logits") for d in devs]
+    offs = [d.pop("vocab_offset") for d in devs]
+    smps = [TP.VocabParallelSampler(B, V, tp, q, "cuda", two_round=True, V_shard=shards[q].V,
+                                    gather=lambda recv, send: None) for q in range(tp)]
+    assert smps[0].tp_cap == TP.TWO_ROUND_TP_CAP
+    outs = [torch.zeros(B, dtype=torch.int64, device="cuda") for _ in range(tp)]
+    stats = [torch.zeros(B, dtype=torch.int32, device="cuda") for _ in range(tp)]
+    # the step's kernels, shard by shard, with the two exchanges done by hand
+    from mstar_rs_b200 import kernel
+    for q in range(tp):
+        kernel.tp_local2(logits[q], smps[q].tp_cap, smps[q].send[: B * smps[q].words], smps[q].xbuf[: B * shards[q].V],
+                         vocab_offset=offs[q], **devs[q])
+    recv = torch.cat([smps[q].send[: B * smps[q].words] for q in range(tp)])
+    for q in range(tp):
+        kernel.tp_merge1(logits[q], smps[q].tp_cap, tp, V, recv, smps[q].pend[: 2 * B], vocab_offset=offs[q],
+                         out_ids=outs[q], out_status=stats[q], **devs[q])
+        kernel.tp_mass(logits[q], smps[q].xbuf[: B * shards[q].V], smps[q].pend[: 2 * B], smps[q].send2[: 2 * B],
+                       vocab_offset=offs[q], **devs[q])
+    recv2 = torch.cat([smps[q].send2[: 2 * B] for q in range(tp)])
+    for q in range(tp):
+        kernel.tp_merge2(logits[q], smps[q].tp_cap, tp, V, recv, recv2, smps[q].pend[: 2 * B], vocab_offset=offs[q],
+                         out_ids=outs[q], out_status=stats[q], **devs[q])
+    torch.cuda.synchronize()
+    for q in range(tp):
+        st = stats[q].cpu().numpy()
+        assert not (st & N.STATUS_TP_OVERFLOW).any(), f"shard {q}: {int(((st & N.STATUS_TP_OVERFLOW) != 0).sum())} rows"
+        np.testing.assert_array_equal(outs[q].cpu().numpy(), ref, err_msg=f"ids on shard {q}")
