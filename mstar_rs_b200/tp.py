@@ -62,7 +62,7 @@ class VocabParallelSampler:
     """Fixed-shape vocab-parallel sampler for up to ``max_bs`` rows.
 
     ``tp_cap`` defaults to TP_CAP (one round) or TWO_ROUND_TP_CAP (two
-    rounds); world * tp_cap must not exceed 2048.  ``gather(recv, send)`` all-gathers ``send`` ([B * words] int32) from every
+    rounds), at most 2048 // world; world * tp_cap must not exceed 2048.  ``gather(recv, send)`` all-gathers ``send`` ([B * words] int32) from every
     rank into ``recv`` ([world, B * words], rank-major); by default it is a
     torch.distributed all-gather over ``group``.
     """
@@ -70,8 +70,10 @@ class VocabParallelSampler:
     def __init__(self, max_bs: int, V_global: int, world: int, rank: int, device, tp_cap: int | None = None,
                  group=None, gather: Callable[[torch.Tensor, torch.Tensor], None] | None = None,
                  two_round: bool = False, V_shard: int | None = None):
-        if tp_cap is None:
-            tp_cap = TWO_ROUND_TP_CAP if two_round else TP_CAP
+        if tp_cap is None:  # the merge holds at most 2048 members per row over all ranks
+            tp_cap = min(TWO_ROUND_TP_CAP if two_round else TP_CAP, 2048 // max(1, world))
+        if world * tp_cap > 2048:
+            raise ValueError(f"world * tp_cap = {world * tp_cap} exceeds the 2048 members a merge holds per row")
         if tp_cap < 1:
             raise ValueError("tp_cap must be >= 1")
         if two_round and world > 16:

@@ -257,3 +257,22 @@ def test_gloo_two_round_exchange(oracle_lib, tmp_path):
     np.testing.assert_array_equal(st[0], st[1])
     assert not (st[0] & tp_np.STATUS_TP_OVERFLOW).any()
     np.testing.assert_array_equal(ids[0], ref)
+
+
+def test_record_capacity_defaults():
+    """Default record capacities: 64 members per shard for one round, 256 for
+    two rounds, never more than the 2048 members a merge holds per row over
+    all ranks; an explicit capacity beyond that is refused up front."""
+    import pytest
+
+    from mstar_rs_b200 import tp as TP
+
+    def cap(world, two_round):
+        return TP.VocabParallelSampler(4, 1000 * world, world, 0, "cpu", two_round=two_round,
+                                       gather=lambda recv, send: None).tp_cap
+
+    assert cap(1, False) == 64 and cap(8, False) == 64
+    assert cap(2, True) == 256 and cap(8, True) == 256
+    assert cap(16, True) == 128
+    with pytest.raises(ValueError, match="2048"):
+        TP.VocabParallelSampler(4, 32000, 16, 0, "cpu", tp_cap=256, gather=lambda recv, send: None)
