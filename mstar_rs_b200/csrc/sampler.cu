@@ -2540,8 +2540,22 @@ __global__ void __launch_bounds__(NT, 1)
         if (!((taint >> i) & 1u)) racc = Elem<T>::acc_max(racc, gm[i]);
       }
     }
-    for (uint32_t t = taint; t; t &= t - 1u)
-      racc = Elem<T>::acc_max(racc, Elem<T>::vred(load_masked<T>(sl, hv + (__ffs(t) - 1) * NT + tid)));
+    if (p.allowed_bits) {
+      // an allowed mask taints nearly every vector: keep each tainted
+      // vector's masked max, so the candidate pass rescans only vectors
+      // whose allowed values reach the cut
+      if (taint) {
+#pragma unroll
+        for (int i = 0; i < NVR; ++i)
+          if ((taint >> i) & 1u) {
+            gm[i] = Elem<T>::vred(load_masked<T>(sl, hv + i * NT + tid));
+            racc = Elem<T>::acc_max(racc, gm[i]);
+          }
+      }
+    } else {
+      for (uint32_t t = taint; t; t &= t - 1u)
+        racc = Elem<T>::acc_max(racc, Elem<T>::vred(load_masked<T>(sl, hv + (__ffs(t) - 1) * NT + tid)));
+    }
   } else {
     constexpr int CV = CHUNK_BYTES / 16;
     for (int j = 0; j < nchunk; ++j) {
@@ -2736,8 +2750,8 @@ __global__ void __launch_bounds__(NT, 1)
         // the thread's vectors whose max reaches the cut, as a bit mask (one
         // compact unrolled test), then one rolled loop over the set bits:
         // the scan's code is instantiated once, not once per vector
-        // (a vector's raw max bounds its masked max: tainted vectors pass
-        // the same test)
+        // (a tainted vector's kept max is its raw max, which bounds its
+        // masked max, or with an allowed mask the masked max itself)
         uint32_t pm = 0;
 #pragma unroll
         for (int i = 0; i < NVR; ++i) {
