@@ -1353,11 +1353,15 @@ __device__ void tail_emit(const Row &r, uint32_t km, int tp_cap, uint32_t *rec, 
 // bucket order and a rank inside each bucket; then the exclusive weight
 // prefix.  Same outputs as tail_sort (RK / RW / RS in rank order).  Returns
 // false, having sorted nothing, when a bucket of A holds more than
-// BUCKET_MAX candidates (runs of exact ties: the caller then sorts by order
-// key, whose buckets split ties by id).  Block-wide; ends with a barrier.
+// BUCKET_MAX candidates (long runs of exact ties: the caller then sorts by
+// order key, whose buckets split ties by id).  A bucket's rank pass costs its
+// size per candidate; 256 keeps rows of 1-2 thousand candidates packed into
+// a narrow min_p span on this path (a 64 limit sent them to the order-key
+// sort: a mixed batch with one such row measured 34.0 -> 26.3 us per step).
+// Block-wide; ends with a barrier.
 constexpr int RANK_SMALL = 128;
 constexpr int RESOLVE_WARP_MAX = 64;  // candidates one warp resolves faster than the whole block
-constexpr uint32_t BUCKET_MAX = 64;
+constexpr uint32_t BUCKET_MAX = 256;
 __device__ bool tail_bucket_sort(const Row &r, uint32_t km, int n, const TailScr &s, CtaSh &sh) {
   const int t = threadIdx.x, lane = t & 31;
   const float m = okey_inv(km);
