@@ -69,17 +69,21 @@ def parse():
 
 
 def make_case(name, rank=0, seed=0, bucket=128):
+    """The workload's batch.  Every data-parallel rank samples the same seeded
+    batch (weak scaling: the per-GPU work is the one-GPU run's, row for row;
+    batches drawn per rank differ in their heaviest row, e.g. one min_p row
+    with 1,700 candidates, and the max over ranks would time that instead)."""
     from mstar_rs_b200 import workloads as W
 
     if name == "qwen_mixed":
-        return W.qwen_mixed(seed=seed + rank)
+        return W.qwen_mixed(seed=seed)
     if name == "orpheus_single":
-        return W.orpheus_single(seed=seed + rank)
+        return W.orpheus_single(seed=seed)
     if name == "bucket":
-        return W.bucket_sweep(bucket, seed=seed + rank)
+        return W.bucket_sweep(bucket, seed=seed)
     if name == "tp":  # the whole row (the reference arm samples it unsharded)
         return W.tp_full(W.tp_sharded(1, seed=seed))
-    return W.constrained(seed=seed + rank)
+    return W.constrained(seed=seed)
 
 
 def algorithmic_bytes(case) -> int:
@@ -182,7 +186,7 @@ def config_of(case, world):
     """The workload description both arms print (the same keys in both)."""
     return {"workload": case.name, "B": case.B, "V": case.V, "logits_dtype": case.dtype,
             "history": None if case.hist_ids is None else int(case.hist_ids.shape[1]),
-            "parallelism": f"dp{world}" if world > 1 else "single",
+            "parallelism": f"dp{world} (every rank samples the same seeded batch)" if world > 1 else "single",
             "rng": "philox in-kernel, offset advanced per step",
             "state_updates": "history append + offset" if case.hist_ids is not None else "offset",
             "history_reset": "restored from the initial Zipf history once per cycle over the logits buffers",
