@@ -9,7 +9,7 @@
 //             staged in shared memory before the slice is requested: issued
 //             behind the slice they would wait for most of the 19 MB stream
 //             of all rows.  Then the slice, as 1-D bulk copies into shared
-//             memory (32 KB per mbarrier; every wait is bounded in time).
+//             memory (64 KB per mbarrier; every wait is bounded in time).
 //   setup     while the copies land: a skip bitmap of the slice's special ids
 //             (history / bias ids, allowed-mask holes), a seen map for
 //             seen-bit penalties, the row's parameters and Philox uniform,
@@ -78,8 +78,8 @@ constexpr int NBK_LOG2 = 11;
 constexpr int NBK = 1 << NBK_LOG2;   // buckets of the fast tail
 constexpr int GBK_LOG2 = 9;
 constexpr int GBK = 1 << GBK_LOG2;   // buckets of the general-path sort
-constexpr int CHUNK_BYTES = 32768;  // bulk-copy granule (one mbarrier each)
-constexpr int MAX_CHUNKS = 8;       // slice data <= 256 KB
+constexpr int CHUNK_BYTES = 65536;  // bulk-copy granule (one mbarrier each)
+constexpr int MAX_CHUNKS = 4;       // slice data <= 256 KB
 constexpr int MAX_ROUNDS = 96;      // bound on general-path rounds
 constexpr int BIAS_SMEM = 256;      // bias entries staged in shared memory
 constexpr int NPARAM = 7;           // per-row sampling parameter words
@@ -100,7 +100,7 @@ static_assert(NBK % NT == 0, "tail bucket scan");
 static_assert(NBK >= 2 * 256 && NBK >= NT, "value-bucket tail: counts and starts over the bucket counts, weights over the masses");
 static_assert(NT == 512, "the rank sort splits 512 threads into 64 / 128 / 256 slots");
 // Bound on one wait for a bulk copy: 2 ms of %globaltimer (a copy of at
-// most 32 KB lands within microseconds), with an iteration cap behind it.
+// most 64 KB lands within microseconds), with an iteration cap behind it.
 constexpr uint64_t kWaitNs = 2000000ull;
 constexpr unsigned kWaitIters = 1u << 26;
 
@@ -2232,7 +2232,7 @@ __global__ void __launch_bounds__(NT, 1)
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- loads.  The small per-row inputs are loaded and staged first; the
-  // slice follows as bulk copies of 32 KB chunks (one mbarrier each, all
+  // slice follows as bulk copies of 64 KB chunks (one mbarrier each, all
   // issued by thread 0) once they are staged.  Requested behind the slice,
   // the small loads wait in the same memory queues as every row's stream
   // (measured: staged at ~3.3 us instead of ~1.9 us), and the setup that
